@@ -1,0 +1,85 @@
+"""Seeded inputs and case specs shared by the golden generator and the tests.
+
+Everything here uses torch's CPU generator, so the same seeds give the same
+tensors in the build container (where the fixtures are made) and on the GPU
+box (where the GPU tests regenerate them).
+"""
+
+from __future__ import annotations
+
+import torch
+
+# Config 1 of the benchmark: one CPU-runnable Veda layer (B=1, 8 heads,
+# head_dim 128, grid (4,16,16) = 1024 tokens, tile (2,8,8), 50% budget).
+CFG1 = dict(seq_len=1024, used=1024, heads=8, dim=128, seed=0,
+            grid=(4, 16, 16), shape=(2, 8, 8), ratio=0.5, pred_seed=100,
+            pred_std=0.02)
+
+# A padded target grid behind text rows: partial tiles, a partial global
+# tile and padding rows [used, seq_len). Small head_dim keeps fixtures tiny;
+# the oracle does not depend on head_dim.
+PADDED = dict(spans=[(360, (8, 12, 20), (4, 8, 4))], used=2280,
+              seq_len=2312, heads=3, dim=32, seed=5, group_heads=[0, 2],
+              pred_seed=101, ratio=0.3, score_seed=7, dout_seed=9,
+              heat_rows=[0, 3, 7, 19, 22])
+
+# Reference (condition) span + target span: segmented budgets.
+SEGMENTED = dict(spans=[(90, (1, 16, 32), (1, 8, 16)),
+                        (90 + 512 + 40, (16, 8, 16), (4, 8, 4))],
+                 used=90 + 512 + 40 + 2048, seq_len=90 + 512 + 40 + 2048,
+                 heads=3, ref_ratio=0.25, target_ratio=0.3, score_seed=11,
+                 subset_rows=[0, 3, 4, 7, 11, 19])
+
+# Layouts of the reference's own tiling tests (tests/unit/
+# test_veda_tiling_plan.py:24-35): text 100, optional condition, audio 50.
+SMALL_LAYOUTS = {
+    'l_4x8x4': dict(spans=[(150, (7, 6, 10), (4, 8, 4))], used=570,
+                    seq_len=600),
+    'l_8x2x8': dict(spans=[(150, (7, 6, 10), (8, 2, 8))], used=570,
+                    seq_len=600),
+    'l_2x8x8': dict(spans=[(150, (7, 6, 10), (2, 8, 8))], used=570,
+                    seq_len=600),
+    'l_cond': dict(spans=[(100, (1, 6, 10), (1, 8, 16)),
+                          (210, (7, 6, 10), (4, 8, 4))], used=630,
+                   seq_len=660),
+    'l_ragged': dict(spans=[(0, (3, 5, 7), (2, 8, 8))], used=105,
+                     seq_len=130),
+}
+
+# Full-size layouts of benchmark configs 2-4 (budgets: (ref, target) ratios).
+BENCH_LAYOUTS = {
+    'cfg2': dict(spans=[(0, (20, 32, 56), (2, 8, 8))], used=35840,
+                 seq_len=35840, budgets=[(None, 0.1)]),
+    'cfg3_a': dict(spans=[(1024, (26, 45, 80), (2, 8, 8))], used=94624,
+                   seq_len=94624, budgets=[(None, 0.1)]),
+    'cfg3_b': dict(spans=[(1024, (26, 45, 80), (1, 8, 16))], used=94624,
+                   seq_len=94624, budgets=[(None, 0.1)]),
+    'cfg4': dict(spans=[(0, (4, 45, 80), (2, 8, 8)),
+                        (14400, (26, 45, 80), (2, 8, 8))], used=108000,
+                 seq_len=108000, budgets=[(0.05, 0.1)]),
+}
+
+
+def qkv(seq_len, heads, dim, seed, dtype):
+    """q, k, v ~ N(0, 1) drawn in that order from one seeded generator."""
+    gen = torch.Generator().manual_seed(seed)
+    return [torch.randn(seq_len, heads, dim, generator=gen).to(dtype)
+            for _ in range(3)]
+
+
+def predictor_weights(heads, dim, seed, std):
+    """proj_q, proj_k [heads, 3*dim, dim] fp32 ~ N(0, std^2)."""
+    gen = torch.Generator().manual_seed(seed)
+    return [torch.randn(heads, 3 * dim, dim, generator=gen) * std
+            for _ in range(2)]
+
+
+def scores(heads, n_tiles, seed):
+    """Random fp32 block scores [heads, n_tiles, n_tiles] (no ties)."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(heads, n_tiles, n_tiles, generator=gen)
+
+
+def dout(shape, seed):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=gen).to(torch.bfloat16)
