@@ -1,0 +1,206 @@
+/*
+ * veda_b200.h -- C ABI of the B200 (sm_100a) Veda sparse-attention library.
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in
+ * elements), plus the CUDA stream to launch on (cudaStream_t passed as
+ * void*). Inputs are borrowed, outputs are preallocated by the caller; no
+ * entry point allocates memory. Each returns VEDA_OK or an error code whose
+ * message is available from veda_last_error() (thread-local).
+ *
+ * Tensor conventions (the reference's own, miowtion/kernels/fa4.py:38-39):
+ *   packed tokens   x[S, H, D]      bf16, D == 128, last dim contiguous
+ *   tile-ordered    t[N, H', D]     bf16, N = n_tiles * 128
+ *   block mask      m[H', R, n]     uint8 (0/1)
+ *   index lists     cnt[H', R] int32, idx[H', R, n] int32 (BlockSparseTensors)
+ *
+ * Kernels that wait on barriers give up after a bounded time; they then
+ * record VEDA_ERR_TIMEOUT in a device status word (veda_device_status) and
+ * return early instead of hanging.
+ */
+#ifndef VEDA_B200_H_
+#define VEDA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  VEDA_OK = 0,
+  VEDA_ERR_INVALID = 1,      /* argument or shape misuse  -> ValueError */
+  VEDA_ERR_UNSUPPORTED = 2,  /* arch / dtype / head_dim   -> NotImplementedError */
+  VEDA_ERR_CUDA = 3,         /* CUDA runtime/driver error -> RuntimeError */
+  VEDA_ERR_TIMEOUT = 4       /* a device-side wait gave up -> RuntimeError */
+};
+
+/* A tiled span of packed rows [start, start + t*h*w) cut into (st,sh,sw)
+ * boxes of 128 tokens (miowtion/veda/tiling.py:108-119, TiledSpan). */
+typedef struct {
+  int64_t start;
+  int32_t grid[3];   /* t, h, w */
+  int32_t shape[3];  /* tile extents, product 128 */
+} veda_span_t;
+
+/* A sparse column block of the video quadrant with its resolved budget
+ * (miowtion/veda/mask.py:96-103 ColumnBlock, :68-76 split_budget). */
+typedef struct {
+  int32_t start;
+  int32_t stop;
+  int32_t k_lo;
+  int32_t k_hi;
+  double frac;        /* Bresenham fraction, already rounded to 12 decimals */
+  int32_t keeps_all;  /* Budget.keeps_all: every non-empty column is kept */
+  int32_t pad_;
+} veda_column_block_t;
+
+/* ---- library state ---------------------------------------------------- */
+
+/* Copies the calling thread's last error message into buf (NUL-terminated);
+ * returns the last error code. */
+int veda_last_error(char* buf, size_t size);
+
+/* Reads (and with reset != 0 clears) the device status word that kernels
+ * set when a bounded wait times out. Synchronizes the current device. */
+int veda_device_status(int32_t* status, int32_t reset);
+
+/* 1 when the current device is sm_100 (B200) and the library can run. */
+int veda_supported_device(void);
+
+/* ---- a1: tile layout -------------------------------------------------- */
+
+/* Replaces miowtion/veda/tiling.py:214-275 (build_tile_layout) for the
+ * permutation itself: writes perm[n_tiles*128] (int64, -1 on padding) and
+ * valid_count[n_tiles] (int32). n_tiles must equal the sum of the spans'
+ * tile counts plus ceil(global rows / 128). */
+int veda_build_layout(const veda_span_t* spans, int32_t n_spans,
+                      int64_t used, int64_t seq_len, int64_t n_tiles,
+                      int64_t* perm, int32_t* valid_count, void* stream);
+
+/* ---- a2/a3/a12/a14: permutation, pooling, inverse ---------------------- */
+
+/* Replaces miowtion/kernels/tile_gather_triton.py:156-209 (gather_tiles /
+ * gather_and_pool) and miowtion/veda/predictor.py:82-168 (pool_tiles):
+ *   out[slot, h, :] = x[perm[slot], heads[h], :] (0 where perm < 0)
+ *   feats[h, tile, 0:3D] = masked mean | max | min over the tile's prefix
+ *   sq[h, tile, :] = E[x^2], var[h, tile, :] = centred Var(x)
+ * perm == NULL pools already tile-ordered rows (x is then [N, H', D] and
+ * heads == NULL). feats / sq / var may be NULL. */
+int veda_gather_pool(const void* x, int64_t x_stride_s, int64_t x_stride_h,
+                     const int64_t* perm, const int32_t* valid_count,
+                     int64_t n_tiles, const int64_t* heads, int32_t n_heads,
+                     void* out, int64_t out_stride_n, int64_t out_stride_h,
+                     float* feats, float* sq, float* var, void* stream);
+
+/* Replaces miowtion/kernels/tile_gather_triton.py:212-224 (scatter_tiles_):
+ *   out[perm[slot], heads[h], :] = tiled[slot, h, :] for perm[slot] >= 0. */
+int veda_scatter(const void* tiled, int64_t t_stride_n, int64_t t_stride_h,
+                 const int64_t* perm, int64_t n_tiles, const int64_t* heads,
+                 int32_t n_heads, void* out, int64_t out_stride_s,
+                 int64_t out_stride_h, void* stream);
+
+/* Replaces miowtion/veda/attention.py:299-305 (_gather_lse):
+ *   out[slot, h] = lse[perm[slot], heads[h]] (0 where perm < 0). */
+int veda_gather_lse(const float* lse, int64_t l_stride_s, int64_t l_stride_h,
+                    const int64_t* perm, int64_t n_tiles,
+                    const int64_t* heads, int32_t n_heads, float* out,
+                    void* stream);
+
+/* ---- a4: predictor logits ---------------------------------------------- */
+
+/* Bytes of workspace veda_predict_logits needs. */
+int64_t veda_predict_workspace(int32_t n_heads, int64_t n_q, int64_t n_k);
+
+/* Replaces miowtion/veda/predictor.py:251-255 + :299-338 (LayerPredictor
+ * embed / forward without optional terms), all fp32:
+ *   q_hat = feats_q @ proj_q[heads[h]] + mean_q,  k_hat likewise,
+ *   logits[h] = q_hat . k_hat^T / sqrt(D).
+ * feats_*: [H', n, 3D]; proj_*: [num_heads, 3D, D]; logits: [H', n_q, n_k]. */
+int veda_predict_logits(const float* feats_q, const float* feats_k,
+                        const float* proj_q, const float* proj_k,
+                        const int64_t* heads, int32_t n_heads, int64_t n_q,
+                        int64_t n_k, float* logits, void* workspace,
+                        int64_t workspace_bytes, void* stream);
+
+/* ---- a5-a8: top-k selection, block mask, index lists ------------------- */
+
+/* Replaces miowtion/veda/mask.py:200-285 (select_video_blocks, rule topk),
+ * :288-317 (dense_block_mask) and miowtion/kernels/fa4.py:266-296
+ * (index_lists, forward direction) in one pass.
+ * scores: [H', R, ld_scores] fp32, row i is video query tile rows[i]
+ *   (rows == NULL: i itself). Columns [0, n_video) are ranked.
+ * global_rows != 0 appends the n - n_video global query rows (R must then be
+ *   n_video); they keep every non-empty tile.
+ * Outputs (each may be NULL):
+ *   mask [H', R_out, n] uint8; lists part/full cnt [H', R_out] and idx
+ *   [H', R_out, n] int32 (fill_tails != 0 writes the non-members after the
+ *   members, ascending, exactly as the reference's stable argsort does);
+ *   sel_index [H', R, K] int64 / sel_keep [H', R, K] uint8 with K = sum of
+ *   the blocks' k_hi (keeps_all blocks contribute their width), in the
+ *   reference's rank order. Ties rank the lower column first. */
+int veda_block_select(const float* scores, int64_t ld_scores,
+                      int32_t n_heads, int64_t n_rows, const int64_t* rows,
+                      const int32_t* valid_count, int64_t n_tiles,
+                      int64_t n_video, const veda_column_block_t* blocks,
+                      int32_t n_blocks, int32_t global_rows, uint8_t* mask,
+                      int32_t* part_cnt, int32_t* part_idx,
+                      int32_t* full_cnt, int32_t* full_idx,
+                      int32_t fill_tails, int64_t* sel_index,
+                      uint8_t* sel_keep, void* stream);
+
+/* Replaces miowtion/kernels/fa4.py:275-296 (index_lists) for an arbitrary
+ * mask [H', R, n] uint8: transpose == 0 gives per-query-tile lists
+ * ([H', R, n]); transpose != 0 gives per-key-tile query lists ([H', n, R]),
+ * partial iff the key tile is partial. */
+int veda_index_lists(const uint8_t* mask, int32_t n_heads, int64_t n_rows,
+                     int64_t n_cols, const int32_t* valid_count,
+                     int32_t transpose, int32_t* part_cnt, int32_t* part_idx,
+                     int32_t* full_cnt, int32_t* full_idx, int32_t fill_tails,
+                     void* stream);
+
+/* ---- a9/a11: block-sparse and dense attention forward (tcgen05) --------- */
+
+/* Replaces miowtion/kernels/fa4.py:299-377 (block_sparse_attention,
+ * forward) with semantics miowtion/kernels/reference.py:1-10, :23-56:
+ *   q [R*128, H', D], k/v [N, H', D] bf16 (head dim contiguous, row stride
+ *   multiple of 8 elements, 16-byte aligned), lists as veda_block_select
+ *   writes them (idx row stride ld_idx), out [R*128, H', D] bf16,
+ *   lse [H', R*128] fp32 (NULL to skip). Query tiles with an empty list
+ *   output 0 and lse -inf. */
+int veda_bsa_fwd(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                 const void* k, int64_t k_stride_n, int64_t k_stride_h,
+                 const void* v, int64_t v_stride_n, int64_t v_stride_h,
+                 int32_t n_heads, int64_t n_q_tiles, int64_t n_kv_tiles,
+                 const int32_t* valid_count, const int32_t* part_cnt,
+                 const int32_t* part_idx, const int32_t* full_cnt,
+                 const int32_t* full_idx, int64_t ld_idx, void* out,
+                 int64_t out_stride_n, int64_t out_stride_h, float* lse,
+                 float softmax_scale, void* stream);
+
+/* Replaces miowtion/kernels/fa4.py:185-205 (dense_attention) and the
+ * row-subset contract of miowtion/h3/attention.py:28-102: full attention of
+ * rows [0, used) of q/k/v [S, H, D]; out [S, H, D] (rows >= used are 0),
+ * lse [S, H] fp32 natural log (rows >= used are 0; NULL to skip). */
+int veda_dense_fwd(const void* q, const void* k, const void* v,
+                   int64_t stride_s, int64_t stride_h, int64_t seq_len,
+                   int64_t used, int32_t n_heads, void* out,
+                   int64_t out_stride_s, int64_t out_stride_h, float* lse,
+                   int64_t lse_stride_s, int64_t lse_stride_h,
+                   float softmax_scale, void* stream);
+
+/* ---- diagnostics --------------------------------------------------------- */
+
+/* One 128x128x128 bf16 tcgen05 MMA per mode, for checking operand and
+ * accumulator layouts on a new device: mode 0 computes d = a . b^T with a,b
+ * K-major in shared memory; mode 1 computes d = a . b with a staged through
+ * tensor memory and b MN-major. a, b: [128,128] bf16 row-major; d: [128,128]
+ * fp32 row-major. */
+int veda_probe_umma(const void* a, const void* b, float* d, int32_t mode,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VEDA_B200_H_ */

@@ -1,0 +1,170 @@
+"""Veda attention functions: the pluggable `AttentionFn` callables.
+
+Mirror of the reference's `miowtion/veda/attention.py` for the sparse
+student: `SparseStudent(clip, plan, predictor)(q, k, v, layer_index)` with
+q, k, v [S, H, D] bf16 returns [S, H, D] bf16 (the `AttentionFn` protocol of
+miowtion/h3/model.py:40-45). Every stage is a CUDA kernel of this package:
+    gather+pool q, k  ->  gather v  ->  predictor logits  ->  top-k lists
+    ->  tcgen05 block-sparse attention  ->  inverse permutation.
+The block lists go from the selection kernel straight to the attention
+kernel; no dense block mask and no Selection are materialised, and nothing
+synchronises the host.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from miowtion_b200 import kernels
+from miowtion_b200 import mask as veda_mask
+from miowtion_b200 import plan as veda_plan
+from miowtion_b200 import predictor as veda_predictor
+from miowtion_b200 import tiling
+
+# Default VedaConfig.collect_bytes (attention.py:30-34): bound on one
+# tile-ordered copy. The B200's 180 GB make the default one group per launch.
+DEFAULT_COLLECT_BYTES = 64 * 2**30
+
+
+@dataclasses.dataclass(frozen=True)
+class VedaConfig:
+    """Sparsity settings (attention.py:37-135; the fields the sparse path
+    reads)."""
+
+    target_budget: veda_mask.Budget = veda_mask.Budget(ratio=0.1)
+    ref_budget: veda_mask.Budget | None = None
+    tile_conditions: bool = False
+    budget_rule: str = 'topk'
+    dense_layers: frozenset[int] = frozenset()
+    collect_bytes: int = DEFAULT_COLLECT_BYTES
+
+
+@dataclasses.dataclass(frozen=True)
+class VideoSpan:
+    """A run of video-like rows on a (T, H, W) grid (h3/layout.py:42-67)."""
+
+    start: int
+    grid: tuple[int, int, int]
+    role: str = 'target'
+
+
+@dataclasses.dataclass
+class PackedLayout:
+    """The parts of the reference's `h3.layout.PackedLayout`
+    (h3/layout.py:70-108) the Veda path reads: packed length, real rows and
+    the video spans (target last)."""
+
+    seq_len: int
+    used: int
+    spans: tuple[VideoSpan, ...]
+
+    @property
+    def target(self) -> VideoSpan:
+        return self.spans[-1]
+
+
+class ClipTiling:
+    """Tile layouts of one clip, one per target shape (attention.py:138-197)."""
+
+    def __init__(self, layout: PackedLayout, config: VedaConfig,
+                 device: torch.device,
+                 condition_spans: tuple[tiling.TiledSpan, ...] = ()):
+        if config.budget_rule not in ('topk', 'threshold'):
+            raise ValueError("budget_rule must be 'topk' or 'threshold': "
+                             f'{config.budget_rule!r}')
+        self.layout = layout
+        self.config = config
+        self.device = torch.device(device)
+        spans = list(condition_spans)
+        if config.tile_conditions:
+            spans += [tiling.TiledSpan(s.start, s.grid,
+                                       tiling.least_padding_shape(s.grid))
+                      for s in layout.spans[:-1]]
+        self._condition_spans = sorted(spans, key=lambda s: s.start)
+        self._cache: dict[tiling.TileShape, tiling.TileLayout] = {}
+
+    def get(self, shape: tiling.TileShape) -> tiling.TileLayout:
+        if shape not in self._cache:
+            target = self.layout.target
+            spans = self._condition_spans + [
+                tiling.TiledSpan(target.start, target.grid, shape)]
+            self._cache[shape] = tiling.build_tile_layout(
+                spans, self.layout.used, self.layout.seq_len, self.device)
+        return self._cache[shape]
+
+    def blocks(self, tile_layout: tiling.TileLayout
+               ) -> list[veda_mask.ColumnBlock]:
+        return veda_mask.column_blocks(tile_layout, self.config.target_budget,
+                                       self.config.ref_budget)
+
+
+_HEAD_DIM_BYTES = 128 * 2
+
+
+def _chunk_heads(tile_layout: tiling.TileLayout, collect_bytes: int) -> int:
+    """Heads per chunk so one tile-ordered copy stays under collect_bytes
+    (attention.py:204-206)."""
+    return max(1, collect_bytes // (tile_layout.num_slots * _HEAD_DIM_BYTES))
+
+
+class SparseStudent:
+    """Stage-2 / evaluation attention: predictor-masked block sparsity
+    (attention.py:692-794)."""
+
+    def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
+                 predictor: veda_predictor.TileScorePredictor):
+        reason = kernels.unavailable_reason(clip.device)
+        if reason is not None:
+            raise RuntimeError(
+                f'SparseStudent needs the B200 block-sparse kernels '
+                f'({reason}); refusing to fall back silently')
+        if clip.config.budget_rule != 'topk':
+            raise NotImplementedError("only the 'topk' budget rule has a "
+                                      'B200 kernel')
+        self.clip = clip
+        self.plan = plan
+        self.predictor = predictor
+        self.calls = {'sparse': 0, 'dense': 0}
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 layer_index: int) -> torch.Tensor:
+        used = self.clip.layout.used
+        if layer_index in self.clip.config.dense_layers:
+            self.calls['dense'] += 1
+            return kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5,
+                                           False, used=used)[0]
+        self.calls['sparse'] += 1
+        seq_len = q.shape[0]
+        out = torch.empty_like(q)
+        if used < seq_len:
+            out[used:] = 0
+        covered = 0
+        for group in self.plan.head_groups(layer_index, self.clip.device):
+            tile_layout = self.clip.get(group.shape)
+            covered += group.heads.numel()
+            for heads in group.heads.split(
+                    _chunk_heads(tile_layout, self.clip.config.collect_bytes)):
+                self._attend(q, k, v, layer_index, tile_layout, heads, out)
+        if covered != q.shape[1]:
+            raise ValueError(f'the plan covers {covered} heads, q has '
+                             f'{q.shape[1]}')
+        return out
+
+    def _attend(self, q, k, v, layer_index: int,
+                tile_layout: tiling.TileLayout, heads: torch.Tensor,
+                out: torch.Tensor) -> None:
+        """Sparse attention of some heads of one group, scattered to out."""
+        q_tiles, feats_q = tiling.gather_and_pool(q, tile_layout, heads)
+        k_tiles, feats_k = tiling.gather_and_pool(k, tile_layout, heads)
+        v_tiles = tiling.gather_tiles(v, tile_layout, heads)
+        with torch.no_grad():
+            logits = self.predictor.layers[layer_index](feats_q, feats_k,
+                                                        heads)
+            lists = veda_mask.select_block_lists(
+                logits[:, :tile_layout.n_video_tiles], tile_layout,
+                self.clip.blocks(tile_layout))
+        o_tiles = kernels.block_sparse_attention_lists(
+            q_tiles, k_tiles, v_tiles, lists, tile_layout)
+        tiling.scatter_rows_(out, o_tiles, tile_layout, heads)

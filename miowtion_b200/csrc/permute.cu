@@ -1,0 +1,342 @@
+// a2/a3/a12/a14: permutation into tile order with fused pooling, the inverse
+// permutation, and the LSE gather. HBM-bound byte movement.
+//
+// One CTA per (tile, head): 256 threads, each owning 8 consecutive head-dim
+// columns (one 16-byte vector) of 8 rows, so every half-warp moves one whole
+// 256-byte row per instruction (fully coalesced reads and writes). Pooling
+// (semantics of miowtion/veda/predictor.py:82-168) reduces in registers,
+// then across the 16 row groups with one shuffle and a shared-memory pass.
+#include "common.cuh"
+
+namespace veda {
+
+namespace {
+
+constexpr int kPoolThreads = 256;
+constexpr int kRowsPerThread = kTile / (kPoolThreads / 16);  // 8
+
+__device__ __forceinline__ void bf16x8_to_float(const uint4& v, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+struct GatherParams {
+  const __nv_bfloat16* x;
+  int64_t x_stride_s, x_stride_h;
+  const int64_t* perm;  // nullptr: identity (x already tile-ordered)
+  const int32_t* valid_count;
+  const int64_t* heads;  // nullptr: head h
+  __nv_bfloat16* out;    // nullptr: pool only
+  int64_t out_stride_n, out_stride_h;
+  float* feats;  // [H', n, 3D] or nullptr
+  float* sq;     // [H', n, D] or nullptr
+  float* var;    // [H', n, D] or nullptr
+  int64_t n_tiles;
+};
+
+__global__ void __launch_bounds__(kPoolThreads)
+    gather_pool_kernel(GatherParams p) {
+  const int64_t tile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int c8 = tid & 15;   // column group: columns [8*c8, 8*c8 + 8)
+  const int rg = tid >> 4;   // row group: rows rg + 16*i
+  const int64_t head = p.heads != nullptr ? p.heads[h] : h;
+  const int count = p.valid_count[tile];
+
+  uint4 vals[kRowsPerThread];
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    const int r = rg + 16 * i;
+    const int64_t slot = tile * kTile + r;
+    // Tile-ordered input keeps its padding rows (zero by contract) in the
+    // sums exactly like predictor.pool_tiles; a gather reads real rows only.
+    int64_t src = slot;
+    bool valid = true;
+    if (p.perm != nullptr) {
+      src = p.perm[slot];
+      valid = src >= 0;
+    }
+    vals[i] = make_uint4(0, 0, 0, 0);
+    if (valid)
+      vals[i] = __ldg(reinterpret_cast<const uint4*>(
+          p.x + src * p.x_stride_s + head * p.x_stride_h + 8 * c8));
+  }
+  if (p.out != nullptr) {
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      const int64_t slot = tile * kTile + rg + 16 * i;
+      *reinterpret_cast<uint4*>(p.out + slot * p.out_stride_n +
+                                h * p.out_stride_h + 8 * c8) = vals[i];
+    }
+  }
+  if (p.feats == nullptr && p.sq == nullptr && p.var == nullptr) return;
+
+  __shared__ float red[3][kPoolThreads / 32][kHeadDim];
+  __shared__ float mean_s[kHeadDim];
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  float sum[8], mx[8], mn[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    sum[c] = 0.f;
+    mx[c] = -INFINITY;
+    mn[c] = INFINITY;
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    const int r = rg + 16 * i;
+    float f[8];
+    bf16x8_to_float(vals[i], f);
+    const bool valid = r < count;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      sum[c] += f[c];  // padding rows hold 0
+      if (valid) {
+        mx[c] = fmaxf(mx[c], f[c]);
+        mn[c] = fminf(mn[c], f[c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    sum[c] += __shfl_xor_sync(0xffffffffu, sum[c], 16);
+    mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 16));
+    mn[c] = fminf(mn[c], __shfl_xor_sync(0xffffffffu, mn[c], 16));
+  }
+  if (lane < 16) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      red[0][warp][8 * c8 + c] = sum[c];
+      red[1][warp][8 * c8 + c] = mx[c];
+      red[2][warp][8 * c8 + c] = mn[c];
+    }
+  }
+  __syncthreads();
+  const float denom = static_cast<float>(max(count, 1));
+  if (tid < kHeadDim) {
+    float s = 0.f, a = -INFINITY, b = INFINITY;
+#pragma unroll
+    for (int w = 0; w < kPoolThreads / 32; ++w) {
+      s += red[0][w][tid];
+      a = fmaxf(a, red[1][w][tid]);
+      b = fminf(b, red[2][w][tid]);
+    }
+    const float mean = s / denom;
+    mean_s[tid] = mean;
+    if (p.feats != nullptr) {
+      float* f = p.feats + (static_cast<int64_t>(h) * p.n_tiles + tile) *
+                               (3 * kHeadDim);
+      const bool empty = count == 0;
+      f[tid] = empty ? 0.f : mean;
+      f[kHeadDim + tid] = empty ? 0.f : a;
+      f[2 * kHeadDim + tid] = empty ? 0.f : b;
+    }
+  }
+  if (p.sq == nullptr && p.var == nullptr) return;
+  __syncthreads();
+  // Second moments from the rows still held in registers; the centred one
+  // is two-pass (predictor.py:133-168 explains why not E[x^2] - E[x]^2).
+  float m8[8], s2[8], v2[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    m8[c] = mean_s[8 * c8 + c];
+    s2[c] = 0.f;
+    v2[c] = 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    const int r = rg + 16 * i;
+    if (r >= count) continue;
+    float f[8];
+    bf16x8_to_float(vals[i], f);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      s2[c] += f[c] * f[c];
+      const float d = f[c] - m8[c];
+      v2[c] += d * d;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    s2[c] += __shfl_xor_sync(0xffffffffu, s2[c], 16);
+    v2[c] += __shfl_xor_sync(0xffffffffu, v2[c], 16);
+  }
+  __syncthreads();
+  if (lane < 16) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      red[0][warp][8 * c8 + c] = s2[c];
+      red[1][warp][8 * c8 + c] = v2[c];
+    }
+  }
+  __syncthreads();
+  if (tid < kHeadDim) {
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int w = 0; w < kPoolThreads / 32; ++w) {
+      a += red[0][w][tid];
+      b += red[1][w][tid];
+    }
+    const int64_t base = (static_cast<int64_t>(h) * p.n_tiles + tile) *
+                         kHeadDim + tid;
+    const bool empty = count == 0;
+    if (p.sq != nullptr) p.sq[base] = empty ? 0.f : a / denom;
+    if (p.var != nullptr) p.var[base] = empty ? 0.f : b / denom;
+  }
+}
+
+struct ScatterParams {
+  const __nv_bfloat16* tiled;
+  int64_t t_stride_n, t_stride_h;
+  const int64_t* perm;
+  const int64_t* heads;
+  __nv_bfloat16* out;
+  int64_t out_stride_s, out_stride_h;
+};
+
+__global__ void __launch_bounds__(kPoolThreads)
+    scatter_kernel(ScatterParams p) {
+  const int64_t tile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int c8 = tid & 15;
+  const int rg = tid >> 4;
+  const int64_t head = p.heads != nullptr ? p.heads[h] : h;
+  uint4 vals[kRowsPerThread];
+  int64_t dst[kRowsPerThread];
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    const int64_t slot = tile * kTile + rg + 16 * i;
+    dst[i] = p.perm[slot];
+    vals[i] = __ldg(reinterpret_cast<const uint4*>(
+        p.tiled + slot * p.t_stride_n + h * p.t_stride_h + 8 * c8));
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    if (dst[i] < 0) continue;
+    *reinterpret_cast<uint4*>(p.out + dst[i] * p.out_stride_s +
+                              head * p.out_stride_h + 8 * c8) = vals[i];
+  }
+}
+
+__global__ void gather_lse_kernel(const float* lse, int64_t ls, int64_t lh,
+                                  const int64_t* perm, int64_t n_slots,
+                                  const int64_t* heads, int n_heads,
+                                  float* out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x +
+                    threadIdx.x;
+  if (i >= n_slots * n_heads) return;
+  const int64_t slot = i / n_heads;
+  const int h = static_cast<int>(i % n_heads);
+  const int64_t src = perm[slot];
+  out[i] = src >= 0 ? lse[src * ls + heads[h] * lh] : 0.f;
+}
+
+int check_rows(const void* p, int64_t stride_row, int64_t stride_head,
+               const char* name) {
+  if (reinterpret_cast<uintptr_t>(p) % 16 != 0 || stride_row % 8 != 0 ||
+      stride_head % 8 != 0)
+    return set_error(VEDA_ERR_INVALID,
+                     std::string(name) +
+                         " must be 16-byte aligned with row/head strides "
+                         "that are multiples of 8 elements");
+  return VEDA_OK;
+}
+
+}  // namespace
+
+}  // namespace veda
+
+using namespace veda;
+
+extern "C" int veda_gather_pool(const void* x, int64_t x_stride_s,
+                                int64_t x_stride_h, const int64_t* perm,
+                                const int32_t* valid_count, int64_t n_tiles,
+                                const int64_t* heads, int32_t n_heads,
+                                void* out, int64_t out_stride_n,
+                                int64_t out_stride_h, float* feats, float* sq,
+                                float* var, void* stream) {
+  VEDA_REQUIRE(x != nullptr && valid_count != nullptr,
+               "x and valid_count are required");
+  VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
+  VEDA_REQUIRE(perm != nullptr || heads == nullptr,
+               "heads needs a permutation (identity pooling uses all heads)");
+  VEDA_REQUIRE(out != nullptr || feats != nullptr || sq != nullptr ||
+                   var != nullptr,
+               "nothing to compute");
+  int rc = check_rows(x, x_stride_s, x_stride_h, "x");
+  if (rc != VEDA_OK) return rc;
+  if (out != nullptr) {
+    rc = check_rows(out, out_stride_n, out_stride_h, "out");
+    if (rc != VEDA_OK) return rc;
+  }
+  if (n_tiles == 0) return VEDA_OK;
+  GatherParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.x_stride_s = x_stride_s;
+  p.x_stride_h = x_stride_h;
+  p.perm = perm;
+  p.valid_count = valid_count;
+  p.heads = heads;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_n = out_stride_n;
+  p.out_stride_h = out_stride_h;
+  p.feats = feats;
+  p.sq = sq;
+  p.var = var;
+  p.n_tiles = n_tiles;
+  dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_heads));
+  gather_pool_kernel<<<grid, kPoolThreads, 0, as_stream(stream)>>>(p);
+  return check_launch("gather_pool_kernel");
+}
+
+extern "C" int veda_scatter(const void* tiled, int64_t t_stride_n,
+                            int64_t t_stride_h, const int64_t* perm,
+                            int64_t n_tiles, const int64_t* heads,
+                            int32_t n_heads, void* out, int64_t out_stride_s,
+                            int64_t out_stride_h, void* stream) {
+  VEDA_REQUIRE(tiled != nullptr && perm != nullptr && out != nullptr,
+               "tiled, perm and out are required");
+  VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
+  int rc = check_rows(tiled, t_stride_n, t_stride_h, "tiled");
+  if (rc != VEDA_OK) return rc;
+  rc = check_rows(out, out_stride_s, out_stride_h, "out");
+  if (rc != VEDA_OK) return rc;
+  if (n_tiles == 0) return VEDA_OK;
+  ScatterParams p{};
+  p.tiled = static_cast<const __nv_bfloat16*>(tiled);
+  p.t_stride_n = t_stride_n;
+  p.t_stride_h = t_stride_h;
+  p.perm = perm;
+  p.heads = heads;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_s = out_stride_s;
+  p.out_stride_h = out_stride_h;
+  dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_heads));
+  scatter_kernel<<<grid, kPoolThreads, 0, as_stream(stream)>>>(p);
+  return check_launch("scatter_kernel");
+}
+
+extern "C" int veda_gather_lse(const float* lse, int64_t l_stride_s,
+                               int64_t l_stride_h, const int64_t* perm,
+                               int64_t n_tiles, const int64_t* heads,
+                               int32_t n_heads, float* out, void* stream) {
+  VEDA_REQUIRE(lse != nullptr && perm != nullptr && heads != nullptr &&
+                   out != nullptr,
+               "lse, perm, heads and out are required");
+  VEDA_REQUIRE(n_heads >= 1, "bad number of heads");
+  const int64_t total = n_tiles * kTile * n_heads;
+  if (total == 0) return VEDA_OK;
+  const int threads = 256;
+  gather_lse_kernel<<<static_cast<unsigned>((total + threads - 1) / threads),
+                      threads, 0, as_stream(stream)>>>(
+      lse, l_stride_s, l_stride_h, perm, n_tiles * kTile, heads, n_heads, out);
+  return check_launch("gather_lse_kernel");
+}

@@ -1,0 +1,198 @@
+// a4: tile-predictor logits in fp32 (miowtion/veda/predictor.py:251-255,
+// :299-338):
+//   q_hat = feats_q @ proj_q[h] + mean_q,  k_hat = feats_k @ proj_k[h] + mean_k
+//   logits = q_hat . k_hat^T / sqrt(D)
+// Two SIMT fp32 GEMM kernels with shared-memory tiles. The work is small
+// (~4 GFLOP at the H3 shape) and must stay fp32 because the scores are only
+// used through their ranking.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace veda {
+
+namespace {
+
+constexpr int kFeat = 3 * kHeadDim;  // 384
+constexpr int kEmbRows = 64;
+constexpr int kEmbK = 32;
+
+// out[h, i, :] = feats[h, i, :] @ proj[heads[h]] + feats[h, i, :D]
+// grid (ceil(n/64), H', 2): z selects the q or the k side.
+struct EmbedParams {
+  const float* feats[2];
+  const float* proj[2];
+  float* out[2];
+  int64_t n[2];
+  const int64_t* heads;
+};
+
+__global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
+  const bool k_side = blockIdx.z != 0;
+  const int h = blockIdx.y;
+  const int64_t n = k_side ? p.n[1] : p.n[0];
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kEmbRows;
+  if (row0 >= n) return;
+  const int64_t head = p.heads[h];
+  const float* feats = (k_side ? p.feats[1] : p.feats[0]) +
+                       static_cast<int64_t>(h) * n * kFeat;
+  const float* proj = (k_side ? p.proj[1] : p.proj[0]) +
+                      head * kFeat * kHeadDim;
+  float* out = (k_side ? p.out[1] : p.out[0]) +
+               static_cast<int64_t>(h) * n * kHeadDim;
+
+  __shared__ float a_s[kEmbK][kEmbRows + 4];  // transposed feats chunk
+  __shared__ float b_s[kEmbK][kHeadDim];
+  const int tid = threadIdx.x;
+  const int tr = tid / 32;  // rows tr*8 .. +8
+  const int tc = tid % 32;  // cols tc*4 .. +4
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  for (int k0 = 0; k0 < kFeat; k0 += kEmbK) {
+    // feats chunk [64 rows x 32 k] -> a_s[k][row]
+    for (int e = tid; e < kEmbRows * kEmbK; e += 256) {
+      const int r = e / kEmbK, k = e % kEmbK;
+      const int64_t row = row0 + r;
+      a_s[k][r] = row < n ? feats[row * kFeat + k0 + k] : 0.f;
+    }
+    for (int e = tid; e < kEmbK * kHeadDim; e += 256) {
+      const int k = e / kHeadDim, c = e % kHeadDim;
+      b_s[k][c] = proj[static_cast<int64_t>(k0 + k) * kHeadDim + c];
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kEmbK; ++k) {
+      float a[8], b[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = a_s[k][tr * 8 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = b_s[k][tc * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = row0 + tr * 8 + i;
+    if (row >= n) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = tc * 4 + j;
+      out[row * kHeadDim + c] = acc[i][j] + feats[row * kFeat + c];
+    }
+  }
+}
+
+// logits[h, i, j] = q_hat[h, i, :] . k_hat[h, j, :] / sqrt(D)
+// grid (ceil(n_k/64), ceil(n_q/64), H'); 256 threads, 4x4 outputs each.
+__global__ void __launch_bounds__(256)
+    logits_kernel(const float* q_hat, const float* k_hat, int64_t n_q,
+                  int64_t n_k, float sqrt_d, float* logits) {
+  const int h = blockIdx.z;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * 64;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const float* qh = q_hat + static_cast<int64_t>(h) * n_q * kHeadDim;
+  const float* kh = k_hat + static_cast<int64_t>(h) * n_k * kHeadDim;
+  __shared__ float q_s[32][64 + 4];
+  __shared__ float k_s[32][64 + 4];
+  const int tid = threadIdx.x;
+  const int ti = tid / 16, tj = tid % 16;
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
+    for (int e = tid; e < 64 * 32; e += 256) {
+      const int r = e / 32, d = e % 32;
+      q_s[d][r] = (i0 + r < n_q) ? qh[(i0 + r) * kHeadDim + d0 + d] : 0.f;
+      k_s[d][r] = (j0 + r < n_k) ? kh[(j0 + r) * kHeadDim + d0 + d] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int d = 0; d < 32; ++d) {
+      float a[4], b[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        a[x] = q_s[d][ti * 4 + x];
+        b[x] = k_s[d][tj * 4 + x];
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(a[x], b[y], acc[x][y]);
+    }
+    __syncthreads();
+  }
+  float* out = logits + static_cast<int64_t>(h) * n_q * n_k;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int64_t i = i0 + ti * 4 + x;
+    if (i >= n_q) continue;
+#pragma unroll
+    for (int y = 0; y < 4; ++y) {
+      const int64_t j = j0 + tj * 4 + y;
+      // Divided, not multiplied by the reciprocal, as the reference does.
+      if (j < n_k) out[i * n_k + j] = __fdiv_rn(acc[x][y], sqrt_d);
+    }
+  }
+}
+
+}  // namespace
+
+}  // namespace veda
+
+using namespace veda;
+
+extern "C" int64_t veda_predict_workspace(int32_t n_heads, int64_t n_q,
+                                          int64_t n_k) {
+  return static_cast<int64_t>(n_heads) * (n_q + n_k) * kHeadDim *
+         static_cast<int64_t>(sizeof(float));
+}
+
+extern "C" int veda_predict_logits(const float* feats_q, const float* feats_k,
+                                   const float* proj_q, const float* proj_k,
+                                   const int64_t* heads, int32_t n_heads,
+                                   int64_t n_q, int64_t n_k, float* logits,
+                                   void* workspace, int64_t workspace_bytes,
+                                   void* stream) {
+  VEDA_REQUIRE(feats_q && feats_k && proj_q && proj_k && heads && logits,
+               "all tensors are required");
+  VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
+  VEDA_REQUIRE(n_q >= 0 && n_k >= 0, "bad tile counts");
+  VEDA_REQUIRE(workspace != nullptr &&
+                   workspace_bytes >= veda_predict_workspace(n_heads, n_q, n_k),
+               "workspace is smaller than veda_predict_workspace()");
+  if (n_q == 0 || n_k == 0) return VEDA_OK;
+  float* q_hat = static_cast<float*>(workspace);
+  float* k_hat = q_hat + static_cast<int64_t>(n_heads) * n_q * kHeadDim;
+  EmbedParams p{};
+  p.feats[0] = feats_q;
+  p.feats[1] = feats_k;
+  p.proj[0] = proj_q;
+  p.proj[1] = proj_k;
+  p.out[0] = q_hat;
+  p.out[1] = k_hat;
+  p.n[0] = n_q;
+  p.n[1] = n_k;
+  p.heads = heads;
+  const int64_t nmax = n_q > n_k ? n_q : n_k;
+  dim3 g1(static_cast<unsigned>((nmax + kEmbRows - 1) / kEmbRows),
+          static_cast<unsigned>(n_heads), 2);
+  embed_kernel<<<g1, 256, 0, as_stream(stream)>>>(p);
+  int rc = check_launch("embed_kernel");
+  if (rc != VEDA_OK) return rc;
+  dim3 g2(static_cast<unsigned>((n_k + 63) / 64),
+          static_cast<unsigned>((n_q + 63) / 64),
+          static_cast<unsigned>(n_heads));
+  logits_kernel<<<g2, 256, 0, as_stream(stream)>>>(
+      q_hat, k_hat, n_q, n_k, sqrtf(static_cast<float>(kHeadDim)), logits);
+  return check_launch("logits_kernel");
+}

@@ -1,0 +1,184 @@
+"""The block-sparse attention backend: drop-in for the reference's
+`miowtion/kernels/fa4.py` (same function names, argument meaning, tensor
+layouts and errors), backed by the sm_100a kernels of this package.
+
+    from miowtion_b200 import kernels as fa4
+
+q, k, v are tile-ordered [N, H', D] bf16 (the reference's FA4-native
+seq-major layout). Block patterns are dense block masks [H', R, n] bool, or
+the full/partial index lists of `mask.select_block_lists`, which the hot
+path passes straight through. There is no fallback: without a B200 and the
+built library every entry point raises.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from miowtion_b200 import _lib
+from miowtion_b200 import mask as veda_mask
+from miowtion_b200 import tiling
+
+_TILE = tiling.TILE_SIZE
+# Host launches are stateless and thread-safe; the lock only mirrors the
+# reference's serialization point (fa4.py:66-70) for callers that rely on it.
+_CALL_LOCK = threading.Lock()
+
+
+def available(device: torch.device | None = None) -> bool:
+    """True on a CUDA sm_100 device with the library built (fa4.py:122-137)."""
+    return unavailable_reason(device) is None
+
+
+def unavailable_reason(device: torch.device | None = None,
+                       dtype: torch.dtype | None = None) -> str | None:
+    """Why the kernels cannot run on `device`, or None (fa4.py:150-182)."""
+    if not torch.cuda.is_available():
+        return 'no CUDA device'
+    if device is not None and torch.device(device).type != 'cuda':
+        return f'device {device} is not CUDA'
+    if dtype is not None and dtype != torch.bfloat16:
+        return f'the kernels take bf16, not {dtype}'
+    major, minor = torch.cuda.get_device_capability(device)
+    if (major, minor) != (10, 0):
+        return (f'sm_{major}{minor} has no tcgen05 tensor cores; the kernels '
+                'are built for sm_100a (B200)')
+    try:
+        _lib.load()
+    except RuntimeError as e:
+        return str(e)
+    return None
+
+
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    scale: float, return_lse: bool, used: int | None = None
+                    ) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Dense attention. q, k, v: [S, H, D] -> out [S, H, D], lse [S, H]
+    (fa4.py:185-205). `used` restricts attention to rows [0, used) with
+    zero outputs (and lse) on the rest (h3/attention.py:28-102)."""
+    _require(q, 'dense_attention')
+    seq_len, heads, dim = q.shape
+    used = seq_len if used is None else used
+    for t in (k, v):
+        if t.shape != q.shape or t.stride() != q.stride():
+            raise ValueError('q, k and v must share shape and strides')
+    out = torch.empty_like(q)
+    lse = (torch.empty(seq_len, heads, dtype=torch.float32, device=q.device)
+           if return_lse else None)
+    _lib.call('veda_dense_fwd', q.data_ptr(), k.data_ptr(), v.data_ptr(),
+              q.stride(0), q.stride(1), seq_len, used, heads, out.data_ptr(),
+              out.stride(0), out.stride(1), _lib.ptr(lse),
+              lse.stride(0) if lse is not None else 0,
+              lse.stride(1) if lse is not None else 0, float(scale),
+              _lib.stream_ptr(q.device))
+    return out, lse
+
+
+def index_lists(block_mask: torch.Tensor, layout: tiling.TileLayout,
+                transpose: bool = False) -> tuple[torch.Tensor, ...]:
+    """Full / partial index lists (fa4.py:275-296):
+    (partial_cnt, partial_idx, full_cnt, full_idx), cnt [1, H', rows] and
+    idx [1, H', rows, cols] int32, bit-identical to the reference's
+    (members ascending, then the non-members ascending)."""
+    lists = _lists(block_mask, layout, transpose=transpose, tails=True)
+    return lists.as_fa4()
+
+
+def _lists(block_mask: torch.Tensor, layout: tiling.TileLayout,
+           transpose: bool, tails: bool) -> veda_mask.BlockLists:
+    if block_mask.dim() != 3 or block_mask.shape[2] != layout.n_tiles:
+        raise ValueError('block_mask must be [H\', R, n_tiles]')
+    if not block_mask.is_cuda:
+        raise RuntimeError('index_lists runs on CUDA only (no CPU fallback)')
+    heads, rows, cols = block_mask.shape
+    if transpose and rows != layout.n_tiles:
+        raise ValueError('transposed lists need all n_tiles query rows')
+    m = block_mask.to(torch.uint8).contiguous()
+    out_rows, out_cols = (cols, rows) if transpose else (rows, cols)
+    dev = block_mask.device
+    lists = veda_mask.BlockLists(
+        part_cnt=torch.empty(heads, out_rows, dtype=torch.int32, device=dev),
+        part_idx=torch.empty(heads, out_rows, out_cols, dtype=torch.int32,
+                             device=dev),
+        full_cnt=torch.empty(heads, out_rows, dtype=torch.int32, device=dev),
+        full_idx=torch.empty(heads, out_rows, out_cols, dtype=torch.int32,
+                             device=dev))
+    _lib.call('veda_index_lists', m.data_ptr(), heads, rows, cols,
+              layout.valid_count.data_ptr(), 1 if transpose else 0,
+              lists.part_cnt.data_ptr(), lists.part_idx.data_ptr(),
+              lists.full_cnt.data_ptr(), lists.full_idx.data_ptr(),
+              1 if tails else 0, _lib.stream_ptr(dev))
+    return lists
+
+
+def _require(q: torch.Tensor, op: str) -> None:
+    reason = unavailable_reason(q.device, q.dtype)
+    if reason is not None:
+        raise NotImplementedError(
+            f'{op} unavailable on {q.device}: {reason}; refusing to fall back '
+            'to dense attention')
+
+
+def block_sparse_attention_lists(q: torch.Tensor, k: torch.Tensor,
+                                 v: torch.Tensor,
+                                 lists: veda_mask.BlockLists,
+                                 layout: tiling.TileLayout,
+                                 return_lse: bool = False):
+    """Forward over prebuilt lists (rows of `lists` = query tiles of q)."""
+    _require(q, 'block_sparse_attention')
+    for name, t in (('q', q), ('k', k), ('v', v)):
+        tiling._check_rows(t, name)  # pylint: disable=protected-access
+    heads = q.shape[1]
+    n_q = q.shape[0] // _TILE
+    if q.shape[0] != n_q * _TILE or k.shape[0] != layout.num_slots or (
+            v.shape != k.shape):
+        raise ValueError('q must hold whole tiles; k, v all key tiles')
+    if lists.part_cnt.shape != (heads, n_q):
+        raise ValueError(f'lists cover {tuple(lists.part_cnt.shape)} '
+                         f'(heads, query tiles), expected {(heads, n_q)}')
+    out = torch.empty_like(q)
+    lse = (torch.empty(heads, n_q * _TILE, dtype=torch.float32,
+                       device=q.device) if return_lse else None)
+    _lib.call('veda_bsa_fwd', q.data_ptr(), q.stride(0), q.stride(1),
+              k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+              v.stride(0), v.stride(1), heads, n_q, layout.n_tiles,
+              layout.valid_count.data_ptr(), lists.part_cnt.data_ptr(),
+              lists.part_idx.data_ptr(), lists.full_cnt.data_ptr(),
+              lists.full_idx.data_ptr(), lists.part_idx.shape[-1],
+              out.data_ptr(), out.stride(0), out.stride(1), _lib.ptr(lse),
+              1.0 / math.sqrt(q.shape[-1]), _lib.stream_ptr(q.device))
+    return (out, lse) if return_lse else out
+
+
+def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           block_mask: torch.Tensor,
+                           layout: tiling.TileLayout,
+                           return_lse: bool = False):
+    """Block-sparse attention on tile-ordered tensors (fa4.py:299-377).
+
+    Args:
+        q: [R * 128, H', D] bf16 query tiles (all tiles, or the subset whose
+            rows `block_mask` describes).
+        k, v: [N, H', D] bf16 (all key tiles).
+        block_mask: [H', R, n_tiles] bool; empty key tiles are skipped.
+        layout: Tile layout (valid prefix of every key tile).
+        return_lse: Also return the [H', R * 128] fp32 log-sum-exp.
+
+    Raises:
+        NotImplementedError: Off B200 (no fallback).
+        ValueError: If gradients are required for a subset of query tiles.
+    """
+    _require(q, 'block_sparse_attention')
+    needs_grad = torch.is_grad_enabled() and any(
+        t.requires_grad for t in (q, k, v))
+    if needs_grad and block_mask.shape[1] != layout.n_tiles:
+        raise ValueError('backward needs the block mask of all query tiles')
+    if needs_grad:
+        raise NotImplementedError('block-sparse backward is not built yet')
+    lists = _lists(block_mask, layout, transpose=False, tails=False)
+    with _CALL_LOCK:
+        return block_sparse_attention_lists(q, k, v, lists, layout,
+                                            return_lse)

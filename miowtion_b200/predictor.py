@@ -1,0 +1,127 @@
+"""Tile-score predictor: which key tiles each query tile should attend.
+
+Mirror of the reference's `miowtion/veda/predictor.py` for the default
+predictor: per tile, q and k are pooled into [mean | max | min]; per layer
+and head a residual projection maps them to D dims,
+    q_hat = pool_q @ P_q[h] + mean_q,   k_hat likewise,
+and block logits are q_hat . k_hat / sqrt(D) in fp32. Pooling and logits run
+in CUDA kernels (csrc/permute.cu, csrc/predict.cu).
+
+The reference's optional terms (`count_term`, `second_order_rank > 0`) are
+not implemented on the device and raise NotImplementedError.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from miowtion_b200 import _lib
+from miowtion_b200 import tiling
+
+INIT_STD = 1e-4  # predictor.py:70
+SECOND_RAW = 'raw'
+SECOND_CENTRAL = 'central'
+
+
+@torch.no_grad()
+def pool_tiles(x: torch.Tensor, layout: tiling.TileLayout,
+               second: str | None = None) -> torch.Tensor:
+    """Masked mean/max/min over the real rows of every tile
+    (predictor.py:82-130): [N, H', D] bf16 -> [H', n, 3D] fp32, or the
+    second moment [H', n, D] ('raw' E[x^2], 'central' Var(x))."""
+    if second not in (None, SECOND_RAW, SECOND_CENTRAL):
+        raise ValueError(f'unknown second moment {second!r}')
+    tiling._check_rows(x, 'x')  # pylint: disable=protected-access
+    if x.shape[0] != layout.num_slots:
+        raise ValueError('x must be tile-ordered [num_slots, H\', D]')
+    heads, dim = x.shape[1], x.shape[2]
+    out = torch.empty(heads, layout.n_tiles, dim if second else 3 * dim,
+                      dtype=torch.float32, device=x.device)
+    feats = out if second is None else None
+    sq = out if second == SECOND_RAW else None
+    var = out if second == SECOND_CENTRAL else None
+    _lib.call('veda_gather_pool', x.data_ptr(), x.stride(0), x.stride(1),
+              None, layout.valid_count.data_ptr(), layout.n_tiles, None,
+              heads, None, 0, 0, _lib.ptr(feats), _lib.ptr(sq),
+              _lib.ptr(var), _lib.stream_ptr(x.device))
+    return out
+
+
+def predict_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
+                   proj_q: torch.Tensor, proj_k: torch.Tensor,
+                   heads: torch.Tensor) -> torch.Tensor:
+    """[H', n_q, n_k] fp32 logits of pooled features (predictor.py:251-338)."""
+    if feats_q.dim() != 3 or feats_q.shape[-1] != 3 * 128:
+        raise ValueError('features must be [H\', n, 384]')
+    if not feats_q.is_cuda:
+        raise RuntimeError('the predictor kernels run on CUDA only')
+    heads = heads.to(device=feats_q.device, dtype=torch.int64).contiguous()
+    feats_q = feats_q.float().contiguous()
+    feats_k = feats_k.float().contiguous()
+    proj_q = proj_q.detach().float().contiguous()
+    proj_k = proj_k.detach().float().contiguous()
+    n_heads, n_q = feats_q.shape[0], feats_q.shape[1]
+    n_k = feats_k.shape[1]
+    if heads.numel() != n_heads or feats_k.shape[0] != n_heads:
+        raise ValueError('heads and features disagree on the head count')
+    lib = _lib.load()
+    ws_bytes = lib.veda_predict_workspace(n_heads, n_q, n_k)
+    workspace = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32,
+                            device=feats_q.device)
+    logits = torch.empty(n_heads, n_q, n_k, dtype=torch.float32,
+                         device=feats_q.device)
+    _lib.call('veda_predict_logits', feats_q.data_ptr(), feats_k.data_ptr(),
+              proj_q.data_ptr(), proj_k.data_ptr(), heads.data_ptr(),
+              n_heads, n_q, n_k, logits.data_ptr(), workspace.data_ptr(),
+              ws_bytes, _lib.stream_ptr(feats_q.device))
+    return logits
+
+
+class LayerPredictor(nn.Module):
+    """Projections of one layer: proj_q, proj_k [num_heads, 3D, D]
+    (predictor.py:197-230)."""
+
+    def __init__(self, num_heads: int, head_dim: int,
+                 second_order_rank: int = 0, count_term: bool = False):
+        super().__init__()
+        if second_order_rank or count_term:
+            raise NotImplementedError(
+                'second-order and count terms have no B200 kernel')
+        if head_dim != 128:
+            raise NotImplementedError('the predictor kernels take head_dim 128')
+        self.head_dim = head_dim
+        self.second_order_rank = 0
+        self.proj_q = nn.Parameter(torch.empty(num_heads, 3 * head_dim,
+                                               head_dim))
+        self.proj_k = nn.Parameter(torch.empty(num_heads, 3 * head_dim,
+                                               head_dim))
+        nn.init.normal_(self.proj_q, std=INIT_STD)
+        nn.init.normal_(self.proj_k, std=INIT_STD)
+
+    def forward(self, feats_q: torch.Tensor, feats_k: torch.Tensor,
+                heads: torch.Tensor) -> torch.Tensor:
+        """Block logits [H', n_q, n_k] fp32 (predictor.py:299-338)."""
+        return predict_logits(feats_q, feats_k, self.proj_q, self.proj_k,
+                              heads)
+
+
+class TileScorePredictor(nn.Module):
+    """All layers: `layers.{i}.proj_q` / `layers.{i}.proj_k`
+    (predictor.py:341-410). Kept replicated across devices."""
+
+    def __init__(self, num_layers: int, num_heads: int, head_dim: int,
+                 second_order_rank: int = 0, count_term: bool = False):
+        super().__init__()
+        self.second_order_rank = second_order_rank
+        self.count_term = count_term
+        self.layers = nn.ModuleList(
+            LayerPredictor(num_heads, head_dim, second_order_rank, count_term)
+            for _ in range(num_layers))
+
+    def scores(self, layer: int, q_tiles: torch.Tensor, k_tiles: torch.Tensor,
+               layout: tiling.TileLayout, heads: torch.Tensor) -> torch.Tensor:
+        """Block logits of one head group [H', n, n] fp32."""
+        feats_q = pool_tiles(q_tiles, layout)
+        feats_k = pool_tiles(k_tiles, layout)
+        return self.layers[layer](feats_q, feats_k, heads)

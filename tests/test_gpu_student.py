@@ -1,0 +1,98 @@
+"""The whole sparse layer (SparseStudent) against the oracle's restatement of
+the reference's SparseStudent (veda/attention.py:724-794)."""
+
+import numpy as np
+import pytest
+import torch
+
+import inputs
+from miowtion_b200 import attention as veda_attention
+from miowtion_b200 import mask as veda_mask
+from miowtion_b200 import plan as veda_plan
+from miowtion_b200 import predictor as veda_predictor
+from miowtion_b200 import tiling
+from oracle import veda_oracle as vo
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+
+
+def make_student(seq_len, used, spans, shapes, head_shape, budget, weights):
+    layout = veda_attention.PackedLayout(seq_len, used, tuple(
+        veda_attention.VideoSpan(s, g) for s, g in spans))
+    config = veda_attention.VedaConfig(target_budget=budget)
+    clip = veda_attention.ClipTiling(layout, config, torch.device(DEV))
+    plan = veda_plan.TilePlan('test', spans[-1][1], shapes, [head_shape])
+    pred = veda_predictor.TileScorePredictor(1, len(head_shape), 128)
+    with torch.no_grad():
+        pred.layers[0].proj_q.copy_(weights[0])
+        pred.layers[0].proj_k.copy_(weights[1])
+    return veda_attention.SparseStudent(clip, plan, pred.to(DEV)), clip, plan
+
+
+def oracle_groups(clip, plan, spans_np):
+    groups = []
+    for g in plan.head_groups(0, 'cpu'):
+        lay = vo.build_tile_layout(
+            [vo.Span(s, tuple(grid), (g.shape.t, g.shape.h, g.shape.w))
+             for s, grid in spans_np], clip.layout.used, clip.layout.seq_len)
+        groups.append((lay, g.heads.numpy()))
+    return groups
+
+
+def run_case(seq_len, used, spans, shapes, head_shape, ratio, seed):
+    heads = len(head_shape)
+    q, k, v = inputs.qkv(seq_len, heads, 128, seed, torch.bfloat16)
+    w = inputs.predictor_weights(heads, 128, seed + 100, 0.02)
+    student, clip, plan = make_student(
+        seq_len, used, spans, shapes, head_shape,
+        veda_mask.Budget(ratio=ratio), w)
+    out = student(q.to(DEV), k.to(DEV), v.to(DEV), 0)
+    torch.cuda.synchronize()
+    want, info = vo.sparse_student_layer(
+        q.float().numpy(), k.float().numpy(), v.float().numpy(),
+        oracle_groups(clip, plan, spans), w[0].numpy(), w[1].numpy(),
+        vo.Budget(ratio=ratio), used=used)
+    return out.float().cpu().numpy(), want, info, student, clip, plan, (q, k,
+                                                                       v)
+
+
+def test_cfg1_layer_matches_oracle():
+    spec = inputs.CFG1
+    got, want, info, student, clip, plan, _ = run_case(
+        spec['seq_len'], spec['used'], [(0, spec['grid'])],
+        [tiling.TileShape(*spec['shape'])], [0] * spec['heads'],
+        spec['ratio'], spec['seed'])
+    assert (info[0]['mask'].sum(-1) == 4).all()
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2)
+    assert student.calls == {'sparse': 1, 'dense': 0}
+
+
+def test_two_shapes_text_rows_and_padding_match_oracle():
+    """Two head groups, a padded grid (partial tiles), global text rows and
+    padding rows [used, seq_len)."""
+    text, grid = 300, (8, 12, 20)
+    used = text + grid[0] * grid[1] * grid[2]
+    got, want, info, student, clip, plan, (q, k, v) = run_case(
+        used + 40, used, [(text, grid)],
+        [tiling.TileShape(2, 8, 8), tiling.TileShape(1, 8, 16)],
+        [0, 1, 0, 1], 0.3, 9)
+    assert (got[used:] == 0).all()
+    # Logit near-ties could flip a selection between fp32 orderings; the
+    # inputs here have none, so the masks agree exactly and so do outputs.
+    for g, (grp, (lay, heads)) in zip(plan.head_groups(0, DEV),
+                                      zip(info, oracle_groups(clip, plan,
+                                                              [(text, grid)]))):
+        tl = clip.get(g.shape)
+        qt, fq = tiling.gather_and_pool(q.to(DEV), tl, g.heads)
+        kt, fk = tiling.gather_and_pool(k.to(DEV), tl, g.heads)
+        logits = student.predictor.layers[0](fq, fk, g.heads)
+        np.testing.assert_allclose(logits.cpu().numpy(), grp['logits'],
+                                   rtol=1e-4, atol=1e-5)
+        lists = veda_mask.select_block_lists(
+            logits[:, :tl.n_video_tiles], tl, clip.blocks(tl),
+            want_mask=True)
+        np.testing.assert_array_equal(lists.mask.cpu().numpy().astype(bool),
+                                      grp['mask'])
+    np.testing.assert_allclose(got[:used], want[:used], rtol=2e-2,
+                               atol=2e-2)
