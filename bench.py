@@ -1,0 +1,430 @@
+"""Benchmark of the Veda sparse-attention layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
+    python bench.py --impl reference ...   # the reference algorithm on CPU
+
+One step = one Veda attention layer forward over synthetic q, k, v already
+resident in HBM: permute + pool q/k/v, predictor logits, budgeted top-k
+lists, tcgen05 block-sparse attention, inverse permutation. With N > 1 the
+heads are split over the ranks by a Ulysses all-to-all from the
+sequence-sharded layout (strong scaling: the layer is fixed, N grows).
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from miowtion_b200 import attention as veda_attention  # noqa: E402
+from miowtion_b200 import mask as veda_mask  # noqa: E402
+from miowtion_b200 import plan as veda_plan  # noqa: E402
+from miowtion_b200 import predictor as veda_predictor  # noqa: E402
+from miowtion_b200 import tiling  # noqa: E402
+from miowtion_b200 import ulysses  # noqa: E402
+
+METRIC = ('sparse-attn ms/layer @90% sparsity; effective TFLOP/s; '
+          'frac of bf16 peak')
+BLOCK_FLOPS = 4 * 128 * 128 * 128  # QK^T + PV of one 128x128 block, fwd
+
+# BASELINE.json configs 2-4 (config 1 is the CPU-sized parity case).
+CONFIGS = {
+    'cfg2': dict(desc='1xB200 fwd, 24 heads, grid (20,32,56)=35840 tokens, '
+                      'tile 2x8x8, 280x280 tiles, 28 key tiles/row (90%)',
+                 heads=24, seq_len=35840, used=35840, target=(0, (20, 32, 56)),
+                 cond=None, shapes=[(2, 8, 8)], head_shape=[0] * 24,
+                 target_ratio=0.1, ref_ratio=None, seed=1),
+    'cfg3': dict(desc='H3-scale fwd, 48 heads, 1024 text + grid (26,45,80), '
+                      'heads 0-23 tile 2x8x8, 24-47 tile 1x8x16, 90% budget',
+                 heads=48, seq_len=94624, used=94624,
+                 target=(1024, (26, 45, 80)), cond=None,
+                 shapes=[(2, 8, 8), (1, 8, 16)],
+                 head_shape=[0] * 24 + [1] * 24, target_ratio=0.1,
+                 ref_ratio=None, seed=2),
+    'cfg4': dict(desc='Ref2VA fwd, 48 heads, ref grid (4,45,80) at 95% + '
+                      'target grid (26,45,80) at 90%, tile 2x8x8',
+                 heads=48, seq_len=108000, used=108000,
+                 target=(14400, (26, 45, 80)), cond=(0, (4, 45, 80)),
+                 shapes=[(2, 8, 8)], head_shape=[0] * 48, target_ratio=0.1,
+                 ref_ratio=0.05, seed=3),
+}
+
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+        peaks['source'] = 'measured'
+        return peaks
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0,
+            'bf16_tflops_sustained': 1400.0, 'source': 'fallback'}
+
+
+def build_student(cfg, device, heads_plan=None):
+    layout = veda_attention.PackedLayout(
+        cfg['seq_len'], cfg['used'],
+        (veda_attention.VideoSpan(cfg['target'][0], cfg['target'][1]),))
+    cond = ()
+    if cfg['cond'] is not None:
+        cond = (tiling.TiledSpan(cfg['cond'][0], cfg['cond'][1],
+                                 tiling.TileShape(2, 8, 8)),)
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=cfg['target_ratio']),
+        ref_budget=(veda_mask.Budget(ratio=cfg['ref_ratio'])
+                    if cfg['ref_ratio'] else None))
+    clip = veda_attention.ClipTiling(layout, config, device, cond)
+    plan = heads_plan or veda_plan.TilePlan(
+        'bench', cfg['target'][1],
+        [tiling.TileShape(*s) for s in cfg['shapes']], [cfg['head_shape']])
+    local_heads = len(plan.head_shape[0])
+    pred = predictor_for(cfg, device)
+    return veda_attention.SparseStudent(clip, plan, pred), clip, plan, \
+        local_heads
+
+
+def predictor_for(cfg, device):
+    """Random-init predictor of the reference architecture, N(0, 0.02)."""
+    gen = torch.Generator().manual_seed(1000 + cfg['seed'])
+    pred = veda_predictor.TileScorePredictor(1, cfg['heads'], 128)
+    with torch.no_grad():
+        for p in (pred.layers[0].proj_q, pred.layers[0].proj_k):
+            p.copy_(torch.randn(p.shape, generator=gen) * 0.02)
+    return pred.to(device)
+
+
+def synthetic_qkv(cfg, rows, row0, device):
+    """q, k, v rows [row0, row0+rows) of ~N(0,1) bf16 [S, H, 128], drawn
+    per 4096-row chunk from a seeded device generator (so every rank draws
+    the same global tensors)."""
+    heads = cfg['heads']
+    out = []
+    for t in range(3):
+        x = torch.empty(rows, heads, 128, dtype=torch.bfloat16, device=device)
+        chunk = 4096
+        for c0 in range(row0 - row0 % chunk, row0 + rows, chunk):
+            gen = torch.Generator(device=device)
+            gen.manual_seed(cfg['seed'] * 1_000_003 + t * 7919 + c0 // chunk)
+            blk = torch.randn(chunk, heads, 128, generator=gen, device=device)
+            lo, hi = max(c0, row0), min(c0 + chunk, row0 + rows)
+            x[lo - row0:hi - row0] = blk[lo - c0:hi - c0].to(torch.bfloat16)
+        out.append(x)
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,'
+             'clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+             'clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,'
+             'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--id={self.index}',
+                 f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
+                 '-lms', '100'], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
+                 'sw_power_cap']
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(mhz) if mhz else None,
+                'sm_max_mhz': max_mhz, 'reasons': sorted(reasons),
+                'samples': len(mhz)}
+
+
+def cpu_baseline(cfg, budget_s=12.0, timed_steps=None):
+    """The reference algorithm (the oracle restatement) on the host cores:
+    the full layer for a time-bounded sample of heads, extrapolated to all
+    heads (heads are independent with equal per-head cost)."""
+    from oracle import veda_oracle as vo
+    import threadpoolctl
+    seq_len, used = cfg['seq_len'], cfg['used']
+    gen = torch.Generator().manual_seed(1000 + cfg['seed'])
+    pq = (torch.randn(cfg['heads'], 384, 128, generator=gen) * 0.02).numpy()
+    pk = (torch.randn(cfg['heads'], 384, 128, generator=gen) * 0.02).numpy()
+    spans_target = cfg['target']
+    layouts = {}
+    times = []
+    head = 0
+    t_all = time.perf_counter()
+    while True:
+        shape = tuple(cfg['shapes'][cfg['head_shape'][head]])
+        if shape not in layouts:
+            spans = []
+            if cfg['cond'] is not None:
+                spans.append(vo.Span(cfg['cond'][0], cfg['cond'][1],
+                                     (2, 8, 8)))
+            spans.append(vo.Span(spans_target[0], spans_target[1], shape))
+            layouts[shape] = vo.build_tile_layout(spans, used, seq_len)
+        gen_h = torch.Generator().manual_seed(cfg['seed'] * 31 + head)
+        q, k, v = (torch.randn(seq_len, 1, 128, generator=gen_h).to(
+            torch.bfloat16).float().numpy() for _ in range(3))
+        t0 = time.perf_counter()
+        vo.sparse_student_layer(
+            q, k, v, [(layouts[shape], np.array([0]))], pq[head:head + 1],
+            pk[head:head + 1], vo.Budget(ratio=cfg['target_ratio']),
+            vo.Budget(ratio=cfg['ref_ratio']) if cfg['ref_ratio'] else None,
+            used=used)
+        times.append(time.perf_counter() - t0)
+        head = (head + 1) % cfg['heads']
+        if timed_steps is not None:
+            if len(times) >= timed_steps:
+                break
+        elif time.perf_counter() - t_all > budget_s:
+            break
+    per_head = sum(times) / len(times)
+    threads = max([i.get('num_threads', 1)
+                   for i in threadpoolctl.threadpool_info()] or [1])
+    return per_head * cfg['heads'] * 1e3, len(times), threads, times
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    warm = max(0, args.warmup)
+    steps = max(1, args.steps)
+    _, _, threads, times = cpu_baseline(cfg, timed_steps=warm + steps)
+    timed = times[warm:]
+    ms = sum(timed) / len(timed) * cfg['heads'] * 1e3
+    sample = (f'per step one head (of {cfg["heads"]}) of the full layer '
+              f'through the oracle (numpy restatement of the reference), '
+              f'x{cfg["heads"]} heads')
+    line = {
+        'metric': METRIC, 'value': ms, 'unit': 'ms/layer', 'impl': 'reference',
+        'n_gpus': args.gpus, 'steps': steps, 'warmup': warm,
+        'ms_per_step': ms, 'higher_is_better': False, 'scaling': 'strong',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': f'{args.config}: {cfg["desc"]}',
+                   'parallelism': 'cpu'},
+        'cpu_baseline': {'value': ms, 'unit': 'ms/layer', 'cores': threads,
+                         'kind': 'port', 'sample': sample},
+        'e2e': {'value': ms, 'unit': 'ms/layer', 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=30)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == 'reference':
+        run_reference(args, cfg)
+        return
+    if args.warmup < 3:
+        raise SystemExit('use at least 3 warm-up steps')
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if world != args.gpus:
+        raise SystemExit(f'--gpus {args.gpus} but WORLD_SIZE={world}')
+    device = torch.device('cuda', local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', device_id=device,
+                                timeout=datetime.timedelta(seconds=120))
+
+    seq_len, heads = cfg['seq_len'], cfg['heads']
+    if heads % world or seq_len % world:
+        raise SystemExit('heads and sequence must divide by the GPU count')
+    full_plan = veda_plan.TilePlan(
+        'bench', cfg['target'][1],
+        [tiling.TileShape(*s) for s in cfg['shapes']], [cfg['head_shape']])
+    plan = ulysses.local_plan(full_plan, rank, world) if world > 1 else None
+    student, clip, plan, local_heads = build_student(cfg, device, plan)
+    shard = seq_len // world
+    q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
+    fn = ulysses.UlyssesSparseStudent(student) if world > 1 else student
+    events = veda_attention.StageEvents()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            fn(q, k, v, 0)
+        barrier()
+        student.events = events
+        events.clear()
+        stream = torch.cuda.current_stream()
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device.index) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                fn(q, k, v, 0)
+            stop.record(stream)
+            barrier()
+        student.events = veda_attention._NO_EVENTS  # pylint: disable=protected-access
+        ms = start.elapsed_time(stop) / args.steps
+        stages = {n: t / args.steps for n, t in events.totals_ms().items()}
+        # Algorithmic work of the local heads (counted after the timing).
+        blocks = 0
+        for group in plan.head_groups(0, device):
+            tl = clip.get(group.shape)
+            qt, fq = tiling.gather_and_pool(q if world == 1 else
+                                            ulysses.seq_to_heads(q), tl,
+                                            group.heads)
+            kt, fk = tiling.gather_and_pool(k if world == 1 else
+                                            ulysses.seq_to_heads(k), tl,
+                                            group.heads)
+            logits = student.predictor.layers[0](fq, fk, group.heads)
+            lists = veda_mask.select_block_lists(
+                logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
+            blocks += int(lists.part_cnt.sum() + lists.full_cnt.sum())
+            del qt, kt
+        # End to end through the public API with host buffers: H2D of this
+        # step's q, k, v shard, the layer, D2H of the output.
+        host = [t.cpu().pin_memory() for t in (q, k, v)]
+        out_host = torch.empty_like(host[0]).pin_memory()
+        dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+        for _ in range(2):
+            for d, h in zip((dq, dk, dv), host):
+                d.copy_(h, non_blocking=True)
+            out_host.copy_(fn(dq, dk, dv, 0), non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for d, h in zip((dq, dk, dv), host):
+                d.copy_(h, non_blocking=True)
+            out_host.copy_(fn(dq, dk, dv, 0), non_blocking=True)
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    vals = torch.tensor([ms, e2e_ms, stages.get('attention', 0.0),
+                         float(blocks)], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = vals[:3].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals[3:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, tot])
+    ms, e2e_ms, attn_ms, total_blocks = vals.tolist()
+    if rank == 0:
+        peaks = load_peaks()
+        peak = peaks['bf16_tflops']
+        flops = total_blocks * BLOCK_FLOPS
+        dense_flops = 4.0 * cfg['used'] ** 2 * 128 * heads
+        eff = flops / (ms * 1e-3) / 1e12
+        attn_tflops = (flops / world) / (attn_ms * 1e-3) / 1e12
+        clk = clocks.summary()
+        line = {
+            'metric': METRIC, 'value': ms, 'unit': 'ms/layer',
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': False,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16',
+            'data': 'synthetic (seeded N(0,1) q/k/v, random-init predictor '
+                    'N(0,0.02))',
+            'config': {'workload': f'{args.config}: {cfg["desc"]}',
+                       'heads': heads, 'seq_len': seq_len, 'head_dim': 128,
+                       'parallelism': f'ulysses-heads x{world}',
+                       'l2': 'inputs exceed L2 (q/k/v/tiles >> 126 MB)'},
+            'effective_tflops': eff,
+            'frac_of_peak': eff / peak,
+            'computed_blocks': int(total_blocks),
+            'dense_equiv_tflop': dense_flops / 1e12,
+            'stages_ms': stages,
+            'roofline': {
+                'bound': 'tensor', 'kernel': 'bsa_fwd_kernel',
+                'achieved': attn_tflops, 'peak': peak, 'unit': 'TFLOP/s',
+                'frac': attn_tflops / peak, 'traffic': None,
+                'peak_source': f'{peaks["source"]} bf16 burst'},
+            'e2e': {'value': e2e_ms, 'unit': 'ms/layer',
+                    'h2d_bytes_per_step': 3 * q.numel() * 2,
+                    'd2h_bytes_per_step': q.numel() * 2},
+            'gpu_launches': args.steps * launches_per_step(plan, world),
+            'clocks': clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            cpu_ms, n_heads, threads, _ = cpu_baseline(cfg)
+            line['cpu_baseline'] = {
+                'value': cpu_ms, 'unit': 'ms/layer', 'cores': threads,
+                'kind': 'port',
+                'sample': f'{n_heads} heads of {heads} through the oracle '
+                          '(numpy restatement), full layer per head, '
+                          'extrapolated linearly over heads'}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def launches_per_step(plan, world):
+    """Our kernels per layer: per head group gather+pool q, k, gather v,
+    embed, logits, select, attention, scatter."""
+    return 8 * len(plan.head_groups(0, 'cpu'))
+
+
+if __name__ == '__main__':
+    main()

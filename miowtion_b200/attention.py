@@ -109,9 +109,51 @@ def _chunk_heads(tile_layout: tiling.TileLayout, collect_bytes: int) -> int:
     return max(1, collect_bytes // (tile_layout.num_slots * _HEAD_DIM_BYTES))
 
 
+class StageEvents:
+    """Optional per-stage CUDA events on the launching stream (for timing:
+    the reference's docs time stages with torch.profiler labels). Records
+    (name, start, stop) around each stage of `SparseStudent._attend`."""
+
+    def __init__(self):
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def start(self, name: str):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return name, ev
+
+    def stop(self, token) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.records.append((token[0], token[1], ev))
+
+    def totals_ms(self) -> dict[str, float]:
+        torch.cuda.synchronize()
+        out: dict[str, float] = {}
+        for name, a, b in self.records:
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+    def clear(self) -> None:
+        self.records.clear()
+
+
+class _NoEvents:
+    def start(self, name):
+        return None
+
+    def stop(self, token):
+        pass
+
+
+_NO_EVENTS = _NoEvents()
+
+
 class SparseStudent:
     """Stage-2 / evaluation attention: predictor-masked block sparsity
     (attention.py:692-794)."""
+
+    events = _NO_EVENTS  # set a StageEvents to time the stages
 
     def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
                  predictor: veda_predictor.TileScorePredictor):
@@ -156,15 +198,27 @@ class SparseStudent:
                 tile_layout: tiling.TileLayout, heads: torch.Tensor,
                 out: torch.Tensor) -> None:
         """Sparse attention of some heads of one group, scattered to out."""
+        ev = self.events
+        t = ev.start('permute_pool')
         q_tiles, feats_q = tiling.gather_and_pool(q, tile_layout, heads)
         k_tiles, feats_k = tiling.gather_and_pool(k, tile_layout, heads)
         v_tiles = tiling.gather_tiles(v, tile_layout, heads)
+        ev.stop(t)
         with torch.no_grad():
+            t = ev.start('score')
             logits = self.predictor.layers[layer_index](feats_q, feats_k,
                                                         heads)
+            ev.stop(t)
+            t = ev.start('topk')
             lists = veda_mask.select_block_lists(
                 logits[:, :tile_layout.n_video_tiles], tile_layout,
                 self.clip.blocks(tile_layout))
+            ev.stop(t)
+        t = ev.start('attention')
         o_tiles = kernels.block_sparse_attention_lists(
             q_tiles, k_tiles, v_tiles, lists, tile_layout)
+        ev.stop(t)
+        t = ev.start('unpermute')
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
+        ev.stop(t)
+        self.last_lists = lists
