@@ -135,8 +135,13 @@ class ClockSampler:
              'clocks_event_reasons.sw_thermal_slowdown,'
              'clocks_event_reasons.sw_power_cap')
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, device: torch.device):
+        # nvidia-smi ignores CUDA_VISIBLE_DEVICES: address the GPU by UUID.
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.index = uuid if uuid.startswith('GPU-') else f'GPU-{uuid}'
+        except (AttributeError, RuntimeError):
+            self.index = str(device.index)
         self.proc = None
         self.lines: list[str] = []
 
@@ -145,7 +150,7 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ['nvidia-smi', f'--id={self.index}',
                  f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
-                 '-lms', '100'], stdout=subprocess.PIPE,
+                 '-lms', '20'], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -156,7 +161,10 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def mark(self, name: str) -> None:
+        setattr(self, name, time.perf_counter())
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -168,10 +176,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        """Samples taken between mark('t0') and mark('t1') only."""
         mhz, max_mhz, reasons = [], None, set()
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
                  'sw_power_cap']
-        for line in self.lines:
+        t0 = getattr(self, 't0', 0.0)
+        t1 = getattr(self, 't1', float('inf'))
+        for stamp, line in self.lines:
+            if not t0 <= stamp <= t1:
+                continue
             parts = [p.strip() for p in line.split(',')]
             if len(parts) < 9:
                 continue
@@ -264,7 +277,7 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=30)
+    ap.add_argument('--steps', type=int, default=400)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
@@ -317,12 +330,14 @@ def main():
         stream = torch.cuda.current_stream()
         start = torch.cuda.Event(enable_timing=True)
         stop = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(device.index) as clocks:
+        with ClockSampler(device) as clocks:
             start.record(stream)
+            clocks.mark('t0')
             for _ in range(args.steps):
                 fn(q, k, v, 0)
             stop.record(stream)
             barrier()
+            clocks.mark('t1')
         student.events = veda_attention._NO_EVENTS  # pylint: disable=protected-access
         ms = start.elapsed_time(stop) / args.steps
         stages = {n: t / args.steps for n, t in events.totals_ms().items()}
@@ -346,6 +361,7 @@ def main():
         host = [t.cpu().pin_memory() for t in (q, k, v)]
         out_host = torch.empty_like(host[0]).pin_memory()
         dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+        e2e_steps = min(args.steps, 30)
         for _ in range(2):
             for d, h in zip((dq, dk, dv), host):
                 d.copy_(h, non_blocking=True)
@@ -354,13 +370,13 @@ def main():
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(e2e_steps):
             for d, h in zip((dq, dk, dv), host):
                 d.copy_(h, non_blocking=True)
             out_host.copy_(fn(dq, dk, dv, 0), non_blocking=True)
         e1.record(stream)
         barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
     vals = torch.tensor([ms, e2e_ms, stages.get('attention', 0.0),
                          float(blocks)], dtype=torch.float64, device=device)
@@ -400,7 +416,7 @@ def main():
                 'achieved': attn_tflops, 'peak': peak, 'unit': 'TFLOP/s',
                 'frac': attn_tflops / peak, 'traffic': None,
                 'peak_source': f'{peaks["source"]} bf16 burst'},
-            'e2e': {'value': e2e_ms, 'unit': 'ms/layer',
+            'e2e': {'value': e2e_ms, 'unit': 'ms/layer', 'steps': e2e_steps,
                     'h2d_bytes_per_step': 3 * q.numel() * 2,
                     'd2h_bytes_per_step': q.numel() * 2},
             'gpu_launches': args.steps * launches_per_step(plan, world),
