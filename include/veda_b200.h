@@ -123,6 +123,29 @@ int veda_predict_logits(const float* feats_q, const float* feats_k,
                         int64_t n_k, float* logits, void* workspace,
                         int64_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. veda_predict_logits without a workspace
+ * argument, for callers that cannot allocate device memory themselves: a
+ * host framework that owns the GPU's memory through its own pool (PyTorch's
+ * caching allocator can hold most of HBM, so a plain cudaMalloc fails even
+ * though the pool has room), or a plugin interface that hands a kernel only
+ * its inputs and outputs. The caller still passes inputs and outputs.
+ * Its scratch is a fixed array inside the library of
+ * VEDA_PREDICT_NOALLOC_MAX_FLOATS floats (32 MiB), which every GPU that loads
+ * the library holds until exit; calls needing more (n_heads * (n_q + n_k) *
+ * 128 floats) are rejected with VEDA_ERR_INVALID. The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress); make that
+ * first call before any stream capture. Every call shares the one array, so
+ * calls that overlap on the GPU (e.g. on two streams) race; serialise them.
+ * Nothing carries over between calls: every scratch element read is first
+ * written by the same call. Calls no cudaMalloc, cudaFree or allocating
+ * library routine. */
+#define VEDA_PREDICT_NOALLOC_MAX_FLOATS 8388608
+int veda_predict_logits_noalloc(const float* feats_q, const float* feats_k,
+                                const float* proj_q, const float* proj_k,
+                                const int64_t* heads, int32_t n_heads,
+                                int64_t n_q, int64_t n_k, float* logits,
+                                void* stream);
+
 /* ---- a5-a8: top-k selection, block mask, index lists ------------------- */
 
 /* Replaces miowtion/veda/mask.py:200-285 (select_video_blocks, rule topk),

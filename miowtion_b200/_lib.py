@@ -61,6 +61,9 @@ SIGNATURES = {
     'veda_predict_logits': (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32,
                                     c_i64, c_i64, c_ptr, c_ptr, c_i64,
                                     c_ptr]),
+    'veda_predict_logits_noalloc': (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr,
+                                            c_ptr, c_i32, c_i64, c_i64,
+                                            c_ptr, c_ptr]),
     'veda_block_select': (c_i32, [c_ptr, c_i64, c_i32, c_i64, c_ptr, c_ptr,
                                   c_i64, c_i64, ctypes.POINTER(ColumnBlockC),
                                   c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr,

@@ -6,6 +6,9 @@
 // (~4 GFLOP at the H3 shape) and must stay fp32 because the scores are only
 // used through their ranking.
 #include <math.h>
+#include <stdio.h>
+
+#include <mutex>
 
 #include "common.cuh"
 
@@ -195,4 +198,77 @@ extern "C" int veda_predict_logits(const float* feats_q, const float* feats_k,
   logits_kernel<<<g2, 256, 0, as_stream(stream)>>>(
       q_hat, k_hat, n_q, n_k, sqrtf(static_cast<float>(kHeadDim)), logits);
   return check_launch("logits_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// veda_predict_logits_noalloc: the same computation with no workspace
+// argument, for callers that cannot allocate device memory themselves.
+//
+// Its scratch (q_hat and k_hat of one call) is this fixed file-scope array,
+// which every GPU that loads the library holds until the process exits. The
+// array's name in host code is only a host-side stand-in: the device address
+// is obtained once per device with cudaGetSymbolAddress (with that device
+// current) on the first call made on it, and passed to the kernels.
+// ---------------------------------------------------------------------------
+
+namespace veda {
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = VEDA_PREDICT_NOALLOC_MAX_FLOATS;
+
+static __device__ __align__(256) float g_predict_scratch[kNoAllocScratchFloats];
+
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[64] = {};
+
+// Device address of g_predict_scratch on the current device.
+int scratch_on_current_device(float** out) {
+  int dev = 0;
+  VEDA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    return set_error(VEDA_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_predict_scratch);
+    if (err != cudaSuccess)
+      return check_cuda(err, "cudaGetSymbolAddress(g_predict_scratch)");
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return VEDA_OK;
+}
+
+}  // namespace
+}  // namespace veda
+
+extern "C" int veda_predict_logits_noalloc(
+    const float* feats_q, const float* feats_k, const float* proj_q,
+    const float* proj_k, const int64_t* heads, int32_t n_heads, int64_t n_q,
+    int64_t n_k, float* logits, void* stream) {
+  VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
+  VEDA_REQUIRE(n_q >= 0 && n_k >= 0, "bad tile counts");
+  const int64_t need = static_cast<int64_t>(n_heads) * (n_q + n_k) * kHeadDim;
+  if (need > kNoAllocScratchFloats) {
+    char buf[256];
+    snprintf(buf, sizeof(buf),
+             "veda_predict_logits_noalloc: %lld heads x (%lld + %lld) tiles "
+             "need %lld scratch floats, above its fixed %lld (32 MiB); call "
+             "it on fewer heads at a time, or use veda_predict_logits with a "
+             "workspace",
+             static_cast<long long>(n_heads), static_cast<long long>(n_q),
+             static_cast<long long>(n_k), static_cast<long long>(need),
+             static_cast<long long>(kNoAllocScratchFloats));
+    return set_error(VEDA_ERR_INVALID, buf);
+  }
+  float* scratch = nullptr;
+  const int rc = scratch_on_current_device(&scratch);
+  if (rc != VEDA_OK) return rc;
+  // The embed kernel writes every q_hat / k_hat element the logits kernel
+  // reads, so nothing left from an earlier call needs clearing.
+  return veda_predict_logits(feats_q, feats_k, proj_q, proj_k, heads, n_heads,
+                             n_q, n_k, logits, scratch,
+                             kNoAllocScratchFloats *
+                                 static_cast<int64_t>(sizeof(float)),
+                             stream);
 }
