@@ -44,7 +44,8 @@ enum Bar {
   kVFull,
   kVEmpty,
   kSFull,
-  kPFull,
+  kPFull0,  // P columns for keys 0-63 written
+  kPFull1,  // P columns for keys 64-127 written
   kODone,
   kDrain,
   kNumBars
@@ -93,6 +94,66 @@ __device__ __forceinline__ Step block_at(const FwdParams& p, int j, int pc,
   return s;
 }
 
+// Columns of each 128-key block whose exponential runs on the FMA pipes.
+constexpr int kPolyCols = 32;
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Max of 128 values as a shallow tree of three-input max instructions.
+__device__ __forceinline__ float row_max128(const float* s) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int c = 8; c < 120; c += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = max3(m[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[120 + i]);
+  return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]),
+              fmaxf(m[6], m[7]));
+}
+
+// 2^x on the FMA pipes for a pair of values: x = n + f with n = rint(x),
+// f in [-1/2, 1/2]; 2^f from the degree-3 minimax polynomial fitted by
+// csrc/fit_exp2_poly.py (max relative error 7.5e-5); 2^n added to the
+// exponent field. Arguments below -125 (masked keys) give ~0.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: rounds to integers
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 q = __ffma2_rn(f, make_float2(0x1.c3f76p-5f, 0x1.c3f76p-5f),
+                        make_float2(0x1.f0de1ap-3f, 0x1.f0de1ap-3f));
+  q = __ffma2_rn(q, f, make_float2(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+  q = __ffma2_rn(q, f, make_float2(0x1.fff692p-1f, 0x1.fff692p-1f));
+  // The integer n sits in the low mantissa bits of t; n << 23 scales by 2^n.
+  const int bx = __float_as_int(q.x) + (__float_as_int(t.x) << 23);
+  const int by = __float_as_int(q.y) + (__float_as_int(t.y) << 23);
+  return make_float2(__int_as_float(bx), __int_as_float(by));
+}
+
+// O *= alpha for this thread's row (its TMEM lane), 16 columns at a time.
+__device__ __forceinline__ void rescale_o(uint32_t t_row, float alpha) {
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    uint32_t o[16];
+    tmem_ld16(t_row + c * 16, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+    tmem_st16(t_row + c * 16, o);
+  }
+  tmem_wait_st();
+}
+
 __global__ void __launch_bounds__(kFwdThreads, 2)
     bsa_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_k,
@@ -129,7 +190,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
   if (tid == 0) {
     for (int b = 0; b < kNumBars; ++b)
-      mbar_init(&bars[b], b == kPFull ? 128 : 1);
+      mbar_init(&bars[b], (b == kPFull0 || b == kPFull1) ? 128 : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -203,13 +264,20 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         }
         umma_commit(&bars[kSFull]);
         umma_commit(&bars[kKEmpty]);
-        if (!mbar_wait(&bars[kPFull], j & 1, abort, p.status)) break;
         if (!mbar_wait(&bars[kVFull], j & 1, abort, p.status)) break;
+        // PV in two halves of 64 keys, each as soon as its P is written.
+        if (!mbar_wait(&bars[kPFull0], j & 1, abort, p.status)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = 0; kk < 4; ++kk)
           umma_ts(t_o, t_s + kk * 8, sw128_desc(a_v + kk * 2048, kHalfBytes),
                   idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(&bars[kPFull1], j & 1, abort, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 4; kk < 8; ++kk)
+          umma_ts(t_o, t_s + kk * 8, sw128_desc(a_v + kk * 2048, kHalfBytes),
+                  idesc_pv, 1u);
         umma_commit(&bars[kODone]);
         umma_commit(&bars[kVEmpty]);
       }
@@ -226,8 +294,12 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     float m_ref = -INFINITY;  // running max, already in log2 units
     float l = 0.f;
     bool ok = true;
+    // The list entry of the next step is loaded one step ahead so its
+    // global-memory latency overlaps the current step.
+    Step next = n_steps > 0 ? block_at(p, 0, pc, fc, list_off) : Step{0, 0};
     for (int j = 0; j < n_steps; ++j) {
-      const Step st = block_at(p, j, pc, fc, list_off);
+      const Step st = next;
+      if (j + 1 < n_steps) next = block_at(p, j + 1, pc, fc, list_off);
       // Waits and breaks stay warp-uniform: tcgen05.ld/st are warp-wide.
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&bars[kSFull], j & 1, abort, p.status))) {
@@ -247,55 +319,92 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         for (int c = 0; c < 128; ++c)
           if (c >= st.valid) s[c] = -INFINITY;
       }
-      float mb = s[0];
-#pragma unroll
-      for (int c = 1; c < 128; ++c) mb = fmaxf(mb, s[c]);
-      mb *= p.scale_log2;
+      const float mb = row_max128(s) * p.scale_log2;
+      // Lazy rescaling: the reference max moves only when a row's max grows
+      // by more than 2^8, so P <= 256 and O is rarely touched.
+      bool rescale = false;
+      float alpha = 1.0f;
       if (j == 0) {
         m_ref = mb;
       } else {
         const bool grow = mb > m_ref + 8.0f;
-        if (__any_sync(0xffffffffu, grow)) {
-          // O holds steps < j; wait for PV(j-1) before rescaling it.
-          if (!__all_sync(0xffffffffu, mbar_wait(&bars[kODone], (j - 1) & 1,
-                                                 abort, p.status))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+        rescale = __any_sync(0xffffffffu, grow);
+        if (rescale) {
           const float m_new = grow ? mb : m_ref;
-          const float alpha = ex2_approx(m_ref - m_new);
-#pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            uint32_t o[16];
-            tmem_ld16(t_o + lane_base + c * 16, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(t_o + lane_base + c * 16, o);
-          }
-          tmem_wait_st();
-          l *= alpha;
+          alpha = ex2_approx(m_ref - m_new);
           m_ref = m_new;
         }
       }
-      const float neg_m = -m_ref;
-      float rs = 0.f;
+      const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 neg_m2 = make_float2(-m_ref, -m_ref);
+      float2 sum_a = make_float2(0.f, 0.f), sum_b = make_float2(0.f, 0.f);
+      // Keys 0-63: exponentials on the MUFU.
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float e = ex2_approx(fmaf(s[c], p.scale_log2, neg_m));
-        s[c] = e;
-        rs += e;
+      for (int c = 0; c < 64; c += 4) {
+        const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2,
+                                     neg_m2);
+        const float2 x1 = __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2,
+                                     neg_m2);
+        const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+        const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+        sum_a = __fadd2_rn(sum_a, e0);
+        sum_b = __fadd2_rn(sum_b, e1);
+        r[c / 2] = pack_bf16(e0.x, e0.y);
+        r[c / 2 + 1] = pack_bf16(e1.x, e1.y);
       }
-      l += rs;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) r[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
+      if (rescale) {
+        // O holds steps < j: wait for PV(j-1), then scale it (PV(j) cannot
+        // start before this thread arrives on kPFull0 below).
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[kODone], (j - 1) & 1,
+                                               abort, p.status))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o(t_o + lane_base, alpha);
+        l *= alpha;
+      }
       tmem_st32(t_s + lane_base + 0, r);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[kPFull0]);
+      // Keys 64-127: P never overwrites S columns 64-127, so they are read
+      // again from TMEM instead of staying live in registers since the max.
+      tmem_ld32(t_s + lane_base + 64, r + 64);
+      tmem_ld32(t_s + lane_base + 96, r + 96);
+      tmem_wait_ld();
+      if (st.valid < kTile) {
+#pragma unroll
+        for (int c = 64; c < 128; ++c)
+          if (c >= st.valid) s[c] = -INFINITY;
+      }
+      // The first 32 on the MUFU, the last kPolyCols on the FMA pipes
+      // (exp2_poly2), which balances the two units.
+#pragma unroll
+      for (int c = 64; c < 128; c += 4) {
+        const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2,
+                                     neg_m2);
+        const float2 x1 = __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2,
+                                     neg_m2);
+        float2 e0, e1;
+        if (c >= 128 - kPolyCols) {
+          e0 = exp2_poly2(x0);
+          e1 = exp2_poly2(x1);
+        } else {
+          e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+          e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+        }
+        sum_a = __fadd2_rn(sum_a, e0);
+        sum_b = __fadd2_rn(sum_b, e1);
+        r[c / 2] = pack_bf16(e0.x, e0.y);
+        r[c / 2 + 1] = pack_bf16(e1.x, e1.y);
+      }
       tmem_st32(t_s + lane_base + 32, r + 32);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars[kPFull]);
+      mbar_arrive(&bars[kPFull1]);
+      const float2 sum2 = __fadd2_rn(sum_a, sum_b);
+      l += sum2.x + sum2.y;
     }
     // ---------------- epilogue ----------------
     if (ok && n_steps > 0)

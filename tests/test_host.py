@@ -107,3 +107,27 @@ def test_plan_groups_and_json(tmp_path):
     assert again.to_json() == plan.to_json()
     assert json.loads(path.read_text())['shapes'] == ['4x8x4', '8x8x2',
                                                       '2x8x8']
+
+
+def test_fma_exp2_polynomial_error_bound():
+    """The cubic the attention kernel evaluates on the FMA pipes (the
+    exp2_poly2 helper of csrc/bsa_fwd.cu) stays within 1e-4 relative error of
+    2^x over the softmax's argument range, emulated in float32 exactly as the
+    kernel computes it."""
+    import os
+    import re
+    import sys
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    csrc = os.path.join(here, 'miowtion_b200', 'csrc')
+    sys.path.insert(0, csrc)
+    import fit_exp2_poly
+    src = open(os.path.join(csrc, 'bsa_fwd.cu')).read()
+    body = src[src.index('float2 exp2_poly2'):]
+    lits = re.findall(r'(0x1\.[0-9a-f]+p-?\d+)f', body)[:8:2]
+    c3, c2, c1, c0 = (float.fromhex(x) for x in lits)
+    coef = np.array([c0, c1, c2, c3])
+    np.testing.assert_allclose(coef, fit_exp2_poly.remez(), rtol=1e-6)
+    x = np.linspace(-124.0, 8.0, 1 << 21).astype(np.float32)
+    got = fit_exp2_poly.exp2_emulated(x, coef).astype(np.float64)
+    rel = np.abs(got / np.exp2(x.astype(np.float64)) - 1.0)
+    assert rel.max() < 1e-4
