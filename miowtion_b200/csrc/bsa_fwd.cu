@@ -3,26 +3,43 @@
 // Semantics (miowtion/kernels/reference.py:1-10, :23-56): a query row of tile
 // i attends to the valid prefix of every key tile listed for i; rows with no
 // key output 0 (lse -inf). Lists are the reference's BlockSparseTensors
-// (miowtion/kernels/fa4.py:266-296); the walk order is the SM100 one of the
-// reference backend, partial list then full list, each from its end
-// (fa4_sm8x/block_sparse_utils.py:813-853), which only affects the fp32
+// (miowtion/kernels/fa4.py:266-296); each list is walked in the reference
+// backend's SM100 order, partial list then full list, each from its end
+// (fa4_sm8x/block_sparse_utils.py:813-853); the order only changes the fp32
 // summation order.
 //
-// One CTA per (head, query tile), two CTAs per SM, 6 warps:
-//   warps 0-3  softmax + epilogue; thread t owns query row t (TMEM lane t)
-//   warp 4     TMA producer: Q once, then K and V of each listed key tile
-//   warp 5     TMEM allocator and the single-thread tcgen05.mma issuer
-// Per listed key tile j:
-//   S = Q K^T          tcgen05.mma, A/B K-major from 128B-swizzled smem,
-//                      fp32 accumulator in TMEM columns [0, 128)
-//   P = exp2(S*c - m)  softmax warps: tcgen05.ld S, mask the key tile's
-//                      padding suffix, online max with lazy rescaling (only
-//                      when the running max grows by more than 2^8), write
-//                      P as bf16 pairs back over S (columns [0, 64))
-//   O += P V           tcgen05.mma with A = P from TMEM, B = V MN-major from
-//                      smem, accumulator in TMEM columns [128, 256)
-// The two co-resident CTAs interleave: one CTA's exponentials overlap the
-// other's MMAs. All mbarrier waits are bounded (common.cuh).
+// Structure: a persistent kernel, one CTA per SM, walking work items (head,
+// query tile) with a stride of the grid. One query tile is in flight at a
+// time; the blocks of consecutive items form one sequence (b = 0, 1, ...),
+// and tensor memory holds three S buffers (block b uses S[b % 3]) and O:
+//     TMEM columns [  0,128) S0   [128,256) S1   [256,384) S2   [384,512) O
+// so the tensor core computes S(b+1) and S(b+2) while the softmax works on
+// S(b), and the softmax never waits for a QK.
+//   warps 0-15 softmax and epilogue. Warp w serves query rows 32(w%4) ..
+//              32(w%4)+31 (its TMEM lanes) and keys 32(w/4) .. 32(w/4)+31 of
+//              every block; the four warps of a row range exchange partial
+//              row maxima through shared memory (named barrier). Each warp
+//              writes its P (bf16 pairs) over the first 16 columns of its
+//              own 32 columns of S. Four warps per SMSP hide one another's
+//              latencies.
+//   warp 16    TMA producer: Q of each item (two buffers), and K(b), V(b-2)
+//              through a 4-slot ring in the MMA warp's order, each K with a
+//              record of its block for the MMA warp.
+//   warp 17    TMEM owner and tcgen05.mma issuer (converged warp, elected
+//              lane issues): QK(0), QK(1), then QK(b), PV(b-2) for b >= 2.
+// Tensor-core instructions of one warp execute in issue order: QK(b+3) may
+// overwrite S while nothing waits for PV(b) (issued earlier, it has read P
+// first). Each block runs
+//     S = Q K^T          8 SS MMAs (M=N=128, K=16), 128B-swizzled K-major
+//     P = exp2(S*c - m)  online softmax, lazy rescaling (the max moves only
+//                        when it grows by more than 2^8), a quarter of the
+//                        exponentials on an FMA polynomial
+//     O += P V           8 TS MMAs (A = P from TMEM, B = V MN-major), the
+//                        first four once keys 0-63 have P, the others once
+//                        keys 64-127 have.
+// The softmax learns a block's valid key count two blocks ahead (partial
+// tiles only; full ones have 128) so that no list read stalls it.
+// All mbarrier waits are bounded (common.cuh).
 #include <math.h>
 
 #include "common.cuh"
@@ -31,30 +48,51 @@ namespace veda {
 
 namespace {
 
-constexpr int kFwdThreads = 192;
+constexpr int kSoftmaxWarps = 16;
+constexpr int kProducerWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
+constexpr int kFwdThreads = 32 * (kSoftmaxWarps + 2);
+constexpr int kRing = 4;
 constexpr uint32_t kTileBytes = 32768;  // 128 x 128 bf16
 constexpr uint32_t kHalfBytes = 16384;  // 128 x 64 bf16 (one TMA box)
-constexpr uint32_t kTmemCols = 256;
-constexpr int kSmemBytes = 3 * kTileBytes + 256 + 1024;
+constexpr uint32_t kTmemCols = 512;
+// The key tiles of the producer's current item in walk order (longer lists
+// are read from global memory).
+constexpr int kListCap = 1024;
+// Exchange between the four warps of a row: partial maxima [block parity][4
+// key quarters][128 rows] and partial sums [4 key quarters][128 rows].
+constexpr int kExchangeFloats = 2 * 4 * 128 + 4 * 128;
+constexpr int kSmemBytes = (2 + kRing) * kTileBytes + kListCap * 4 +
+                           kExchangeFloats * 4 + 512 + 1024;
+
+// Of each warp's 32 columns, those whose exponential runs on the FMA pipes.
+// A quarter balances the MUFU (ex2 at 16 a clock per SM) against the FMA
+// pipes: measured on B200 with four such warps per SMSP, 8 of 32 columns
+// gives the shortest P computation (0, 16 and 32 are slower).
+constexpr int kPolyCols = 8;
+
+constexpr int kSBufs = 3;
 
 enum Bar {
-  kQFull = 0,
-  kKFull,
-  kKEmpty,
-  kVFull,
-  kVEmpty,
-  kSFull,
-  kPFull0,  // P columns for keys 0-63 written
-  kPFull1,  // P columns for keys 64-127 written
-  kODone,
-  kDrain,
-  kNumBars
+  kQFull = 0,       // [2] per Q buffer (item parity)
+  kQEmpty = 2,      // [2] the item's last QK finished reading Q
+  kRingFull = 4,    // [kRing]
+  kRingEmpty = 8,   // [kRing]
+  kSFull = 12,      // [3] per S buffer
+  kPFull0 = 15,     // [3] P of keys 0-63 written (warps 0-7)
+  kPFull1 = 18,     // [3] P of keys 64-127 written (warps 8-15)
+  kPVDone = 21,     // [3] the block's PV finished (per S buffer)
+  kODone = 24,      // the item's last PV finished
+  kOFree = 25,      // the epilogue has read O (16 warps)
+  kDrain = 26,      // MMAs in flight after an abort
+  kNumBars = 27
 };
 
 struct FwdParams {
   int n_heads;
   int n_q_tiles;
   int n_kv_tiles;
+  int n_items;
   const int32_t* valid_count;
   const int32_t* part_cnt;
   const int32_t* part_idx;
@@ -71,31 +109,118 @@ struct FwdParams {
   unsigned int* status;
 };
 
-// Key tile of step j and the number of valid keys in it (128 when full).
-struct Step {
-  int kv;
-  int valid;
+// One key block of a slot's stream.
+struct Block {
+  int h, qt;   // work item
+  int kv;      // key tile
+  int valid;   // valid key rows of the tile (128 when full)
+  int blk;     // running block number of the slot (barrier phases)
+  int ka;      // running number of non-empty items of the slot
+  bool first, last;
 };
 
-__device__ __forceinline__ Step block_at(const FwdParams& p, int j, int pc,
-                                         int fc, int64_t list_off) {
-  Step s;
-  if (p.dense) {
-    s.kv = j;
-    const int64_t rest = p.used - static_cast<int64_t>(j) * kTile;
-    s.valid = rest < kTile ? static_cast<int>(rest) : kTile;
-  } else if (j < pc) {
-    s.kv = p.part_idx[list_off + (pc - 1 - j)];
-    s.valid = p.valid_count[s.kv];
-  } else {
-    s.kv = p.full_idx[list_off + (fc - 1 - (j - pc))];
-    s.valid = kTile;
-  }
-  return s;
-}
+// The work items of one slot, item by item and block by block. Every role
+// walks the same sequence, so they agree on barrier phases without talking.
+struct Stream {
+  int it, stride;
+  int h, qt, pc, fc, len;
+  int64_t off;
+  int j, blk, ka;
+  // List lengths of item it + stride, loaded one item ahead so that their
+  // latency overlaps the current item.
+  int npc, nfc;
 
-// Columns of each 128-key block whose exponential runs on the FMA pipes.
-constexpr int kPolyCols = 32;
+  __device__ void fetch(const FwdParams& p, int item) {
+    npc = 0;
+    nfc = 0;
+    if (item >= p.n_items) return;
+    if (p.dense) {
+      nfc = p.n_kv_tiles;
+      return;
+    }
+    const int64_t row = static_cast<int64_t>(item / p.n_q_tiles) *
+                            p.n_q_tiles +
+                        (p.n_q_tiles - 1 - item % p.n_q_tiles);
+    npc = p.part_cnt[row];
+    nfc = p.full_cnt[row];
+  }
+
+  __device__ void load_item(const FwdParams& p) {
+    h = it / p.n_q_tiles;
+    // Heaviest query tiles (the dense global rows, last in tile order) first.
+    qt = p.n_q_tiles - 1 - it % p.n_q_tiles;
+    off = p.dense ? 0
+                  : (static_cast<int64_t>(h) * p.n_q_tiles + qt) * p.ld_idx;
+    pc = npc;
+    fc = nfc;
+    len = pc + fc;
+    j = 0;
+    fetch(p, it + stride);
+  }
+
+  // Positions on the first item (on the first non-empty one unless
+  // `keep_empty`, which the softmax uses to write the empty items' rows).
+  __device__ void init(const FwdParams& p, int first, int step,
+                       bool keep_empty) {
+    it = first;
+    stride = step;
+    blk = 0;
+    ka = -1;
+    if (it < p.n_items) {
+      fetch(p, it);
+      load_item(p);
+      if (len > 0) ka = 0;
+      if (!keep_empty) skip_empty(p);
+    }
+  }
+
+  __device__ void skip_empty(const FwdParams& p) {
+    while (it < p.n_items && len == 0) {
+      it += stride;
+      if (it < p.n_items) {
+        load_item(p);
+        if (len > 0) ++ka;
+      }
+    }
+  }
+
+  __device__ void next_item(const FwdParams& p, bool keep_empty) {
+    it += stride;
+    if (it < p.n_items) {
+      load_item(p);
+      if (len > 0) ++ka;
+      if (!keep_empty) skip_empty(p);
+    }
+  }
+
+  __device__ bool valid(const FwdParams& p) const { return it < p.n_items; }
+
+  // The current block without its key tile (no memory access).
+  __device__ Block flags() const {
+    Block b{};
+    b.h = h;
+    b.qt = qt;
+    b.blk = blk;
+    b.ka = ka;
+    b.first = j == 0;
+    b.last = j == len - 1;
+    return b;
+  }
+
+  // Key tile of block jj of the current item, read from global memory.
+  __device__ int kv_global(const FwdParams& p, int jj) const {
+    if (p.dense) return jj;
+    return jj < pc ? p.part_idx[off + (pc - 1 - jj)]
+                   : p.full_idx[off + (fc - 1 - (jj - pc))];
+  }
+
+  // Next block; at the end of an item, the next (non-empty) item.
+  __device__ void next_block(const FwdParams& p) {
+    ++blk;
+    if (++j < len) return;
+    next_item(p, false);
+  }
+};
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -103,17 +228,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// Max of 128 values as a shallow tree of three-input max instructions.
-__device__ __forceinline__ float row_max128(const float* s) {
+// Max of 32 values as a shallow tree of three-input max instructions.
+__device__ __forceinline__ float row_max32(const float* s) {
   float m[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = s[i];
+  for (int i = 0; i < 8; ++i) m[i] = max3(s[i], s[8 + i], s[16 + i]);
 #pragma unroll
-  for (int c = 8; c < 120; c += 16)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = max3(m[i], s[c + i], s[c + 8 + i]);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[120 + i]);
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[24 + i]);
   return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]),
               fmaxf(m[6], m[7]));
 }
@@ -139,62 +260,126 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   return make_float2(__int_as_float(bx), __int_as_float(by));
 }
 
-// O *= alpha for this thread's row (its TMEM lane), 16 columns at a time.
-__device__ __forceinline__ void rescale_o(uint32_t t_row, float alpha) {
-#pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    uint32_t o[16];
-    tmem_ld16(t_row + c * 16, o);
-    tmem_wait_ld();
+// O *= alpha for 32 columns of this thread's row (its TMEM lane).
+__device__ __forceinline__ void rescale_o32(uint32_t t_row, float alpha) {
+  uint32_t o[32];
+  tmem_ld32(t_row, o);
+  tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-    tmem_st16(t_row + c * 16, o);
-  }
+  for (int i = 0; i < 32; ++i)
+    o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+  tmem_st32(t_row, o);
   tmem_wait_st();
 }
 
-__global__ void __launch_bounds__(kFwdThreads, 2)
+// P for this warp's 32 keys: x = s*c - m, exp2 on the MUFU (or, for the last
+// kPolyCols columns, on the FMA pipes), bf16 pairs into r[c/2]. Returns the
+// (fp32) sum of the exponentials.
+__device__ __forceinline__ float2 p32(uint32_t* r, const float* s,
+                                      float2 scale2, float2 neg_m2) {
+  float2 sum_a = make_float2(0.f, 0.f), sum_b = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 32; c += 4) {
+    const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2, neg_m2);
+    const float2 x1 =
+        __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2, neg_m2);
+    float2 e0, e1;
+    if (c >= 32 - kPolyCols) {
+      e0 = exp2_poly2(x0);
+      e1 = exp2_poly2(x1);
+    } else {
+      e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+      e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+    }
+    sum_a = __fadd2_rn(sum_a, e0);
+    sum_b = __fadd2_rn(sum_b, e1);
+    r[c / 2] = pack_bf16(e0.x, e0.y);
+    r[c / 2 + 1] = pack_bf16(e1.x, e1.y);
+  }
+  return __fadd2_rn(sum_a, sum_b);
+}
+
+// Named barrier for the four warps of a row range (128 threads; ids 1-4, 0
+// is __syncthreads).
+__device__ __forceinline__ void row_sync(int id) {
+  asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+}
+
+// Warp-uniform wait: tcgen05.ld/st after it are warp-wide instructions.
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity,
+                                         volatile int* abort,
+                                         unsigned int* status) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, status));
+}
+
+// The record of a block, written by the producer before the block's K copy
+// and published by that ring slot's full barrier, so the MMA warp needs no
+// walk of the work stream. With ka the item's number among the CTA's
+// non-empty items: bit 0 end of the stream, bit 1 first block of the item,
+// bit 2 last block, bit 3 ka & 1 (its Q buffer, and the parity of the O
+// barriers' phase), bit 4 (ka >> 1) & 1 (the parity of the Q buffer's
+// phase), bit 5 ka >= 1 (O held an earlier item).
+constexpr uint32_t kRecEnd = 1, kRecFirst = 2, kRecLast = 4, kRecItem = 8,
+                   kRecQPhase = 16, kRecLater = 32;
+
+__device__ __forceinline__ uint32_t block_record(const Block& b) {
+  return (b.first ? kRecFirst : 0u) | (b.last ? kRecLast : 0u) |
+         ((b.ka & 1) ? kRecItem : 0u) | (((b.ka >> 1) & 1) ? kRecQPhase : 0u) |
+         (b.ka >= 1 ? kRecLater : 0u);
+}
+
+// Waits for two phases: one probe of both (non-blocking test_wait, the two
+// tests independent so their latencies overlap), bounded waits if either is
+// still open.
+__device__ __forceinline__ bool wait_both(uint64_t* a, uint32_t pa, uint64_t* b,
+                                          uint32_t pb, volatile int* abort,
+                                          unsigned int* status) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred x, y; "
+      "mbarrier.test_wait.parity.shared::cta.b64 x, [%1], %2; "
+      "mbarrier.test_wait.parity.shared::cta.b64 y, [%3], %4; "
+      "and.pred x, x, y; selp.u32 %0, 1, 0, x; }"
+      : "=r"(ok)
+      : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb)
+      : "memory");
+  if (__all_sync(0xffffffffu, ok != 0)) return true;
+  return wait_all(a, pa, abort, status) && wait_all(b, pb, abort, status);
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_k,
                    const __grid_constant__ CUtensorMap map_v, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* s_q = smem;
-  uint8_t* s_k = smem + kTileBytes;
-  uint8_t* s_v = smem + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * kTileBytes);
+  uint8_t* s_q = smem;                      // [2] x 32 KB (item parity)
+  uint8_t* s_ring = smem + 2 * kTileBytes;  // [kRing] x 32 KB
+  int32_t* s_list =
+      reinterpret_cast<int32_t*>(smem + (2 + kRing) * kTileBytes);
+  float* s_xchg = reinterpret_cast<float*>(s_list + kListCap);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_xchg + kExchangeFloats);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  static_assert(kNumBars + 1 <= 32, "barriers overlap the block records");
+  volatile uint32_t* s_rec = reinterpret_cast<volatile uint32_t*>(bars + 32);
 
   const int tid = threadIdx.x;
   const int warp = tid / 32;
   const int lane = tid % 32;
-  const int bid = blockIdx.x;
-  const int h = bid / p.n_q_tiles;
-  // Heaviest query tiles (the dense global rows, last in tile order) first.
-  const int qt = p.n_q_tiles - 1 - bid % p.n_q_tiles;
-
-  int pc = 0, fc = 0;
-  int64_t list_off = 0;
-  if (p.dense) {
-    fc = p.n_kv_tiles;
-  } else {
-    const int64_t row = static_cast<int64_t>(h) * p.n_q_tiles + qt;
-    pc = p.part_cnt[row];
-    fc = p.full_cnt[row];
-    list_off = row * p.ld_idx;
-  }
-  const int n_steps = pc + fc;
 
   if (tid == 0) {
-    for (int b = 0; b < kNumBars; ++b)
-      mbar_init(&bars[b], (b == kPFull0 || b == kPFull1) ? 128 : 1);
+    for (int b = 0; b < kNumBars; ++b) {
+      uint32_t count = 1;
+      if (b >= kPFull0 && b < kPFull1 + kSBufs) count = kSoftmaxWarps / 2;
+      if (b == kOFree) count = kSoftmaxWarps;
+      mbar_init(&bars[b], count);
+    }
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -202,255 +387,386 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem;        // S / P
-  const uint32_t t_o = tmem + 128;  // O
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0 && n_steps > 0) {
+  if (warp == kProducerWarp) {
+    // ---------------- TMA producer (one warp) ----------------
+    // Loads in the MMA warp's order: K(0), K(1), then K(b), V(b-2) for
+    // b >= 2, then the end record and V of the last two blocks; Q of an item
+    // before its first K. The whole warp walks the stream (it copies each item's list
+    // to shared memory) and waits converged; lane 0 issues the copies.
+    if (lane == 0) {
       prefetch_tensor_map(&map_q);
       prefetch_tensor_map(&map_k);
       prefetch_tensor_map(&map_v);
-      const int q_row = qt * kTile;
-      mbar_arrive_expect_tx(&bars[kQFull], kTileBytes);
-      tma_load_3d(s_q, &map_q, &bars[kQFull], 0, h, q_row);
-      tma_load_3d(s_q + kHalfBytes, &map_q, &bars[kQFull], 64, h, q_row);
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_steps; ++j) {
-        const int kv_row = block_at(p, j, pc, fc, list_off).kv * kTile;
-        if (j > 0 && !mbar_wait(&bars[kKEmpty], (j - 1) & 1, abort, p.status))
-          break;
-        mbar_arrive_expect_tx(&bars[kKFull], kTileBytes);
-        tma_load_3d(s_k, &map_k, &bars[kKFull], 0, h, kv_row);
-        tma_load_3d(s_k + kHalfBytes, &map_k, &bars[kKFull], 64, h, kv_row);
-        ++k_issued;
-        if (j > 0 && !mbar_wait(&bars[kVEmpty], (j - 1) & 1, abort, p.status))
-          break;
-        mbar_arrive_expect_tx(&bars[kVFull], kTileBytes);
-        tma_load_3d(s_v, &map_v, &bars[kVFull], 0, h, kv_row);
-        tma_load_3d(s_v + kHalfBytes, &map_v, &bars[kVFull], 64, h, kv_row);
-        ++v_issued;
-      }
-      if (*abort) {
-        // Let the copies already in flight land before the CTA retires: at
-        // most one per buffer is outstanding, the last one issued.
-        volatile int never = 0;
-        mbar_wait(&bars[kQFull], 0, &never, nullptr);
-        if (k_issued > 0)
-          mbar_wait(&bars[kKFull], (k_issued - 1) & 1, &never, nullptr);
-        if (v_issued > 0)
-          mbar_wait(&bars[kVFull], (v_issued - 1) & 1, &never, nullptr);
-      }
     }
-  } else if (warp == 5) {
-    // ---------------- tcgen05.mma issuer ----------------
-    if (lane == 0 && n_steps > 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16(128, 128, false, false);
-      constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
-      const uint32_t a_q = smem_u32(s_q);
-      const uint32_t a_k = smem_u32(s_k);
-      const uint32_t a_v = smem_u32(s_v);
-      bool ok = mbar_wait(&bars[kQFull], 0, abort, p.status);
-      for (int j = 0; ok && j < n_steps; ++j) {
-        if (!mbar_wait(&bars[kKFull], j & 1, abort, p.status)) break;
-        if (j > 0 && !mbar_wait(&bars[kODone], (j - 1) & 1, abort, p.status))
+    Stream st;
+    st.init(p, blockIdx.x, gridDim.x, false);
+    int pos = 0;       // ring positions used
+    int q_issued = 0;  // items whose Q was loaded
+    // Key tile and head of blocks b - 1 and b - 2.
+    int kv1 = 0, h1 = 0, kv2 = 0, h2 = 0;
+    int n_blocks = 0;
+    bool run = true;
+    // Waits until the ring slot of `pos` is free; -1 on abort.
+    auto ring_slot = [&]() -> int {
+      const int slot = pos % kRing;
+      if (pos >= kRing &&
+          !wait_all(&bars[kRingEmpty + slot], ((pos / kRing) - 1) & 1, abort,
+                    p.status))
+        return -1;
+      return slot;
+    };
+    auto load_tile = [&](const CUtensorMap* map, int slot, int h, int kv) {
+      uint8_t* dst = s_ring + slot * kTileBytes;
+      mbar_arrive_expect_tx(&bars[kRingFull + slot], kTileBytes);
+      tma_load_3d(dst, map, &bars[kRingFull + slot], 0, h, kv * kTile);
+      tma_load_3d(dst + kHalfBytes, map, &bars[kRingFull + slot], 64, h,
+                  kv * kTile);
+    };
+    while (st.valid(p)) {
+      const Block b = st.flags();
+      if (b.first) {
+        if (!p.dense && st.len <= kListCap)
+          for (int jj = lane; jj < st.len; jj += 32)
+            s_list[jj] = st.kv_global(p, jj);
+        __syncwarp();
+        // The Q buffer frees after the last QK of the item two back.
+        const int qb = b.ka & 1;
+        if (b.ka >= 2 && !wait_all(&bars[kQEmpty + qb],
+                                   ((b.ka >> 1) & 1) ^ 1, abort, p.status)) {
+          run = false;
           break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_ss(t_s, sw128_desc(a_q + off, 16), sw128_desc(a_k + off, 16),
-                  idesc_qk, kk > 0);
         }
-        umma_commit(&bars[kSFull]);
-        umma_commit(&bars[kKEmpty]);
-        if (!mbar_wait(&bars[kVFull], j & 1, abort, p.status)) break;
-        // PV in two halves of 64 keys, each as soon as its P is written.
-        if (!mbar_wait(&bars[kPFull0], j & 1, abort, p.status)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_ts(t_o, t_s + kk * 8, sw128_desc(a_v + kk * 2048, kHalfBytes),
-                  idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        if (!mbar_wait(&bars[kPFull1], j & 1, abort, p.status)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 4; kk < 8; ++kk)
-          umma_ts(t_o, t_s + kk * 8, sw128_desc(a_v + kk * 2048, kHalfBytes),
-                  idesc_pv, 1u);
-        umma_commit(&bars[kODone]);
-        umma_commit(&bars[kVEmpty]);
+        if (lane == 0) {
+          uint8_t* dst = s_q + qb * kTileBytes;
+          mbar_arrive_expect_tx(&bars[kQFull + qb], kTileBytes);
+          tma_load_3d(dst, &map_q, &bars[kQFull + qb], 0, b.h, b.qt * kTile);
+          tma_load_3d(dst + kHalfBytes, &map_q, &bars[kQFull + qb], 64, b.h,
+                      b.qt * kTile);
+        }
+        __syncwarp();
+        q_issued = b.ka + 1;
       }
-      if (*abort) {
-        volatile int never = 0;
-        umma_commit(&bars[kDrain]);
-        mbar_wait(&bars[kDrain], 0, &never, nullptr);
-      }
-    }
-  } else {
-    // ---------------- softmax + epilogue (warps 0-3) ----------------
-    const int row = tid;  // TMEM lane and query row within the tile
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    float m_ref = -INFINITY;  // running max, already in log2 units
-    float l = 0.f;
-    bool ok = true;
-    // The list entry of the next step is loaded one step ahead so its
-    // global-memory latency overlaps the current step.
-    Step next = n_steps > 0 ? block_at(p, 0, pc, fc, list_off) : Step{0, 0};
-    for (int j = 0; j < n_steps; ++j) {
-      const Step st = next;
-      if (j + 1 < n_steps) next = block_at(p, j + 1, pc, fc, list_off);
-      // Waits and breaks stay warp-uniform: tcgen05.ld/st are warp-wide.
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(&bars[kSFull], j & 1, abort, p.status))) {
-        ok = false;
+      const int kv = p.dense ? st.j
+                             : (st.len <= kListCap ? s_list[st.j]
+                                                   : st.kv_global(p, st.j));
+      int slot = ring_slot();
+      if (slot < 0) {
+        run = false;
         break;
       }
-      tc_fence_after();
-      uint32_t r[128];
-      tmem_ld32(t_s + lane_base + 0, r);
-      tmem_ld32(t_s + lane_base + 32, r + 32);
-      tmem_ld32(t_s + lane_base + 64, r + 64);
-      tmem_ld32(t_s + lane_base + 96, r + 96);
-      tmem_wait_ld();
-      float* s = reinterpret_cast<float*>(r);
-      if (st.valid < kTile) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= st.valid) s[c] = -INFINITY;
+      if (lane == 0) {
+        s_rec[slot] = block_record(b);
+        load_tile(&map_k, slot, b.h, kv);
       }
-      const float mb = row_max128(s) * p.scale_log2;
-      // Lazy rescaling: the reference max moves only when a row's max grows
-      // by more than 2^8, so P <= 256 and O is rarely touched.
-      bool rescale = false;
-      float alpha = 1.0f;
-      if (j == 0) {
-        m_ref = mb;
-      } else {
-        const bool grow = mb > m_ref + 8.0f;
-        rescale = __any_sync(0xffffffffu, grow);
-        if (rescale) {
-          const float m_new = grow ? mb : m_ref;
-          alpha = ex2_approx(m_ref - m_new);
-          m_ref = m_new;
+      __syncwarp();
+      ++pos;
+      if (n_blocks >= 2) {
+        slot = ring_slot();
+        if (slot < 0) {
+          run = false;
+          break;
+        }
+        if (lane == 0) load_tile(&map_v, slot, h2, kv2);
+        __syncwarp();
+        ++pos;
+      }
+      kv2 = kv1;
+      h2 = h1;
+      kv1 = kv;
+      h1 = b.h;
+      ++n_blocks;
+      st.next_block(p);
+    }
+    if (run) {
+      // The end record completes its slot's full barrier without a copy.
+      int slot = ring_slot();
+      if (slot >= 0) {
+        if (lane == 0) {
+          s_rec[slot] = kRecEnd;
+          mbar_arrive(&bars[kRingFull + slot]);
+        }
+        __syncwarp();
+        ++pos;
+        for (int k = n_blocks >= 2 ? 2 : n_blocks; k >= 1 && slot >= 0; --k) {
+          slot = ring_slot();
+          if (slot >= 0) {
+            if (lane == 0)
+              load_tile(&map_v, slot, k == 2 ? h2 : h1, k == 2 ? kv2 : kv1);
+            __syncwarp();
+            ++pos;
+          }
         }
       }
-      const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
-      const float2 neg_m2 = make_float2(-m_ref, -m_ref);
-      float2 sum_a = make_float2(0.f, 0.f), sum_b = make_float2(0.f, 0.f);
-      // Keys 0-63: exponentials on the MUFU.
+    }
+    if (lane == 0 && *abort) {
+      // Let the copies already in flight land before the CTA retires.
+      volatile int never = 0;
+      for (int ka = q_issued - 2; ka < q_issued; ++ka)
+        if (ka >= 0)
+          mbar_wait(&bars[kQFull + (ka & 1)], (ka >> 1) & 1, &never, nullptr);
+      for (int k = pos - kRing; k < pos; ++k)
+        if (k >= 0)
+          mbar_wait(&bars[kRingFull + k % kRing], (k / kRing) & 1, &never,
+                    nullptr);
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- tcgen05.mma issuer ----------------
+    constexpr uint32_t idesc_qk = idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
+    // Descriptor low halves; per step only a constant is added (16-byte
+    // units): K-major steps advance 32 B inside a 128-B swizzle row and
+    // jump to the second 64-column box after four steps; V steps advance
+    // 16 key rows (2 KB).
+    const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
+    const uint32_t k_lo = sw128_desc_lo(smem_u32(s_ring), 16);
+    const uint32_t v_lo = sw128_desc_lo(smem_u32(s_ring), kHalfBytes);
+    constexpr uint32_t kTileUnits = kTileBytes >> 4;
+    const uint32_t t_o = tmem + kSBufs * 128;
+    int pos = 0;       // ring positions consumed
+    uint32_t blk = 0;  // blocks whose QK was issued
+    uint32_t r1 = 0, r2 = 0;  // records of blocks blk - 1 and blk - 2
+    // PV(b) with its block's record: V in the next ring slot, P in
+    // S[b % 3].
+    auto issue_pv = [&](uint32_t b, uint32_t rec) -> bool {
+      const uint32_t sb = b % kSBufs;
+      const uint32_t spar = (b / kSBufs) & 1;
+      const bool first = rec & kRecFirst;
+      const int vslot = pos % kRing;
+      // The item's first PV overwrites O: the epilogue must have read the
+      // previous item's.
+      if (first && (rec & kRecLater) &&
+          !wait_all(&bars[kOFree], (rec & kRecItem) ? 0u : 1u, abort,
+                    p.status))
+        return false;
+      if (!wait_both(&bars[kRingFull + vslot], (pos / kRing) & 1,
+                     &bars[kPFull0 + sb], spar, abort, p.status))
+        return false;
+      tc_fence_after();
+      const uint32_t bv = v_lo + vslot * kTileUnits;
+      const uint32_t t_p = tmem + sb * 128;
+      // P of key step kk (16 keys, 8 columns) lies in the first 16 columns
+      // of its key quarter's 32.
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2,
-                                     neg_m2);
-        const float2 x1 = __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2,
-                                     neg_m2);
-        const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-        const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-        sum_a = __fadd2_rn(sum_a, e0);
-        sum_b = __fadd2_rn(sum_b, e1);
-        r[c / 2] = pack_bf16(e0.x, e0.y);
-        r[c / 2 + 1] = pack_bf16(e1.x, e1.y);
+      for (int kk = 0; kk < 4; ++kk)
+        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
+                     idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+      if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 4; kk < 8; ++kk)
+        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
+                     idesc_pv, 1u);
+      umma_commit_warp(&bars[kRingEmpty + vslot]);
+      umma_commit_warp(&bars[kPVDone + sb]);
+      if (rec & kRecLast) umma_commit_warp(&bars[kODone]);
+      ++pos;
+      return true;
+    };
+    while (true) {
+      const int slot = pos % kRing;
+      if (!wait_all(&bars[kRingFull + slot], (pos / kRing) & 1, abort,
+                    p.status))
+        break;
+      const uint32_t rec = s_rec[slot];
+      ++pos;
+      if (rec & kRecEnd) {
+        if (blk >= 2 && !issue_pv(blk - 2, r2)) break;
+        if (blk >= 1) issue_pv(blk - 1, r1);
+        break;
       }
-      if (rescale) {
-        // O holds steps < j: wait for PV(j-1), then scale it (PV(j) cannot
-        // start before this thread arrives on kPFull0 below).
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars[kODone], (j - 1) & 1,
-                                               abort, p.status))) {
+      // QK(blk) into S[blk % 3].
+      const uint32_t qb = (rec & kRecItem) ? 1u : 0u;
+      if ((rec & kRecFirst) &&
+          !wait_all(&bars[kQFull + qb], (rec & kRecQPhase) ? 1u : 0u, abort,
+                    p.status))
+        break;
+      tc_fence_after();
+      const uint32_t a = q_lo + qb * kTileUnits;
+      const uint32_t b_ = k_lo + slot * kTileUnits;
+      const uint32_t sb = blk % kSBufs;
+      const uint32_t t_s = tmem + sb * 128;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+        umma_ss_warp(t_s, a + off, b_ + off, idesc_qk, kk > 0 ? 1u : 0u);
+      }
+      umma_commit_warp(&bars[kSFull + sb]);
+      umma_commit_warp(&bars[kRingEmpty + slot]);
+      if (rec & kRecLast) umma_commit_warp(&bars[kQEmpty + qb]);
+      if (blk >= 2 && !issue_pv(blk - 2, r2)) break;
+      r2 = r1;
+      r1 = rec;
+      ++blk;
+    }
+    if (*abort) {
+      // Let the MMAs in flight finish before TMEM is released.
+      volatile int never = 0;
+      umma_commit_warp(&bars[kDrain]);
+      mbar_wait(&bars[kDrain], 0, &never, nullptr);
+    }
+  } else {
+    // ---------------- softmax + epilogue (warps 0-15) ----------------
+    const int kq = warp / 4;       // keys [32 kq, 32 kq + 32) of a block
+    const int quarter = warp % 4;  // TMEM lane quarter
+    const int row = quarter * 32 + lane;  // query row of the tile
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    float* xmax = s_xchg;            // [block parity][key quarter][row]
+    float* xsum = s_xchg + 2 * 512;  // [key quarter][row]
+    const uint32_t t_o = tmem + kSBufs * 128 + kq * 32 + lane_base;
+    Stream st;
+    st.init(p, blockIdx.x, gridDim.x, true);
+    // Valid key count of block jj of the current item: partial tiles from
+    // valid_count (part list first, walked from its end), full ones 128.
+    auto part_kv = [&](int jj) -> int {
+      return p.part_idx[st.off + (st.pc - 1 - jj)];
+    };
+    auto dense_valid = [&](int jj) -> int {
+      const int64_t rest = p.used - static_cast<int64_t>(jj) * kTile;
+      return rest < kTile ? static_cast<int>(rest) : kTile;
+    };
+    bool ok = true;
+    while (ok && st.valid(p)) {
+      const int h = st.h, qt = st.qt, len = st.len, ka = st.ka, pc = st.pc;
+      float m_ref = -INFINITY;  // running max, in log2 units
+      float l = 0.f;            // this warp's part of the row sum
+      // Pipeline: v0 = valid count of block j, v1 of block j + 1 (load in
+      // flight), k2 = key tile of block j + 2 if it is partial.
+      int v0 = kTile, v1 = kTile, k2 = 0;
+      if (p.dense) {
+        v0 = dense_valid(0);
+        v1 = dense_valid(1);
+      } else {
+        if (pc > 0) v0 = p.valid_count[part_kv(0)];
+        if (pc > 1) v1 = p.valid_count[part_kv(1)];
+        if (pc > 2) k2 = part_kv(2);
+      }
+      for (int j = 0; j < len; ++j) {
+        const int valid = v0;
+        v0 = v1;
+        if (p.dense) {
+          v1 = dense_valid(j + 2);
+        } else {
+          v1 = j + 2 < pc ? p.valid_count[k2] : kTile;
+          if (j + 3 < pc) k2 = part_kv(j + 3);
+        }
+        const int blk = st.blk;
+        st.j += 1;
+        st.blk += 1;
+        const uint32_t sb = static_cast<uint32_t>(blk) % kSBufs;
+        const uint32_t spar = (static_cast<uint32_t>(blk) / kSBufs) & 1;
+        const int xb = blk & 1;
+        if (!wait_all(&bars[kSFull + sb], spar, abort, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        rescale_o(t_o + lane_base, alpha);
-        l *= alpha;
-      }
-      tmem_st32(t_s + lane_base + 0, r);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars[kPFull0]);
-      // Keys 64-127: P never overwrites S columns 64-127, so they are read
-      // again from TMEM instead of staying live in registers since the max.
-      tmem_ld32(t_s + lane_base + 64, r + 64);
-      tmem_ld32(t_s + lane_base + 96, r + 96);
-      tmem_wait_ld();
-      if (st.valid < kTile) {
+        const uint32_t t_s = tmem + sb * 128 + kq * 32 + lane_base;
+        uint32_t r[32];
+        tmem_ld32(t_s, r);
+        tmem_wait_ld();
+        float* sc = reinterpret_cast<float*>(r);
+        if (valid < kTile) {
 #pragma unroll
-        for (int c = 64; c < 128; ++c)
-          if (c >= st.valid) s[c] = -INFINITY;
-      }
-      // The first 32 on the MUFU, the last kPolyCols on the FMA pipes
-      // (exp2_poly2), which balances the two units.
-#pragma unroll
-      for (int c = 64; c < 128; c += 4) {
-        const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2,
-                                     neg_m2);
-        const float2 x1 = __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2,
-                                     neg_m2);
-        float2 e0, e1;
-        if (c >= 128 - kPolyCols) {
-          e0 = exp2_poly2(x0);
-          e1 = exp2_poly2(x1);
+          for (int c = 0; c < 32; ++c)
+            if (kq * 32 + c >= valid) sc[c] = -INFINITY;
+        }
+        const float pm = row_max32(sc);
+        float* xm = xmax + xb * 512 + row;
+        xm[kq * 128] = pm;
+        row_sync(1 + quarter);
+        const float mb = max3(fmaxf(xm[0], xm[128]), xm[256], xm[384]) *
+                         p.scale_log2;
+        bool rescale = false;
+        float alpha = 1.0f;
+        if (j == 0) {
+          m_ref = mb;
         } else {
-          e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-          e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+          // The four warps of a row see the same maxima: same decision.
+          const bool grow = mb > m_ref + 8.0f;
+          rescale = __any_sync(0xffffffffu, grow);
+          if (rescale) {
+            const float m_new = grow ? mb : m_ref;
+            alpha = ex2_approx(m_ref - m_new);
+            m_ref = m_new;
+          }
         }
-        sum_a = __fadd2_rn(sum_a, e0);
-        sum_b = __fadd2_rn(sum_b, e1);
-        r[c / 2] = pack_bf16(e0.x, e0.y);
-        r[c / 2 + 1] = pack_bf16(e1.x, e1.y);
+        const float2 sum = p32(r, sc, make_float2(p.scale_log2, p.scale_log2),
+                               make_float2(-m_ref, -m_ref));
+        if (rescale) {
+          // O holds PV of the previous block once that PV has finished.
+          const uint32_t pb = static_cast<uint32_t>(blk - 1);
+          if (!wait_all(&bars[kPVDone + pb % kSBufs], (pb / kSBufs) & 1,
+                        abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          rescale_o32(t_o, alpha);
+          l *= alpha;
+        }
+        tmem_st16(t_s, r);  // P over the first 16 of this warp's columns
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[(kq < 2 ? kPFull0 : kPFull1) + sb]);
+        l += sum.x + sum.y;
       }
-      tmem_st32(t_s + lane_base + 32, r + 32);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars[kPFull1]);
-      const float2 sum2 = __fadd2_rn(sum_a, sum_b);
-      l += sum2.x + sum2.y;
-    }
-    // ---------------- epilogue ----------------
-    if (ok && n_steps > 0)
-      ok = mbar_wait(&bars[kODone], (n_steps - 1) & 1, abort, p.status);
-    ok = __all_sync(0xffffffffu, ok);
-    const int64_t q_row = static_cast<int64_t>(qt) * kTile + row;
-    // Dense mode: rows >= used keep the zeros written before the launch.
-    const bool write = !p.dense || q_row < p.used;
-    if (ok) {
-      __nv_bfloat16* dst = p.out + q_row * p.out_stride_n + h * p.out_stride_h;
-      if (n_steps > 0) tc_fence_after();
-      const float inv_l = n_steps > 0 ? 1.0f / l : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        if (n_steps > 0) {
-          tmem_ld32(t_o + lane_base + c * 32, o);  // warp-wide, unpredicated
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0u;
+      if (!ok) break;
+      // ---------------- epilogue of the item ----------------
+      float l_row = 0.f;
+      if (len > 0) {
+        xsum[kq * 128 + row] = l;
+        row_sync(1 + quarter);
+        l_row = (xsum[row] + xsum[128 + row]) + (xsum[256 + row] + xsum[384 + row]);
+        if (!wait_all(&bars[kODone], ka & 1, abort, p.status)) {
+          ok = false;
+          break;
         }
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          packed[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv_l,
-                                __uint_as_float(o[2 * i + 1]) * inv_l);
-        if (write) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1],
-                               packed[4 * i + 2], packed[4 * i + 3]);
-        }
+        tc_fence_after();
       }
-      if (p.lse != nullptr && write) {
-        const float lse = n_steps > 0
-                              ? (m_ref + lg2_approx(l)) * 0.69314718055994531f
-                              : -INFINITY;
+      const int64_t q_row = static_cast<int64_t>(qt) * kTile + row;
+      // Dense mode: rows >= used keep the zeros written before the launch.
+      const bool write = !p.dense || q_row < p.used;
+      const float inv_l = len > 0 ? 1.0f / l_row : 0.f;
+      uint32_t o[32];
+      if (len > 0) {
+        tmem_ld32(t_o, o);  // warp-wide, unpredicated
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kOFree]);  // O may be overwritten
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (write) {
+        uint4* d4 = reinterpret_cast<uint4*>(p.out + q_row * p.out_stride_n +
+                                             h * p.out_stride_h + kq * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d4[i] = make_uint4(
+              pack_bf16(__uint_as_float(o[8 * i]) * inv_l,
+                        __uint_as_float(o[8 * i + 1]) * inv_l),
+              pack_bf16(__uint_as_float(o[8 * i + 2]) * inv_l,
+                        __uint_as_float(o[8 * i + 3]) * inv_l),
+              pack_bf16(__uint_as_float(o[8 * i + 4]) * inv_l,
+                        __uint_as_float(o[8 * i + 5]) * inv_l),
+              pack_bf16(__uint_as_float(o[8 * i + 6]) * inv_l,
+                        __uint_as_float(o[8 * i + 7]) * inv_l));
+      }
+      if (kq == 0 && p.lse != nullptr && write) {
+        const float lse =
+            len > 0 ? (m_ref + lg2_approx(l_row)) * 0.69314718055994531f
+                    : -INFINITY;
         p.lse[q_row * p.lse_stride_row + h * p.lse_stride_h] = lse;
       }
+      st.next_item(p, true);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -473,18 +789,21 @@ __global__ void zero_rows_kernel(__nv_bfloat16* out, int64_t stride_s,
 }
 
 int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk,
-               const CUtensorMap& mv, const FwdParams& p, int64_t grid,
+               const CUtensorMap& mv, const FwdParams& p,
                cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    VEDA_CUDA(cudaGetDevice(&dev));
+    VEDA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount,
+                                     dev));
     VEDA_CUDA(cudaFuncSetAttribute(bsa_fwd_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemBytes));
-    configured = true;
   }
-  if (grid == 0) return VEDA_OK;
-  bsa_fwd_kernel<<<static_cast<unsigned>(grid), kFwdThreads, kSmemBytes,
-                   stream>>>(mq, mk, mv, p);
+  if (p.n_items == 0) return VEDA_OK;
+  const int grid = p.n_items < sms ? p.n_items : sms;
+  bsa_fwd_kernel<<<grid, kFwdThreads, kSmemBytes, stream>>>(mq, mk, mv, p);
   return check_launch("bsa_fwd_kernel");
 }
 
@@ -514,7 +833,7 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   VEDA_REQUIRE(n_heads >= 1 && n_q_tiles >= 0 && n_kv_tiles >= 1,
                "bad shape");
   VEDA_REQUIRE(ld_idx >= n_kv_tiles, "ld_idx must be >= n_kv_tiles");
-  VEDA_REQUIRE(n_q_tiles * n_heads < (int64_t(1) << 31), "grid too large");
+  VEDA_REQUIRE(n_q_tiles * n_heads < (int64_t(1) << 30), "too many tiles");
   VEDA_REQUIRE(softmax_scale > 0.f, "softmax_scale must be positive");
   VEDA_REQUIRE(reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
                    out_stride_n % 8 == 0 && out_stride_h % 8 == 0,
@@ -533,6 +852,7 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   p.n_heads = n_heads;
   p.n_q_tiles = static_cast<int>(n_q_tiles);
   p.n_kv_tiles = static_cast<int>(n_kv_tiles);
+  p.n_items = static_cast<int>(n_q_tiles * n_heads);
   p.valid_count = valid_count;
   p.part_cnt = part_cnt;
   p.part_idx = part_idx;
@@ -549,7 +869,7 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   p.dense = 0;
   p.used = 0;
   p.status = device_status_ptr();
-  return launch_fwd(mq, mk, mv, p, n_q_tiles * n_heads, as_stream(stream));
+  return launch_fwd(mq, mk, mv, p, as_stream(stream));
 }
 
 extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
@@ -569,7 +889,7 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
                    out_stride_s % 8 == 0 && out_stride_h % 8 == 0,
                "out must be 16-byte aligned with strides multiple of 8");
   const int64_t tiles = (used + kTile - 1) / kTile;
-  VEDA_REQUIRE(tiles * n_heads < (int64_t(1) << 31), "grid too large");
+  VEDA_REQUIRE(tiles * n_heads < (int64_t(1) << 30), "too many tiles");
   if (seq_len > used) {
     const int64_t n = (seq_len - used) * n_heads * (kHeadDim / 8);
     zero_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
@@ -591,6 +911,7 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
   p.n_heads = n_heads;
   p.n_q_tiles = static_cast<int>(tiles);
   p.n_kv_tiles = static_cast<int>(tiles);
+  p.n_items = static_cast<int>(tiles * n_heads);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_n = out_stride_s;
   p.out_stride_h = out_stride_h;
@@ -601,5 +922,5 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
   p.dense = 1;
   p.used = used;
   p.status = device_status_ptr();
-  return launch_fwd(mq, mk, mv, p, tiles * n_heads, as_stream(stream));
+  return launch_fwd(mq, mk, mv, p, as_stream(stream));
 }

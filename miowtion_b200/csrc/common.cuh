@@ -274,6 +274,61 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// The same descriptor split into 32-bit halves, so that issue loops add a
+// per-step offset (in 16-byte units) to the low half with one instruction:
+// the start address occupies the low 14 bits and never carries out of them
+// inside shared memory. The high half (SBO 1024 B, version 1, SWIZZLE_128B)
+// is the same for every operand here.
+__device__ __forceinline__ uint32_t sw128_desc_lo(uint32_t smem_addr,
+                                                  uint32_t lbo_bytes) {
+  return ((smem_addr >> 4) & 0x3FFF) | (((lbo_bytes >> 4) & 0x3FFF) << 16);
+}
+constexpr uint32_t kSw128DescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+
+// Warp-collective issue: every lane of the warp executes these (converged),
+// and the lane that elect.sync picks issues the instruction. An issue loop
+// written this way keeps the warp converged between MMA groups; a loop run
+// by one lane inside `if (lane == 0)` pays ~100 cycles of tensor-core idle
+// for every branch or barrier wait between groups (measured on B200).
+//
+// D[tmem] (+)= A[smem] . B[smem], descriptors given as low halves.
+__device__ __forceinline__ void umma_ss_warp(uint32_t d_tmem, uint32_t a_lo,
+                                             uint32_t b_lo, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p, e; .reg .b64 da, db; .reg .b32 rx; "
+      "elect.sync rx|e, 0xFFFFFFFF; mov.b64 da, {%1, %5}; "
+      "mov.b64 db, {%2, %5}; setp.ne.b32 p, %4, 0; "
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p; }" ::"r"(
+          d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] . B[smem], B descriptor given as its low half.
+__device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                             uint32_t b_lo, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p, e; .reg .b64 db; .reg .b32 rx; "
+      "elect.sync rx|e, 0xFFFFFFFF; mov.b64 db, {%2, %5}; "
+      "setp.ne.b32 p, %4, 0; "
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p; }" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      : "memory");
+}
+
+// tcgen05.commit from the elected lane: `bar` completes one arrival when
+// every MMA this warp issued before has completed.
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{ .reg .pred e; .reg .b32 rx; elect.sync rx|e, 0xFFFFFFFF; "
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster."
+      "b64 [%0]; }" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
 // Shared-memory matrix descriptor (tcgen05 "SM100" format, version 1) of a
 // 128-byte-swizzled operand. K-major: rows of 64 bf16, 8-row atoms 1024 B
 // apart (SBO). MN-major: 64-element MN chunks `lbo` bytes apart, 8-row K
