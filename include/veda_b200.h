@@ -212,6 +212,44 @@ int veda_dense_fwd(const void* q, const void* k, const void* v,
                    int64_t lse_stride_s, int64_t lse_stride_h,
                    float softmax_scale, void* stream);
 
+/* ---- a10: block-sparse attention backward (tcgen05) ---------------------- */
+
+/* Bytes of device workspace veda_bsa_bwd needs (the per-row D = rowsum(dO*O)
+ * and LSE*log2(e), fp32 [2][H'][R*128]); -1 for a bad shape. */
+int64_t veda_bsa_bwd_workspace(int32_t n_heads, int64_t n_q_tiles);
+
+/* Replaces the backward of miowtion/kernels/fa4.py:299-377 (FA4 through
+ * autograd, fa4.py:337-359; reference gradients
+ * tests/gpu/test_kernels_gpu.py:200-250): dq, dk, dv of the forward above.
+ *   q/k/v/out/dout as in veda_bsa_fwd (out, dout [R*128, H', D]);
+ *   lse fp32 natural log as veda_bsa_fwd wrote it, element (row, head) at
+ *   lse[row * lse_stride_row + head * lse_stride_h];
+ *   the forward lists (per query tile, ld_idx >= n_kv_tiles) and the
+ *   transposed lists (per key tile, ld_t_idx >= n_q_tiles) as
+ *   veda_index_lists writes them;
+ *   dq [R*128, H', D], dk/dv [N, H', D] bf16 outputs (every row written:
+ *   rows of tiles without any block get 0);
+ *   workspace: veda_bsa_bwd_workspace bytes, 16-byte aligned.
+ * Deterministic (no atomics): dq query-major, dk/dv key-major. */
+int veda_bsa_bwd(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                 const void* k, int64_t k_stride_n, int64_t k_stride_h,
+                 const void* v, int64_t v_stride_n, int64_t v_stride_h,
+                 const void* out, int64_t out_stride_n, int64_t out_stride_h,
+                 const void* dout, int64_t dout_stride_n,
+                 int64_t dout_stride_h, const float* lse,
+                 int64_t lse_stride_row, int64_t lse_stride_h,
+                 int32_t n_heads, int64_t n_q_tiles, int64_t n_kv_tiles,
+                 const int32_t* valid_count, const int32_t* part_cnt,
+                 const int32_t* part_idx, const int32_t* full_cnt,
+                 const int32_t* full_idx, int64_t ld_idx,
+                 const int32_t* t_part_cnt, const int32_t* t_part_idx,
+                 const int32_t* t_full_cnt, const int32_t* t_full_idx,
+                 int64_t ld_t_idx, void* dq, int64_t dq_stride_n,
+                 int64_t dq_stride_h, void* dk, int64_t dk_stride_n,
+                 int64_t dk_stride_h, void* dv, int64_t dv_stride_n,
+                 int64_t dv_stride_h, float softmax_scale, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* One 128x128x128 bf16 tcgen05 MMA per mode, for checking operand and

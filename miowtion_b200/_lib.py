@@ -77,6 +77,14 @@ SIGNATURES = {
     'veda_dense_fwd': (c_i32, [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64,
                                c_i64, c_i32, c_ptr, c_i64, c_i64, c_ptr,
                                c_i64, c_i64, c_f32, c_ptr]),
+    'veda_bsa_bwd_workspace': (c_i64, [c_i32, c_i64]),
+    'veda_bsa_bwd': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_ptr,
+                             c_i64, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64,
+                             c_i64, c_ptr, c_i64, c_i64, c_i32, c_i64, c_i64,
+                             c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
+                             c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i64, c_i64,
+                             c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_f32,
+                             c_ptr, ctypes.c_size_t, c_ptr]),
     'veda_probe_umma': (c_i32, [c_ptr, c_ptr, c_ptr, c_i32, c_ptr]),
 }
 

@@ -153,6 +153,78 @@ def block_sparse_attention_lists(q: torch.Tensor, k: torch.Tensor,
     return (out, lse) if return_lse else out
 
 
+def block_sparse_attention_bwd(q: torch.Tensor, k: torch.Tensor,
+                               v: torch.Tensor, out: torch.Tensor,
+                               dout: torch.Tensor, lse: torch.Tensor,
+                               lists: veda_mask.BlockLists,
+                               t_lists: veda_mask.BlockLists,
+                               layout: tiling.TileLayout
+                               ) -> tuple[torch.Tensor, ...]:
+    """dq, dk, dv of `block_sparse_attention_lists` (the backward FA4 runs
+    through autograd, fa4.py:337-359). `lists` are the forward lists (per
+    query tile), `t_lists` the transposed ones (per key tile,
+    `index_lists(..., transpose=True)`); `lse` [H', R * 128] as the forward
+    returned it. Rows of tiles without any block get zero gradients."""
+    _require(q, 'block_sparse_attention backward')
+    heads = q.shape[1]
+    n_q = q.shape[0] // _TILE
+    if t_lists.part_cnt.shape != (heads, layout.n_tiles):
+        raise ValueError('transposed lists must cover every key tile')
+    dout = dout if dout.stride(-1) == 1 and dout.stride(0) % 8 == 0 and (
+        dout.stride(1) % 8 == 0) else dout.contiguous()
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    need = _lib.load().veda_bsa_bwd_workspace(heads, n_q)
+    ws = torch.empty(max(need, 16) // 4, dtype=torch.float32, device=q.device)
+    _lib.call('veda_bsa_bwd', q.data_ptr(), q.stride(0), q.stride(1),
+              k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+              v.stride(0), v.stride(1), out.data_ptr(), out.stride(0),
+              out.stride(1), dout.data_ptr(), dout.stride(0), dout.stride(1),
+              lse.data_ptr(), lse.stride(1), lse.stride(0), heads, n_q,
+              layout.n_tiles, layout.valid_count.data_ptr(),
+              lists.part_cnt.data_ptr(), lists.part_idx.data_ptr(),
+              lists.full_cnt.data_ptr(), lists.full_idx.data_ptr(),
+              lists.part_idx.shape[-1], t_lists.part_cnt.data_ptr(),
+              t_lists.part_idx.data_ptr(), t_lists.full_cnt.data_ptr(),
+              t_lists.full_idx.data_ptr(), t_lists.part_idx.shape[-1],
+              dq.data_ptr(), dq.stride(0), dq.stride(1), dk.data_ptr(),
+              dk.stride(0), dk.stride(1), dv.data_ptr(), dv.stride(0),
+              dv.stride(1), 1.0 / math.sqrt(q.shape[-1]), ws.data_ptr(),
+              ws.numel() * 4, _lib.stream_ptr(q.device))
+    return dq, dk, dv
+
+
+class _BlockSparseAttention(torch.autograd.Function):
+    """Forward and backward over prebuilt forward and transposed lists."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lists, t_lists, layout):
+        out, lse = block_sparse_attention_lists(q, k, v, lists, layout,
+                                                return_lse=True)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.lists, ctx.t_lists, ctx.layout = lists, t_lists, layout
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, dout, _dlse):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = block_sparse_attention_bwd(q, k, v, out, dout, lse,
+                                                ctx.lists, ctx.t_lists,
+                                                ctx.layout)
+        return dq, dk, dv, None, None, None
+
+
+def block_sparse_attention_autograd(q: torch.Tensor, k: torch.Tensor,
+                                    v: torch.Tensor,
+                                    lists: veda_mask.BlockLists,
+                                    t_lists: veda_mask.BlockLists,
+                                    layout: tiling.TileLayout):
+    """(out, lse) with gradients for q, k, v (both list directions given)."""
+    return _BlockSparseAttention.apply(q, k, v, lists, t_lists, layout)
+
+
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            block_mask: torch.Tensor,
                            layout: tiling.TileLayout,
@@ -176,9 +248,13 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         t.requires_grad for t in (q, k, v))
     if needs_grad and block_mask.shape[1] != layout.n_tiles:
         raise ValueError('backward needs the block mask of all query tiles')
-    if needs_grad:
-        raise NotImplementedError('block-sparse backward is not built yet')
     lists = _lists(block_mask, layout, transpose=False, tails=False)
     with _CALL_LOCK:
+        if needs_grad:
+            # The backward walks key-tile-major lists (fa4.py:353-359).
+            t_lists = _lists(block_mask, layout, transpose=True, tails=False)
+            out, lse = _BlockSparseAttention.apply(q, k, v, lists, t_lists,
+                                                   layout)
+            return (out, lse) if return_lse else out
         return block_sparse_attention_lists(q, k, v, lists, layout,
                                             return_lse)
