@@ -215,7 +215,9 @@ int veda_dense_fwd(const void* q, const void* k, const void* v,
 /* ---- a10: block-sparse attention backward (tcgen05) ---------------------- */
 
 /* Bytes of device workspace veda_bsa_bwd needs (the per-row D = rowsum(dO*O)
- * and LSE*log2(e), fp32 [2][H'][R*128]); -1 for a bad shape. */
+ * and LSE*log2(e), fp32 [2][H'][R*128], then two work-item counters that
+ * veda_bsa_bwd zeroes on the stream); -1 for a bad shape. Concurrent calls
+ * need separate workspaces. */
 int64_t veda_bsa_bwd_workspace(int32_t n_heads, int64_t n_q_tiles);
 
 /* Replaces the backward of miowtion/kernels/fa4.py:299-377 (FA4 through

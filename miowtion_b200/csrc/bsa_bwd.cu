@@ -21,8 +21,8 @@
 //           dP^T = V dO^T, P^T and dS^T written back over them, then
 //           dV += P^T dO and dK += dS^T Q (TS MMAs); K and V stay in shared
 //           memory for the whole key tile.
-// Both main kernels are persistent (one CTA per SM, items with a stride of
-// the grid, heaviest rows first), with 8 compute warps (warp w: TMEM lanes
+// Both main kernels are persistent (one CTA per SM taking items from a
+// global counter, heaviest rows first within a head), with 8 compute warps (warp w: TMEM lanes
 // 32(w%4).., columns 64(w/4)..), a TMA producer warp and a converged MMA
 // warp. The walk of each list is the forward's: partial list then full list,
 // each from its end. All waits are bounded (common.cuh).
@@ -70,69 +70,112 @@ struct BwdParams {
   int64_t grad2_sn, grad2_sh;
   float scale;
   float scale_log2;
+  unsigned int* counter;  // the item counter, zero at launch
   unsigned int* status;
 };
 
-// The items (head, list row) of one CTA, heaviest rows (the last ones: the
-// global tiles) first, and their blocks. Every role walks the same sequence,
-// so they agree on barrier phases without talking.
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity,
+                                         volatile int* abort,
+                                         unsigned int* status) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, status));
+}
+
+// Work items are handed out dynamically: the producer warp of each CTA takes
+// the next item index from a global counter and publishes it in a shared
+// queue, which the MMA warp and the compute warps read in the same order.
+// All CTAs then work on neighbouring items at any time (the tiles they load
+// stay in L2) and load balances itself, however unequal the lists are.
+constexpr int kQueue = 8;
+constexpr int kQueueReaders = 9;  // the MMA warp and 8 compute warps
+
+struct ItemQueue {
+  volatile int* slots;   // [kQueue] item indices, -1 = end
+  uint64_t* full;        // [kQueue] published (producer)
+  uint64_t* empty;       // [kQueue] read by every reader
+  unsigned int* counter;
+  int n_items;
+  volatile int* abort;
+  unsigned int* status;
+};
+
+// The items (head, list row) one CTA takes, heaviest rows (the last ones:
+// the global tiles) first within a head, and their blocks. Every role walks
+// the same sequence, so they agree on barrier phases without talking.
 struct ListStream {
   const ListSet* L;
-  int n_items, it, stride;
+  const ItemQueue* Q;
+  bool producer;
+  int q;  // queue position
+  int n_items, it;
   int h, row, pc, fc, len, j, blk, ka;
   int64_t off;
-  int npc, nfc;  // counts of item it + stride, read an item ahead
+  bool ok;  // false after an expired wait
 
-  __device__ void fetch(int item) {
-    npc = 0;
-    nfc = 0;
-    if (item >= n_items) return;
-    const int64_t r = static_cast<int64_t>(item / L->n_rows) * L->n_rows +
-                      (L->n_rows - 1 - item % L->n_rows);
-    npc = L->part_cnt[r];
-    nfc = L->full_cnt[r];
+  // The next item index from the queue (warp-collective); -1 at the end.
+  __device__ int pull() {
+    const int slot = q % kQueue;
+    const uint32_t phase = (q / kQueue) & 1;
+    int item = -1;
+    if (producer) {
+      if (q >= kQueue && !wait_all(&Q->empty[slot], phase ^ 1, Q->abort,
+                                   Q->status)) {
+        ok = false;
+        return -1;
+      }
+      if ((threadIdx.x & 31) == 0) {
+        item = static_cast<int>(atomicAdd(Q->counter, 1u));
+        if (item >= Q->n_items) item = -1;
+        Q->slots[slot] = item;
+        mbar_arrive(&Q->full[slot]);
+      }
+      item = __shfl_sync(0xffffffffu, item, 0);
+    } else {
+      if (!wait_all(&Q->full[slot], phase, Q->abort, Q->status)) {
+        ok = false;
+        return -1;
+      }
+      item = Q->slots[slot];
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&Q->empty[slot]);
+    }
+    ++q;
+    return item;
   }
-  __device__ void load_item() {
+  __device__ void set_item(int item) {
+    if (item < 0) {
+      it = n_items;
+      return;
+    }
+    it = item;
     h = it / L->n_rows;
     row = L->n_rows - 1 - it % L->n_rows;
-    off = (static_cast<int64_t>(h) * L->n_rows + row) * L->ld;
-    pc = npc;
-    fc = nfc;
+    const int64_t r = static_cast<int64_t>(h) * L->n_rows + row;
+    off = r * L->ld;
+    pc = L->part_cnt[r];
+    fc = L->full_cnt[r];
     len = pc + fc;
     j = 0;
-    fetch(it + stride);
+    if (len > 0) ++ka;
   }
-  __device__ void init(const ListSet* ls, int heads, int first, int step,
-                       bool keep_empty) {
+  __device__ void init(const ListSet* ls, const ItemQueue* queue,
+                       bool is_producer, bool keep_empty) {
     L = ls;
-    n_items = heads * ls->n_rows;
-    it = first;
-    stride = step;
+    Q = queue;
+    producer = is_producer;
+    q = 0;
+    n_items = queue->n_items;
     blk = 0;
     ka = -1;
-    if (it < n_items) {
-      fetch(it);
-      load_item();
-      if (len > 0) ka = 0;
-      if (!keep_empty) skip_empty();
-    }
+    ok = true;
+    set_item(pull());
+    if (!keep_empty) skip_empty();
   }
   __device__ void skip_empty() {
-    while (it < n_items && len == 0) {
-      it += stride;
-      if (it < n_items) {
-        load_item();
-        if (len > 0) ++ka;
-      }
-    }
+    while (it < n_items && len == 0) set_item(pull());
   }
   __device__ void next_item(bool keep_empty) {
-    it += stride;
-    if (it < n_items) {
-      load_item();
-      if (len > 0) ++ka;
-      if (!keep_empty) skip_empty();
-    }
+    set_item(pull());
+    if (!keep_empty) skip_empty();
   }
   __device__ bool valid() const { return it < n_items; }
   // Entry jj of the current item's walk: part list, then full list, each
@@ -147,12 +190,6 @@ struct ListStream {
     next_item(false);
   }
 };
-
-__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity,
-                                         volatile int* abort,
-                                         unsigned int* status) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, status));
-}
 
 __device__ __forceinline__ void arrive_warp(uint64_t* bar) {
   tc_fence_before();
@@ -249,9 +286,11 @@ enum DqBar {
   kDqDone,         // the item's last dQ MMA finished
   kDqFree,         // the epilogue has read dQ (8 warps)
   kDqDrain,
-  kDqNumBars
+  kDqItemFull,                       // [kQueue]
+  kDqItemEmpty = kDqItemFull + kQueue,  // [kQueue]
+  kDqNumBars = kDqItemEmpty + kQueue
 };
-constexpr int kDqSmem = 6 * kTileBytes + kListCap * 4 + 256 + 1024;
+constexpr int kDqSmem = 6 * kTileBytes + kListCap * 4 + 512 + 1024;
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bsa_bwd_dq_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -268,13 +307,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_list + kListCap);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDqNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const ItemQueue queue{reinterpret_cast<volatile int*>(tmem_slot + 2),
+                        bars + kDqItemFull, bars + kDqItemEmpty, p.counter,
+                        p.n_heads * p.lists.n_rows, abort, p.status};
 
   const int tid = threadIdx.x;
   const int warp = tid / 32;
   const int lane = tid % 32;
   if (tid == 0) {
     for (int b = 0; b < kDqNumBars; ++b)
-      mbar_init(&bars[b], (b == kDsFull || b == kDqFree) ? 8 : 1);
+      mbar_init(&bars[b], (b == kDsFull || b == kDqFree) ? 8
+                          : (b >= kDqItemEmpty)         ? kQueueReaders
+                                                        : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -295,7 +339,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       prefetch_tensor_map(&map_v);
     }
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, false);
+    st.init(&p.lists, &queue, true, false);
     int q_loads = 0, kv_loads = 0;
     while (st.valid()) {
       if (st.j == 0) {
@@ -345,7 +389,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t kvmn_lo = sw128_desc_lo(smem_u32(s_kv), kHalfBytes);
     const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, false);
+    st.init(&p.lists, &queue, false, false);
     while (st.valid()) {
       const bool first = st.j == 0, last = st.j == st.len - 1;
       const int ka = st.ka;
@@ -398,7 +442,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int64_t n_rows_q = static_cast<int64_t>(p.n_q_tiles) * kTile;
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, true);
+    st.init(&p.lists, &queue, false, true);
     bool ok = true;
     while (ok && st.valid()) {
       const int h = st.h, qt = st.row, len = st.len, ka = st.ka;
@@ -483,10 +527,12 @@ enum KvBar {
   kKvDone,         // the item's last dV/dK MMAs finished
   kKvFree,         // the epilogue has read dV and dK (8 warps)
   kKvDrain,
-  kKvNumBars
+  kKvItemFull,                       // [kQueue]
+  kKvItemEmpty = kKvItemFull + kQueue,  // [kQueue]
+  kKvNumBars = kKvItemEmpty + kQueue
 };
 // K, V, then [2 stages] x (Q, dO), then [2 stages] x (L, D) vectors.
-constexpr int kKvSmem = 6 * kTileBytes + 2 * 1024 + kListCap * 4 + 256 + 1024;
+constexpr int kKvSmem = 6 * kTileBytes + 2 * 1024 + kListCap * 4 + 512 + 1024;
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bsa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -505,6 +551,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_list + kListCap);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kKvNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const ItemQueue queue{reinterpret_cast<volatile int*>(tmem_slot + 2),
+                        bars + kKvItemFull, bars + kKvItemEmpty, p.counter,
+                        p.n_heads * p.lists.n_rows, abort, p.status};
 
   const int tid = threadIdx.x;
   const int warp = tid / 32;
@@ -512,7 +561,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int64_t n_rows_q = static_cast<int64_t>(p.n_q_tiles) * kTile;
   if (tid == 0) {
     for (int b = 0; b < kKvNumBars; ++b)
-      mbar_init(&bars[b], (b == kPdsFull || b == kKvFree) ? 8 : 1);
+      mbar_init(&bars[b], (b == kPdsFull || b == kKvFree) ? 8
+                          : (b >= kKvItemEmpty)         ? kQueueReaders
+                                                        : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -533,7 +584,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       prefetch_tensor_map(&map_v);
     }
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, false);
+    st.init(&p.lists, &queue, true, false);
     int kt_loads = 0, qd_loads = 0;
     while (st.valid()) {
       if (st.j == 0) {
@@ -590,7 +641,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t t_s = tmem, t_dp = tmem + 128;
     const uint32_t t_dv = tmem + 256, t_dk = tmem + 384;
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, false);
+    st.init(&p.lists, &queue, false, false);
     while (st.valid()) {
       const bool first = st.j == 0, last = st.j == st.len - 1;
       const int ka = st.ka;
@@ -647,7 +698,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = quarter * 32 + lane;  // key row of the tile
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     ListStream st;
-    st.init(&p.lists, p.n_heads, blockIdx.x, gridDim.x, true);
+    st.init(&p.lists, &queue, false, true);
     bool ok = true;
     while (ok && st.valid()) {
       const int h = st.h, kt = st.row, len = st.len, ka = st.ka;
@@ -752,8 +803,10 @@ using namespace veda;
 extern "C" int64_t veda_bsa_bwd_workspace(int32_t n_heads,
                                           int64_t n_q_tiles) {
   if (n_heads < 1 || n_q_tiles < 0) return -1;
+  // D and LSE*log2(e) per query row, then the two kernels' item counters.
   return 2 * static_cast<int64_t>(n_heads) * n_q_tiles * kTile *
-         static_cast<int64_t>(sizeof(float));
+             static_cast<int64_t>(sizeof(float)) +
+         16;
 }
 
 extern "C" int veda_bsa_bwd(
@@ -805,7 +858,10 @@ extern "C" int veda_bsa_bwd(
   const int64_t rows = n_q_tiles * kTile;
   float* delta = static_cast<float*>(workspace);
   float* lse2 = delta + static_cast<size_t>(n_heads) * rows;
+  unsigned int* counters = reinterpret_cast<unsigned int*>(
+      lse2 + static_cast<size_t>(n_heads) * rows);
   cudaStream_t s = as_stream(stream);
+  VEDA_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned int), s));
   if (n_q_tiles > 0) {
     const int64_t warps = rows * n_heads;
     bwd_prep_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0,
@@ -854,6 +910,7 @@ extern "C" int veda_bsa_bwd(
     BwdParams pq = p;
     pq.lists = ListSet{static_cast<int>(n_q_tiles), part_cnt, part_idx,
                        full_cnt, full_idx, ld_idx};
+    pq.counter = counters;
     pq.grad = static_cast<__nv_bfloat16*>(dq);
     pq.grad_sn = dq_stride_n;
     pq.grad_sh = dq_stride_h;
@@ -866,6 +923,7 @@ extern "C" int veda_bsa_bwd(
   BwdParams pk = p;
   pk.lists = ListSet{static_cast<int>(n_kv_tiles), t_part_cnt, t_part_idx,
                      t_full_cnt, t_full_idx, ld_t_idx};
+  pk.counter = counters + 1;
   pk.grad = static_cast<__nv_bfloat16*>(dk);
   pk.grad_sn = dk_stride_n;
   pk.grad_sh = dk_stride_h;
