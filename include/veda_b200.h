@@ -252,6 +252,25 @@ int veda_bsa_bwd(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                  int64_t dv_stride_h, float softmax_scale, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/* ---- a13: teacher block heat (tcgen05) ------------------------------------ */
+
+/* Replaces miowtion/veda/heatmap.py:36-110 (teacher_heat_reference and the
+ * Triton kernel it dispatches to, miowtion/kernels/block_heat_triton.py:
+ * 140-173): heat [H', n_q, n_tiles] fp32 for query tiles q_tiles[0..n_q)
+ * against every key tile. q, k [n_tiles*128, H', D] bf16 tile-ordered; lse
+ * the dense teacher's natural-log LSE in tile order, element (slot, head) at
+ * lse[slot * lse_stride_row + head * lse_stride_h]. reduce_sum == 0: the
+ * block's peak probability exp(max s*scale - L); != 0: its mass
+ * sum exp(s*scale - L); s is q.k rounded to bf16; 0 where a tile has no
+ * valid row or key. */
+int veda_teacher_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                      const void* k, int64_t k_stride_n, int64_t k_stride_h,
+                      const float* lse, int64_t lse_stride_row,
+                      int64_t lse_stride_h, int32_t n_heads, int64_t n_tiles,
+                      const int32_t* valid_count, const int64_t* q_tiles,
+                      int64_t n_q, int32_t reduce_sum, float* heat,
+                      float softmax_scale, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* One 128x128x128 bf16 tcgen05 MMA per mode, for checking operand and

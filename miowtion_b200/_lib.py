@@ -85,6 +85,9 @@ SIGNATURES = {
                              c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i64, c_i64,
                              c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_f32,
                              c_ptr, ctypes.c_size_t, c_ptr]),
+    'veda_teacher_heat': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64,
+                                  c_ptr, c_i64, c_i64, c_i32, c_i64, c_ptr,
+                                  c_ptr, c_i64, c_i32, c_ptr, c_f32, c_ptr]),
     'veda_probe_umma': (c_i32, [c_ptr, c_ptr, c_ptr, c_i32, c_ptr]),
 }
 
