@@ -8,7 +8,10 @@ miowtion/h3/model.py:40-45). Every stage is a CUDA kernel of this package:
     ->  tcgen05 block-sparse attention  ->  inverse permutation.
 The block lists go from the selection kernel straight to the attention
 kernel; no dense block mask and no Selection are materialised, and nothing
-synchronises the host.
+synchronises the host. With gradients enabled (the stage-2 student step,
+attention.py:335-359 of the reference) q, k and v receive gradients through
+the permutation and the sparse attention (the selection itself is discrete);
+the backward walks transposed key-tile lists built from the same selection.
 """
 
 from __future__ import annotations
@@ -149,6 +152,45 @@ class _NoEvents:
 _NO_EVENTS = _NoEvents()
 
 
+class _SparseGroup(torch.autograd.Function):
+    """One head group's sparse attention in sequence order, differentiable
+    in q, k and v: gather -> block-sparse attention -> inverse permutation,
+    and back. The tiles of q and k (gathered with the pooling the predictor
+    needs) and both list directions are computed by the caller."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, q_tiles, k_tiles, heads, layout, lists,
+                t_lists):
+        v_tiles = tiling.gather_tiles(v, layout, heads)
+        o_tiles, lse = kernels.block_sparse_attention_lists(
+            q_tiles, k_tiles, v_tiles, lists, layout, return_lse=True)
+        local = torch.arange(heads.numel(), device=q.device)
+        out = torch.zeros(q.shape[0], heads.numel(), q.shape[2],
+                          dtype=q.dtype, device=q.device)
+        tiling.scatter_rows_(out, o_tiles, layout, local)
+        ctx.save_for_backward(q_tiles, k_tiles, v_tiles, o_tiles, lse, heads)
+        ctx.layout, ctx.lists, ctx.t_lists = layout, lists, t_lists
+        ctx.shape = q.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q_tiles, k_tiles, v_tiles, o_tiles, lse, heads = ctx.saved_tensors
+        layout = ctx.layout
+        local = torch.arange(heads.numel(), device=dout.device)
+        dout = dout.contiguous()
+        do_tiles = tiling.gather_tiles(dout, layout, local)
+        grads = kernels.block_sparse_attention_bwd(
+            q_tiles, k_tiles, v_tiles, o_tiles, do_tiles, lse, ctx.lists,
+            ctx.t_lists, layout)
+        outs = []
+        for g in grads:
+            full = torch.zeros(ctx.shape, dtype=g.dtype, device=g.device)
+            tiling.scatter_rows_(full, g, layout, heads)
+            outs.append(full)
+        return (*outs, None, None, None, None, None, None)
+
+
 class SparseStudent:
     """Stage-2 / evaluation attention: predictor-masked block sparsity
     (attention.py:692-794)."""
@@ -178,6 +220,9 @@ class SparseStudent:
             return kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5,
                                            False, used=used)[0]
         self.calls['sparse'] += 1
+        if torch.is_grad_enabled() and any(t.requires_grad
+                                           for t in (q, k, v)):
+            return self._attend_grad(q, k, v, layer_index)
         seq_len = q.shape[0]
         out = torch.empty_like(q)
         if used < seq_len:
@@ -222,3 +267,34 @@ class SparseStudent:
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
         ev.stop(t)
         self.last_lists = lists
+
+    def _attend_grad(self, q, k, v, layer_index: int) -> torch.Tensor:
+        """The differentiable layer: per head group, the forward of
+        `_attend` inside `_SparseGroup`, plus the transposed lists the
+        backward walks (fa4.py:353-359)."""
+        parts, all_heads = [], []
+        for group in self.plan.head_groups(layer_index, self.clip.device):
+            tile_layout = self.clip.get(group.shape)
+            heads = group.heads
+            with torch.no_grad():
+                q_tiles, feats_q = tiling.gather_and_pool(q.detach(),
+                                                          tile_layout, heads)
+                k_tiles, feats_k = tiling.gather_and_pool(k.detach(),
+                                                          tile_layout, heads)
+                logits = self.predictor.layers[layer_index](feats_q, feats_k,
+                                                            heads)
+                lists = veda_mask.select_block_lists(
+                    logits[:, :tile_layout.n_video_tiles], tile_layout,
+                    self.clip.blocks(tile_layout), want_mask=True)
+                t_lists = kernels.index_lists_from_mask(lists.mask,
+                                                        tile_layout)
+            parts.append(_SparseGroup.apply(q, k, v, q_tiles, k_tiles, heads,
+                                            tile_layout, lists, t_lists))
+            all_heads.append(heads)
+            self.last_lists = lists
+        heads = torch.cat(all_heads)
+        if heads.numel() != q.shape[1]:
+            raise ValueError(f'the plan covers {heads.numel()} heads, q has '
+                             f'{q.shape[1]}')
+        out = torch.zeros_like(q)
+        return out.index_copy(1, heads, torch.cat(parts, 1))

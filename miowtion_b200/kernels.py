@@ -114,6 +114,15 @@ def _lists(block_mask: torch.Tensor, layout: tiling.TileLayout,
     return lists
 
 
+def index_lists_from_mask(mask: torch.Tensor, layout: tiling.TileLayout,
+                          transpose: bool = True) -> veda_mask.BlockLists:
+    """Lists of a uint8 or bool block mask [H', n, n] (the mask
+    `select_block_lists(..., want_mask=True)` returns), by default the
+    transposed ones the backward walks."""
+    return _lists(mask.bool() if mask.dtype != torch.bool else mask, layout,
+                  transpose=transpose, tails=False)
+
+
 def _require(q: torch.Tensor, op: str) -> None:
     reason = unavailable_reason(q.device, q.dtype)
     if reason is not None:

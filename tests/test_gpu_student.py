@@ -96,3 +96,47 @@ def test_two_shapes_text_rows_and_padding_match_oracle():
                                       grp['mask'])
     np.testing.assert_allclose(got[:used], want[:used], rtol=2e-2,
                                atol=2e-2)
+
+
+def test_student_backward_matches_oracle():
+    """Gradients of the whole layer (two head groups, partial tiles, text
+    rows, padding rows) against the oracle: per group, the tile-level
+    backward of the reference's attention on the oracle's own selection,
+    mapped back through the permutation. Tolerance: the reference's
+    backward test (3e-2)."""
+    text, grid = 300, (8, 12, 20)
+    used = text + grid[0] * grid[1] * grid[2]
+    seq_len = used + 40
+    spans = [(text, grid)]
+    head_shape = [0, 1, 0, 1]
+    ratio, seed = 0.3, 9
+    q, k, v = inputs.qkv(seq_len, len(head_shape), 128, seed, torch.bfloat16)
+    w = inputs.predictor_weights(len(head_shape), 128, seed + 100, 0.02)
+    student, clip, plan = make_student(
+        seq_len, used, spans,
+        [tiling.TileShape(2, 8, 8), tiling.TileShape(1, 8, 16)], head_shape,
+        veda_mask.Budget(ratio=ratio), w)
+    gen = torch.Generator().manual_seed(4)
+    dout = torch.randn(q.shape, generator=gen).to(torch.bfloat16)
+    ts = [t.to(DEV).requires_grad_(True) for t in (q, k, v)]
+    out = student(*ts, 0)
+    out.backward(dout.to(DEV))
+    got = [t.grad.float().cpu().numpy() for t in ts]
+
+    qf, kf, vf, df = (t.float().numpy() for t in (q, k, v, dout))
+    _, info = vo.sparse_student_layer(
+        qf, kf, vf, oracle_groups(clip, plan, spans), w[0].numpy(),
+        w[1].numpy(), vo.Budget(ratio=ratio), used=used)
+    want = [np.zeros((seq_len + 1,) + q.shape[1:], np.float32)
+            for _ in range(3)]
+    for (lay, heads), inf in zip(oracle_groups(clip, plan, spans), info):
+        tiles = [vo.gather_tiles(x, lay, heads) for x in (qf, kf, vf, df)]
+        grads = vo.block_sparse_attention_bwd(*tiles, inf['mask'],
+                                              lay.valid_count)
+        for buf, g in zip(want, grads):
+            vo.scatter_tiles(buf, g, lay, heads)
+    for name, g, wnt in zip('qkv', got, want):
+        np.testing.assert_allclose(g[:used], wnt[:used], rtol=3e-2, atol=3e-2,
+                                   err_msg=f'd{name}')
+        assert (g[used:] == 0).all()
+        assert not (g[:used] == 0).all()
