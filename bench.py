@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
     python bench.py --impl reference ...   # the reference algorithm on CPU
+    python bench.py --config cfg5 ...      # the stage-2 training step
 
 One step = one Veda attention layer forward over synthetic q, k, v already
 resident in HBM: permute + pool q/k/v, predictor logits, budgeted top-k
@@ -61,6 +62,15 @@ CONFIGS = {
                  target=(14400, (26, 45, 80)), cond=(0, (4, 45, 80)),
                  shapes=[(2, 8, 8)], head_shape=[0] * 48, target_ratio=0.1,
                  ref_ratio=0.05, seed=3),
+    # Config 5: the config-3 layer as a stage-2 training step.
+    'cfg5': dict(desc='stage-2 step on the config-3 shapes: dense fwd + LSE, '
+                      'teacher heat (sum) for all query tiles, sparse student '
+                      'fwd + bwd (transposed lists), dO ~N(0,1) seed 4',
+                 heads=48, seq_len=94624, used=94624,
+                 target=(1024, (26, 45, 80)), cond=None,
+                 shapes=[(2, 8, 8), (1, 8, 16)],
+                 head_shape=[0] * 24 + [1] * 24, target_ratio=0.1,
+                 ref_ratio=None, seed=2, dout_seed=4, train=True),
 }
 
 
@@ -289,6 +299,9 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit('use at least 3 warm-up steps')
+    if cfg.get('train'):
+        run_train_step(args, cfg)
+        return
 
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -434,6 +447,155 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_train_step(args, cfg):
+    """Config 5 on one GPU: the teacher (dense forward with LSE, LSE in tile
+    order, block heat with reduce='sum' for every query tile) and the sparse
+    student forward + backward on the same q, k, v."""
+    from miowtion_b200 import heatmap
+    from miowtion_b200 import kernels
+    if int(os.environ.get('WORLD_SIZE', '1')) != 1 or args.gpus != 1:
+        raise SystemExit('cfg5 runs on one GPU')
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    student, clip, plan, _ = build_student(cfg, device)
+    q, k, v = synthetic_qkv(cfg, cfg['seq_len'], 0, device)
+    gen = torch.Generator(device=device).manual_seed(cfg['dout_seed'])
+    dout = torch.randn(q.shape, generator=gen, device=device).to(
+        torch.bfloat16)
+    scale = 128 ** -0.5
+    groups = plan.head_groups(0, device)
+    stream = torch.cuda.current_stream()
+    stage_ms = {'dense_fwd_lse': 0.0, 'heat': 0.0, 'student_fwd': 0.0,
+                'student_bwd': 0.0}
+
+    def step(qs, ks, vs, dos, timed):
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        marks[0].record(stream)
+        with torch.no_grad():
+            _, lse = kernels.dense_attention(qs, ks, vs, scale, True,
+                                             used=cfg['used'])
+            marks[1].record(stream)
+            heat_sum = 0.0
+            for g in groups:
+                tl = clip.get(g.shape)
+                lse_t = tiling.gather_lse(lse, tl, g.heads)
+                qt = tiling.gather_tiles(qs, tl, g.heads)
+                kt = tiling.gather_tiles(ks, tl, g.heads)
+                heat = heatmap.teacher_heat(
+                    qt, kt, lse_t, tl,
+                    torch.arange(tl.n_tiles, device=device), 'sum')
+                heat_sum = heat_sum + heat.sum()
+                del qt, kt, lse_t
+            marks[2].record(stream)
+        leaves = [t.detach().requires_grad_(True) for t in (qs, ks, vs)]
+        with torch.enable_grad():
+            out = student(*leaves, 0)
+            marks[3].record(stream)
+            out.backward(dos)
+        marks[4].record(stream)
+        if timed:
+            torch.cuda.synchronize()
+            for i, n in enumerate(stage_ms):
+                stage_ms[n] += marks[i].elapsed_time(marks[i + 1])
+        return heat_sum + leaves[0].grad.float().abs().sum() * 0
+
+    for _ in range(args.warmup):
+        step(q, k, v, dout, False)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        start.record(stream)
+        clocks.mark('t0')
+        for _ in range(args.steps):
+            step(q, k, v, dout, False)
+        stop.record(stream)
+        torch.cuda.synchronize()
+        clocks.mark('t1')
+    ms = start.elapsed_time(stop) / args.steps
+    # Stage split (separate, synchronised passes).
+    for _ in range(2):
+        step(q, k, v, dout, True)
+    stages = {n: t / 2 for n, t in stage_ms.items()}
+    # End to end: H2D of this step's q, k, v, dO from pinned memory, the
+    # step, D2H of its scalar result.
+    host = [t.cpu().pin_memory() for t in (q, k, v, dout)]
+    dev_in = [torch.empty_like(t) for t in (q, k, v, dout)]
+    res_host = torch.empty((), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 5))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        for d, h in zip(dev_in, host):
+            d.copy_(h, non_blocking=True)
+        res_host.copy_(step(*dev_in, False), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    # Algorithmic work (counted after timing).
+    blocks = 0
+    with torch.no_grad():
+        for g in groups:
+            tl = clip.get(g.shape)
+            _, fq = tiling.gather_and_pool(q, tl, g.heads)
+            _, fk = tiling.gather_and_pool(k, tl, g.heads)
+            logits = student.predictor.layers[0](fq, fk, g.heads)
+            lists = veda_mask.select_block_lists(
+                logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
+            blocks += int(lists.part_cnt.sum() + lists.full_cnt.sum())
+    used, heads = cfg['used'], cfg['heads']
+    n_tiles = sum(clip.get(g.shape).n_tiles * g.heads.numel()
+                  for g in groups)  # query tiles x heads
+    heat_flops = sum(2.0 * (clip.get(g.shape).n_tiles * 128) ** 2 * 128 *
+                     g.heads.numel() for g in groups)
+    dense_flops = 4.0 * used ** 2 * 128 * heads
+    sparse_flops = 3.5 * blocks * BLOCK_FLOPS  # fwd + bwd (2.5x fwd)
+    total = dense_flops + heat_flops + sparse_flops
+    peaks = load_peaks()
+    peak = peaks['bf16_tflops']
+    line = {
+        'metric': METRIC, 'value': ms, 'unit': 'ms/step', 'n_gpus': 1,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+        'higher_is_better': False, 'scaling': 'strong', 'vs_baseline': None,
+        'dtype': 'bf16',
+        'data': 'synthetic (seeded N(0,1) q/k/v and dO, random-init '
+                'predictor N(0,0.02))',
+        'config': {'workload': f'{args.config}: {cfg["desc"]}',
+                   'heads': heads, 'seq_len': cfg['seq_len'],
+                   'head_dim': 128, 'parallelism': 'single GPU',
+                   'l2': 'inputs exceed L2 (q/k/v >> 126 MB)'},
+        'stages_ms': stages,
+        'computed_blocks': blocks,
+        'algorithmic_tflop': total / 1e12,
+        'effective_tflops': total / (ms * 1e-3) / 1e12,
+        'frac_of_peak': total / (ms * 1e-3) / 1e12 / peak,
+        'stage_tflops': {
+            'dense_fwd_lse': dense_flops / stages['dense_fwd_lse'] / 1e9,
+            'heat': heat_flops / stages['heat'] / 1e9,
+            'student_bwd_attention_equiv': 2.5 * blocks * BLOCK_FLOPS /
+                                           stages['student_bwd'] / 1e9},
+        'roofline': {
+            'bound': 'tensor', 'kernel': 'bsa_fwd_kernel (dense mode)',
+            'achieved': dense_flops / stages['dense_fwd_lse'] / 1e9,
+            'peak': peak, 'unit': 'TFLOP/s',
+            'frac': dense_flops / stages['dense_fwd_lse'] / 1e9 / peak,
+            'traffic': None,
+            'peak_source': f'{peaks["source"]} bf16 burst'},
+        'e2e': {'value': e2e_ms, 'unit': 'ms/step', 'steps': e2e_steps,
+                'h2d_bytes_per_step': 4 * q.numel() * 2,
+                'd2h_bytes_per_step': 4},
+        # Ours per step: dense fwd; per group gather_lse, gather q, k, heat
+        # (4), student fwd gather+pool q, k, embed, logits, select, transposed
+        # lists, gather v, attention, scatter (9 + 1), backward gather dO,
+        # prep, dq, dkdv, scatter x3 (7).
+        'gpu_launches': args.steps * (1 + 21 * len(groups)),
+        'clocks': clocks.summary(),
+        'query_tile_heads': n_tiles,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def launches_per_step(plan, world):

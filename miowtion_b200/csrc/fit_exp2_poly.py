@@ -8,7 +8,7 @@ Remez exchange algorithm starting from Chebyshev extrema.
 
     python miowtion_b200/csrc/fit_exp2_poly.py
 
-prints the coefficients (as float32 hex literals for csrc/bsa_fwd.cu) and
+prints the coefficients (as float32 hex literals for csrc/exp2_poly.cuh) and
 the max relative error of the float32 Horner evaluation.
 """
 

@@ -17,20 +17,31 @@
 // even). Q of the item stays in shared memory; key tiles stream through a
 // 4-slot ring; S = Q K^T (8 SS MMAs, M=N=128, K=16) goes to one of four TMEM
 // buffers (512 columns), so the tensor core runs up to four blocks ahead of
-// the reduction. Warp w (0-7) reduces rows 32(w%4) .. +31 (its TMEM lanes)
-// over keys 64(w/4) .. +63 to one partial per block; warp 8 issues TMA; warp
-// 9 issues the MMAs (converged, elected lane) and, when a buffer comes back,
-// combines the eight partials and writes the block's heat. All waits are
-// bounded (common.cuh).
+// the reduction. Warp w (0-15) reduces rows 32(w%4) .. +31 (its TMEM lanes)
+// over keys 32(w/4) .. +31 to one partial per block; four such warps per
+// SMSP hide one another's latencies. For reduce='sum' (one exponential per
+// score, so the MUFU's 16 ex2 a clock per SM bound it) a quarter of the
+// exponentials run on the FMA pipes (exp2_poly.cuh). Warp 16 issues TMA,
+// warp 17 the MMAs (converged, elected lane), and warp 18 combines each
+// block's sixteen partials into its heat, off the other two warps' paths.
+// All waits are bounded (common.cuh).
 #include <math.h>
 
 #include "common.cuh"
+#include "exp2_poly.cuh"
 
 namespace veda {
 
 namespace {
 
-constexpr int kHeatThreads = 320;
+constexpr int kWarps = 16;  // reduction warps
+constexpr int kProducerWarp = kWarps;
+constexpr int kMmaWarp = kWarps + 1;
+constexpr int kWriterWarp = kWarps + 2;
+constexpr int kHeatThreads = 32 * (kWarps + 3);
+// Of each warp's 32 columns, those whose exponential (reduce='sum') runs on
+// the FMA pipes.
+constexpr int kPolyCols = 8;
 constexpr int kSBufs = 4;
 constexpr int kRing = 4;
 constexpr uint32_t kTileBytes = 32768;
@@ -45,8 +56,9 @@ enum Bar {
   kKFull = 4,                  // [kRing]
   kKEmpty = kKFull + kRing,    // [kRing]
   kSFull = kKEmpty + kRing,    // [kSBufs]
-  kSFree = kSFull + kSBufs,    // [kSBufs] the 8 warps read S, wrote partials
-  kDrain = kSFree + kSBufs,
+  kSFree = kSFull + kSBufs,    // [kSBufs] the warps read S, wrote partials
+  kPartFree = kSFree + kSBufs,  // [kSBufs] the writer read the partials
+  kDrain = kPartFree + kSBufs,
   kNumBars
 };
 
@@ -84,8 +96,7 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
   uint8_t* s_q = smem;                      // [2]
   uint8_t* s_k = smem + 2 * kTileBytes;     // [kRing]
   float* s_part = reinterpret_cast<float*>(smem + (2 + kRing) * kTileBytes);
-  int64_t* s_dst = reinterpret_cast<int64_t*>(s_part + kSBufs * 8);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_dst + kSBufs);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_part + kSBufs * kWarps);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -95,11 +106,11 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
   const int n = p.n_tiles;
   if (tid == 0) {
     for (int b = 0; b < kNumBars; ++b)
-      mbar_init(&bars[b], (b >= kSFree && b < kSFree + kSBufs) ? 8 : 1);
+      mbar_init(&bars[b], (b >= kSFree && b < kSFree + kSBufs) ? kWarps : 1);
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tensor_map(&map_q);
@@ -159,29 +170,44 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
           mbar_wait(&bars[kKFull + k % kRing], (k / kRing) & 1, &never,
                     nullptr);
     }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer and heat writer ----------------
+  } else if (warp == kWriterWarp) {
+    // ---------------- heat writer ----------------
+    // Walks the same blocks as the other roles: block w of this CTA is key
+    // tile t of item it.
+    int64_t w = 0;
+    bool run = true;
+    for (int it = blockIdx.x; run && it < p.n_items; it += gridDim.x) {
+      for (int t = 0; t < n; ++t, ++w) {
+        const int sb = static_cast<int>(w % kSBufs);
+        if (!wait_all(&bars[kSFree + sb], (w / kSBufs) & 1, abort,
+                      p.status)) {
+          run = false;
+          break;
+        }
+        if (lane == 0) {
+          float v;
+          if (p.sum) {
+            v = 0.f;
+#pragma unroll
+            for (int i = 0; i < kWarps; ++i) v += s_part[sb * kWarps + i];
+          } else {
+            v = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < kWarps; ++i)
+              v = fmaxf(v, s_part[sb * kWarps + i]);
+            v = ex2_approx(v);  // partials are in log2 units
+          }
+          p.heat[static_cast<int64_t>(it) * n + t] = v;
+          mbar_arrive(&bars[kPartFree + sb]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = idesc_bf16(128, 128, false, false);
     const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
     const uint32_t k_lo = sw128_desc_lo(smem_u32(s_k), 16);
-    // Combines the partials of the block in S buffer sb into its heat.
-    auto write_heat = [&](int sb) {
-      if (lane == 0) {
-        float v;
-        if (p.sum) {
-          v = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) v += s_part[sb * 8 + w];
-        } else {
-          v = -INFINITY;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) v = fmaxf(v, s_part[sb * 8 + w]);
-          v = ex2_approx(v);  // partials are in log2 units
-        }
-        p.heat[s_dst[sb]] = v;
-      }
-      __syncwarp();
-    };
     int b = 0, ka = 0;
     bool run = true;
     for (int it = blockIdx.x; run && it < p.n_items; it += gridDim.x, ++ka) {
@@ -191,21 +217,18 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
       for (int t = 0; t < n; ++t, ++b) {
         const int sb = b % kSBufs;
         const int slot = b % kRing;
-        if (b >= kSBufs) {
-          if (!wait_all(&bars[kSFree + sb], ((b / kSBufs) - 1) & 1, abort,
-                        p.status)) {
-            run = false;
-            break;
-          }
-          write_heat(sb);
+        // S buffer sb is free once block b - kSBufs's partials are read.
+        if (b >= kSBufs && !wait_all(&bars[kPartFree + sb],
+                                     ((b / kSBufs) - 1) & 1, abort,
+                                     p.status)) {
+          run = false;
+          break;
         }
         if (!wait_all(&bars[kKFull + slot], (b / kRing) & 1, abort,
                       p.status)) {
           run = false;
           break;
         }
-        if (lane == 0)
-          s_dst[sb] = static_cast<int64_t>(it) * n + t;
         tc_fence_after();
         const uint32_t a = q_lo + qb * kTileUnits;
         const uint32_t bk = k_lo + slot * kTileUnits;
@@ -219,21 +242,14 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
         if (t == n - 1) umma_commit_warp(&bars[kQEmpty + qb]);
       }
     }
-    // The last blocks' heats.
-    for (int k = (b > kSBufs ? b - kSBufs : 0); run && k < b; ++k) {
-      const int sb = k % kSBufs;
-      if (!wait_all(&bars[kSFree + sb], (k / kSBufs) & 1, abort, p.status))
-        break;
-      write_heat(sb);
-    }
     if (*abort) {
       volatile int never = 0;
       umma_commit_warp(&bars[kDrain]);
       mbar_wait(&bars[kDrain], 0, &never, nullptr);
     }
   } else {
-    // ---------------- reduction warps 0-7 ----------------
-    const int half = warp / 4;
+    // ---------------- reduction warps 0-15 ----------------
+    const int kq = warp / 4;  // keys 32 kq .. 32 kq + 31 of each block
     const int quarter = warp % 4;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -248,6 +264,8 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
                          h * p.lse_sh] *
                        kLog2e
                  : 0.f;
+      const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 neg_l2 = make_float2(-l2, -l2);
       int kvalid_next = p.valid_count[0];
       for (int t = 0; t < n; ++t, ++b) {
         const int kvalid = kvalid_next;
@@ -259,33 +277,39 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t r[64];
-        const uint32_t t_s = tmem + sb * 128 + half * 64 + lane_base;
-        tmem_ld32(t_s, r);
-        tmem_ld32(t_s + 32, r + 32);
+        uint32_t r[32];
+        tmem_ld32(tmem + sb * 128 + kq * 32 + lane_base, r);
         tmem_wait_ld();
-        const int nk = kvalid - half * 64;  // valid keys among this 64
+        const int nk = kvalid - kq * 32;  // valid keys among these 32
         float v;
         if (p.sum) {
-          float a0 = 0.f, a1 = 0.f;
+          // Keys past the valid prefix (partial tiles only) score -inf.
+          if (nk < 32) {
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float s0 = c < nk ? round_bf16(__uint_as_float(r[c]))
-                                    : -INFINITY;
-            const float s1 = c + 1 < nk
-                                 ? round_bf16(__uint_as_float(r[c + 1]))
-                                 : -INFINITY;
-            a0 += ex2_approx(fmaf(s0, p.scale_log2, -l2));
-            a1 += ex2_approx(fmaf(s1, p.scale_log2, -l2));
+            for (int c = 0; c < 32; ++c)
+              if (c >= nk) r[c] = __float_as_uint(-INFINITY);
           }
-          v = row_ok ? a0 + a1 : 0.f;
+          float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            // Scores rounded to bf16 (the reference's bmm output dtype).
+            const float2 sr = __bfloat1622float2(__floats2bfloat162_rn(
+                __uint_as_float(r[c]), __uint_as_float(r[c + 1])));
+            const float2 x = __ffma2_rn(sr, scale2, neg_l2);
+            const float2 e = c >= 32 - kPolyCols
+                                 ? exp2_poly2(x)
+                                 : make_float2(ex2_approx(x.x),
+                                               ex2_approx(x.y));
+            acc = __fadd2_rn(acc, e);
+          }
+          v = row_ok ? acc.x + acc.y : 0.f;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1)
             v += __shfl_xor_sync(0xffffffffu, v, o);
         } else {
           float m = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
+          for (int c = 0; c < 32; ++c)
             if (c < nk) m = fmaxf(m, __uint_as_float(r[c]));
           // Rounding is monotone: the max of the rounded scores is the
           // rounded max.
@@ -296,7 +320,7 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
           for (int o = 16; o > 0; o >>= 1)
             v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
         }
-        if (lane == 0) s_part[sb * 8 + warp] = v;
+        if (lane == 0) s_part[sb * kWarps + warp] = v;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kSFree + sb]);
@@ -305,7 +329,7 @@ __global__ void __launch_bounds__(kHeatThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

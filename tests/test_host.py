@@ -110,8 +110,8 @@ def test_plan_groups_and_json(tmp_path):
 
 
 def test_fma_exp2_polynomial_error_bound():
-    """The cubic the attention kernel evaluates on the FMA pipes (the
-    exp2_poly2 helper of csrc/bsa_fwd.cu) stays within 1e-4 relative error of
+    """The cubic the attention and heat kernels evaluate on the FMA pipes
+    (exp2_poly2 of csrc/exp2_poly.cuh) stays within 1e-4 relative error of
     2^x over the softmax's argument range, emulated in float32 exactly as the
     kernel computes it."""
     import os
@@ -121,7 +121,7 @@ def test_fma_exp2_polynomial_error_bound():
     csrc = os.path.join(here, 'miowtion_b200', 'csrc')
     sys.path.insert(0, csrc)
     import fit_exp2_poly
-    src = open(os.path.join(csrc, 'bsa_fwd.cu')).read()
+    src = open(os.path.join(csrc, 'exp2_poly.cuh')).read()
     body = src[src.index('float2 exp2_poly2'):]
     lits = re.findall(r'(0x1\.[0-9a-f]+p-?\d+)f', body)[:8:2]
     c3, c2, c1, c0 = (float.fromhex(x) for x in lits)
