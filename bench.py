@@ -6,9 +6,14 @@
 
 One step = one Veda attention layer forward over synthetic q, k, v already
 resident in HBM: permute + pool q/k/v, predictor logits, budgeted top-k
-lists, tcgen05 block-sparse attention, inverse permutation. With N > 1 the
-heads are split over the ranks by a Ulysses all-to-all from the
-sequence-sharded layout (strong scaling: the layer is fixed, N grows).
+lists, tcgen05 block-sparse attention, inverse permutation. With N > 1:
+  --parallel clips    every rank runs the layer on its own clip (the
+                      reference's one-clip-per-GPU data parallelism, no
+                      collective on the data path; weak scaling, the value
+                      is ms per layer of the whole job); default for cfg2;
+  --parallel ulysses  one clip, heads split over the ranks by an all-to-all
+                      from the sequence-sharded layout (BASELINE configs 3
+                      and 4; strong scaling); default for cfg3 and cfg4.
 Prints one JSON line on rank 0.
 """
 
@@ -46,6 +51,7 @@ BLOCK_FLOPS = 4 * 128 * 128 * 128  # QK^T + PV of one 128x128 block, fwd
 CONFIGS = {
     'cfg2': dict(desc='1xB200 fwd, 24 heads, grid (20,32,56)=35840 tokens, '
                       'tile 2x8x8, 280x280 tiles, 28 key tiles/row (90%)',
+                 parallel='clips',
                  heads=24, seq_len=35840, used=35840, target=(0, (20, 32, 56)),
                  cond=None, shapes=[(2, 8, 8)], head_shape=[0] * 24,
                  target_ratio=0.1, ref_ratio=None, seed=1),
@@ -117,10 +123,10 @@ def predictor_for(cfg, device):
     return pred.to(device)
 
 
-def synthetic_qkv(cfg, rows, row0, device):
+def synthetic_qkv(cfg, rows, row0, device, clip=0):
     """q, k, v rows [row0, row0+rows) of ~N(0,1) bf16 [S, H, 128], drawn
     per 4096-row chunk from a seeded device generator (so every rank draws
-    the same global tensors)."""
+    the same global tensors); `clip` > 0 draws a different clip."""
     heads = cfg['heads']
     out = []
     for t in range(3):
@@ -128,7 +134,8 @@ def synthetic_qkv(cfg, rows, row0, device):
         chunk = 4096
         for c0 in range(row0 - row0 % chunk, row0 + rows, chunk):
             gen = torch.Generator(device=device)
-            gen.manual_seed(cfg['seed'] * 1_000_003 + t * 7919 + c0 // chunk)
+            gen.manual_seed(cfg['seed'] * 1_000_003 + t * 7919 + c0 // chunk
+                            + clip * 104_729)
             blk = torch.randn(chunk, heads, 128, generator=gen, device=device)
             lo, hi = max(c0, row0), min(c0 + chunk, row0 + rows)
             x[lo - row0:hi - row0] = blk[lo - c0:hi - c0].to(torch.bfloat16)
@@ -292,6 +299,9 @@ def main():
     ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--parallel', choices=['clips', 'ulysses'], default=None,
+                    help='multi-GPU mode (default: clips for cfg2, ulysses '
+                         'for cfg3/cfg4)')
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.impl == 'reference':
@@ -316,16 +326,23 @@ def main():
                                 timeout=datetime.timedelta(seconds=120))
 
     seq_len, heads = cfg['seq_len'], cfg['heads']
-    if heads % world or seq_len % world:
+    mode = args.parallel or cfg.get('parallel', 'ulysses')
+    heads_split = world > 1 and mode == 'ulysses'
+    if heads_split and (heads % world or seq_len % world):
         raise SystemExit('heads and sequence must divide by the GPU count')
     full_plan = veda_plan.TilePlan(
         'bench', cfg['target'][1],
         [tiling.TileShape(*s) for s in cfg['shapes']], [cfg['head_shape']])
-    plan = ulysses.local_plan(full_plan, rank, world) if world > 1 else None
+    plan = ulysses.local_plan(full_plan, rank, world) if heads_split else None
     student, clip, plan, local_heads = build_student(cfg, device, plan)
-    shard = seq_len // world
-    q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
-    fn = ulysses.UlyssesSparseStudent(student) if world > 1 else student
+    if heads_split:
+        shard = seq_len // world
+        q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
+        fn = ulysses.UlyssesSparseStudent(student)
+    else:
+        # The whole layer on this rank's own clip (clip 0 on one GPU).
+        q, k, v = synthetic_qkv(cfg, seq_len, 0, device, clip=rank)
+        fn = student
     events = veda_attention.StageEvents()
 
     def barrier():
@@ -358,11 +375,11 @@ def main():
         blocks = 0
         for group in plan.head_groups(0, device):
             tl = clip.get(group.shape)
-            qt, fq = tiling.gather_and_pool(q if world == 1 else
-                                            ulysses.seq_to_heads(q), tl,
+            qt, fq = tiling.gather_and_pool(ulysses.seq_to_heads(q)
+                                            if heads_split else q, tl,
                                             group.heads)
-            kt, fk = tiling.gather_and_pool(k if world == 1 else
-                                            ulysses.seq_to_heads(k), tl,
+            kt, fk = tiling.gather_and_pool(ulysses.seq_to_heads(k)
+                                            if heads_split else k, tl,
                                             group.heads)
             logits = student.predictor.layers[0](fq, fk, group.heads)
             lists = veda_mask.select_block_lists(
@@ -400,24 +417,32 @@ def main():
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
         vals = torch.cat([mx, tot])
     ms, e2e_ms, attn_ms, total_blocks = vals.tolist()
+    # Clips mode: `world` layers ran in the max-over-ranks time, so the whole
+    # job spends ms / world per layer.
+    layers = 1 if heads_split else world
+    step_ms = ms
+    ms, e2e_ms = ms / layers, e2e_ms / layers
     if rank == 0:
         peaks = load_peaks()
         peak = peaks['bf16_tflops']
         flops = total_blocks * BLOCK_FLOPS
-        dense_flops = 4.0 * cfg['used'] ** 2 * 128 * heads
-        eff = flops / (ms * 1e-3) / 1e12
+        dense_flops = 4.0 * cfg['used'] ** 2 * 128 * heads * layers
+        eff = flops / (ms * layers * 1e-3) / 1e12
         attn_tflops = (flops / world) / (attn_ms * 1e-3) / 1e12
         clk = clocks.summary()
         line = {
             'metric': METRIC, 'value': ms, 'unit': 'ms/layer',
             'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
-            'ms_per_step': ms, 'higher_is_better': False,
-            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16',
+            'ms_per_step': step_ms, 'higher_is_better': False,
+            'scaling': 'strong' if heads_split or world == 1 else 'weak',
+            'vs_baseline': None, 'dtype': 'bf16',
             'data': 'synthetic (seeded N(0,1) q/k/v, random-init predictor '
                     'N(0,0.02))',
             'config': {'workload': f'{args.config}: {cfg["desc"]}',
                        'heads': heads, 'seq_len': seq_len, 'head_dim': 128,
-                       'parallelism': f'ulysses-heads x{world}',
+                       'parallelism': (f'ulysses-heads x{world}'
+                                       if heads_split else
+                                       f'clip per GPU x{world}'),
                        'l2': 'inputs exceed L2 (q/k/v/tiles >> 126 MB)'},
             'effective_tflops': eff,
             'frac_of_peak': eff / peak,
@@ -429,9 +454,11 @@ def main():
                 'achieved': attn_tflops, 'peak': peak, 'unit': 'TFLOP/s',
                 'frac': attn_tflops / peak, 'traffic': None,
                 'peak_source': f'{peaks["source"]} bf16 burst'},
+            # Bytes of all ranks per step (each rank copies its q, k, v in
+            # and its output back).
             'e2e': {'value': e2e_ms, 'unit': 'ms/layer', 'steps': e2e_steps,
-                    'h2d_bytes_per_step': 3 * q.numel() * 2,
-                    'd2h_bytes_per_step': q.numel() * 2},
+                    'h2d_bytes_per_step': world * 3 * q.numel() * 2,
+                    'd2h_bytes_per_step': world * q.numel() * 2},
             'gpu_launches': args.steps * launches_per_step(plan, world),
             'clocks': clk,
         }
