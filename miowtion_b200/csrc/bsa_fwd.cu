@@ -22,14 +22,16 @@
 //              writes its P (bf16 pairs) over the first 16 columns of its
 //              own 32 columns of S. Four warps per SMSP hide one another's
 //              latencies.
-//   warp 16    TMA producer: Q of each item (two buffers), and K(b), V(b-2)
-//              through a 4-slot ring in the MMA warp's order, each K with a
-//              record of its block for the MMA warp.
-//   warp 17    TMEM owner and tcgen05.mma issuer (converged warp, elected
-//              lane issues): QK(0), QK(1), then QK(b), PV(b-2) for b >= 2.
-// Tensor-core instructions of one warp execute in issue order: QK(b+3) may
-// overwrite S while nothing waits for PV(b) (issued earlier, it has read P
-// first). Each block runs
+//   warp 16    TMA producer: Q of each item (two buffers), K(b) and V(b)
+//              through two 2-slot rings, each tile with a record of its block
+//              for the warp that consumes it.
+//   warp 17    QK issuer and TMEM owner: S(b) = Q K(b)^T once K(b) landed
+//              and S[b % 3] is free (PV(b-3) finished).
+//   warp 18    PV issuer: O += P(b) V(b) as the softmax writes P(b).
+// Both issuers run converged with the elected lane issuing. Split this way,
+// neither waits on the other's dependencies: the QK stream runs ahead while
+// the PV stream waits for the softmax, and the tensor core takes MMAs from
+// both. Each block runs
 //     S = Q K^T          8 SS MMAs (M=N=128, K=16), 128B-swizzled K-major
 //     P = exp2(S*c - m)  online softmax, lazy rescaling (the max moves only
 //                        when it grows by more than 2^8), a quarter of the
@@ -51,9 +53,10 @@ namespace {
 
 constexpr int kSoftmaxWarps = 16;
 constexpr int kProducerWarp = kSoftmaxWarps;
-constexpr int kMmaWarp = kSoftmaxWarps + 1;
-constexpr int kFwdThreads = 32 * (kSoftmaxWarps + 2);
-constexpr int kRing = 4;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;  // QK issuer, TMEM owner
+constexpr int kPvWarp = kSoftmaxWarps + 2;
+constexpr int kFwdThreads = 32 * (kSoftmaxWarps + 3);
+constexpr int kRing = 2;  // per K and V ring
 constexpr uint32_t kTileBytes = 32768;  // 128 x 128 bf16
 constexpr uint32_t kHalfBytes = 16384;  // 128 x 64 bf16 (one TMA box)
 constexpr uint32_t kTmemCols = 512;
@@ -63,7 +66,7 @@ constexpr int kListCap = 1024;
 // Exchange between the four warps of a row: partial maxima [block parity][4
 // key quarters][128 rows] and partial sums [4 key quarters][128 rows].
 constexpr int kExchangeFloats = 2 * 4 * 128 + 4 * 128;
-constexpr int kSmemBytes = (2 + kRing) * kTileBytes + kListCap * 4 +
+constexpr int kSmemBytes = (2 + 2 * kRing) * kTileBytes + kListCap * 4 +
                            kExchangeFloats * 4 + 512 + 1024;
 
 // Of each warp's 32 columns, those whose exponential runs on the FMA pipes.
@@ -77,16 +80,19 @@ constexpr int kSBufs = 3;
 enum Bar {
   kQFull = 0,       // [2] per Q buffer (item parity)
   kQEmpty = 2,      // [2] the item's last QK finished reading Q
-  kRingFull = 4,    // [kRing]
-  kRingEmpty = 8,   // [kRing]
+  kKFull = 4,       // [kRing] K tile (and its record) landed
+  kKEmpty = 6,      // [kRing] its QK finished
+  kVFull = 8,       // [kRing] V tile (and its record) landed
+  kVEmpty = 10,     // [kRing] its PV finished
   kSFull = 12,      // [3] per S buffer
   kPFull0 = 15,     // [3] P of keys 0-63 written (warps 0-7)
   kPFull1 = 18,     // [3] P of keys 64-127 written (warps 8-15)
   kPVDone = 21,     // [3] the block's PV finished (per S buffer)
   kODone = 24,      // the item's last PV finished
   kOFree = 25,      // the epilogue has read O (16 warps)
-  kDrain = 26,      // MMAs in flight after an abort
-  kNumBars = 27
+  kDrainQk = 26,    // MMAs in flight after an abort, per issuer
+  kDrainPv = 27,
+  kNumBars = 28
 };
 
 struct FwdParams {
@@ -308,25 +314,6 @@ __device__ __forceinline__ uint32_t block_record(const Block& b) {
          (b.ka >= 1 ? kRecLater : 0u);
 }
 
-// Waits for two phases: one probe of both (non-blocking test_wait, the two
-// tests independent so their latencies overlap), bounded waits if either is
-// still open.
-__device__ __forceinline__ bool wait_both(uint64_t* a, uint32_t pa, uint64_t* b,
-                                          uint32_t pb, volatile int* abort,
-                                          unsigned int* status) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred x, y; "
-      "mbarrier.test_wait.parity.shared::cta.b64 x, [%1], %2; "
-      "mbarrier.test_wait.parity.shared::cta.b64 y, [%3], %4; "
-      "and.pred x, x, y; selp.u32 %0, 1, 0, x; }"
-      : "=r"(ok)
-      : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb)
-      : "memory");
-  if (__all_sync(0xffffffffu, ok != 0)) return true;
-  return wait_all(a, pa, abort, status) && wait_all(b, pb, abort, status);
-}
-
 __global__ void __launch_bounds__(kFwdThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_k,
@@ -334,16 +321,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* s_q = smem;                      // [2] x 32 KB (item parity)
-  uint8_t* s_ring = smem + 2 * kTileBytes;  // [kRing] x 32 KB
+  uint8_t* s_q = smem;                           // [2] x 32 KB (item parity)
+  uint8_t* s_k = smem + 2 * kTileBytes;          // [kRing] x 32 KB
+  uint8_t* s_v = s_k + kRing * kTileBytes;       // [kRing] x 32 KB
   int32_t* s_list =
-      reinterpret_cast<int32_t*>(smem + (2 + kRing) * kTileBytes);
+      reinterpret_cast<int32_t*>(smem + (2 + 2 * kRing) * kTileBytes);
   float* s_xchg = reinterpret_cast<float*>(s_list + kListCap);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_xchg + kExchangeFloats);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   static_assert(kNumBars + 1 <= 32, "barriers overlap the block records");
-  volatile uint32_t* s_rec = reinterpret_cast<volatile uint32_t*>(bars + 32);
+  // Block records beside the K and the V ring slots.
+  volatile uint32_t* k_rec = reinterpret_cast<volatile uint32_t*>(bars + 32);
+  volatile uint32_t* v_rec = k_rec + kRing;
 
   const int tid = threadIdx.x;
   const int warp = tid / 32;
@@ -370,10 +360,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == kProducerWarp) {
     // ---------------- TMA producer (one warp) ----------------
-    // Loads in the MMA warp's order: K(0), K(1), then K(b), V(b-2) for
-    // b >= 2, then the end record and V of the last two blocks; Q of an item
-    // before its first K. The whole warp walks the stream (it copies each item's list
-    // to shared memory) and waits converged; lane 0 issues the copies.
+    // K(b) through the K ring, V(b) through the V ring, V two blocks behind
+    // K (the PV of a block trails its QK by the softmax); Q of an item
+    // before its first K; end records after the last tiles. The whole warp
+    // walks the stream (it copies each item's list to shared memory) and
+    // waits converged; lane 0 issues the copies.
     if (lane == 0) {
       prefetch_tensor_map(&map_q);
       prefetch_tensor_map(&map_k);
@@ -381,27 +372,38 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     Stream st;
     st.init(p, blockIdx.x, gridDim.x, false);
-    int pos = 0;       // ring positions used
-    int q_issued = 0;  // items whose Q was loaded
-    // Key tile and head of blocks b - 1 and b - 2.
+    int nk = 0, nv = 0;  // K and V tiles loaded
+    int q_issued = 0;    // items whose Q was loaded
+    // Key tile, head and record of blocks b - 1 and b - 2.
     int kv1 = 0, h1 = 0, kv2 = 0, h2 = 0;
-    int n_blocks = 0;
+    uint32_t r1 = 0, r2 = 0;
     bool run = true;
-    // Waits until the ring slot of `pos` is free; -1 on abort.
-    auto ring_slot = [&]() -> int {
-      const int slot = pos % kRing;
-      if (pos >= kRing &&
-          !wait_all(&bars[kRingEmpty + slot], ((pos / kRing) - 1) & 1, abort,
-                    p.status))
+    // Waits for a free slot of a ring (n tiles loaded so far); -1 on abort.
+    auto slot_of = [&](int n, int empty_bar) -> int {
+      const int slot = n % kRing;
+      if (n >= kRing && !wait_all(&bars[empty_bar + slot],
+                                  ((n / kRing) - 1) & 1, abort, p.status))
         return -1;
       return slot;
     };
-    auto load_tile = [&](const CUtensorMap* map, int slot, int h, int kv) {
-      uint8_t* dst = s_ring + slot * kTileBytes;
-      mbar_arrive_expect_tx(&bars[kRingFull + slot], kTileBytes);
-      tma_load_3d(dst, map, &bars[kRingFull + slot], 0, h, kv * kTile);
-      tma_load_3d(dst + kHalfBytes, map, &bars[kRingFull + slot], 64, h,
+    auto load = [&](const CUtensorMap* map, uint8_t* ring, int full_bar,
+                    int slot, int h, int kv) {
+      uint8_t* dst = ring + slot * kTileBytes;
+      mbar_arrive_expect_tx(&bars[full_bar + slot], kTileBytes);
+      tma_load_3d(dst, map, &bars[full_bar + slot], 0, h, kv * kTile);
+      tma_load_3d(dst + kHalfBytes, map, &bars[full_bar + slot], 64, h,
                   kv * kTile);
+    };
+    auto load_v = [&](int h, int kv, uint32_t rec) -> bool {
+      const int slot = slot_of(nv, kVEmpty);
+      if (slot < 0) return false;
+      if (lane == 0) {
+        v_rec[slot] = rec;
+        load(&map_v, s_v, kVFull, slot, h, kv);
+      }
+      __syncwarp();
+      ++nv;
+      return true;
     };
     while (st.valid(p)) {
       const Block b = st.flags();
@@ -430,52 +432,49 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int kv = p.dense ? st.j
                              : (st.len <= kListCap ? s_list[st.j]
                                                    : st.kv_global(p, st.j));
-      int slot = ring_slot();
+      const uint32_t rec = block_record(b);
+      const int slot = slot_of(nk, kKEmpty);
       if (slot < 0) {
         run = false;
         break;
       }
       if (lane == 0) {
-        s_rec[slot] = block_record(b);
-        load_tile(&map_k, slot, b.h, kv);
+        k_rec[slot] = rec;
+        load(&map_k, s_k, kKFull, slot, b.h, kv);
       }
       __syncwarp();
-      ++pos;
-      if (n_blocks >= 2) {
-        slot = ring_slot();
-        if (slot < 0) {
-          run = false;
-          break;
-        }
-        if (lane == 0) load_tile(&map_v, slot, h2, kv2);
-        __syncwarp();
-        ++pos;
+      ++nk;
+      if (nk >= 3 && !load_v(h2, kv2, r2)) {
+        run = false;
+        break;
       }
       kv2 = kv1;
       h2 = h1;
+      r2 = r1;
       kv1 = kv;
       h1 = b.h;
-      ++n_blocks;
+      r1 = rec;
       st.next_block(p);
     }
     if (run) {
-      // The end record completes its slot's full barrier without a copy.
-      int slot = ring_slot();
+      // The last V tiles, then an end record in each ring (completing the
+      // slot's full barrier without a copy).
+      if (nk >= 2) run = load_v(h2, kv2, r2);
+      if (run && nk >= 1) run = load_v(h1, kv1, r1);
+      int slot = run ? slot_of(nk, kKEmpty) : -1;
       if (slot >= 0) {
         if (lane == 0) {
-          s_rec[slot] = kRecEnd;
-          mbar_arrive(&bars[kRingFull + slot]);
+          k_rec[slot] = kRecEnd;
+          mbar_arrive(&bars[kKFull + slot]);
         }
         __syncwarp();
-        ++pos;
-        for (int k = n_blocks >= 2 ? 2 : n_blocks; k >= 1 && slot >= 0; --k) {
-          slot = ring_slot();
-          if (slot >= 0) {
-            if (lane == 0)
-              load_tile(&map_v, slot, k == 2 ? h2 : h1, k == 2 ? kv2 : kv1);
-            __syncwarp();
-            ++pos;
+        slot = slot_of(nv, kVEmpty);
+        if (slot >= 0) {
+          if (lane == 0) {
+            v_rec[slot] = kRecEnd;
+            mbar_arrive(&bars[kVFull + slot]);
           }
+          __syncwarp();
         }
       }
     }
@@ -485,78 +484,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int ka = q_issued - 2; ka < q_issued; ++ka)
         if (ka >= 0)
           mbar_wait(&bars[kQFull + (ka & 1)], (ka >> 1) & 1, &never, nullptr);
-      for (int k = pos - kRing; k < pos; ++k)
+      for (int k = nk - kRing; k < nk; ++k)
         if (k >= 0)
-          mbar_wait(&bars[kRingFull + k % kRing], (k / kRing) & 1, &never,
+          mbar_wait(&bars[kKFull + k % kRing], (k / kRing) & 1, &never,
+                    nullptr);
+      for (int k = nv - kRing; k < nv; ++k)
+        if (k >= 0)
+          mbar_wait(&bars[kVFull + k % kRing], (k / kRing) & 1, &never,
                     nullptr);
     }
   } else if (warp == kMmaWarp) {
-    // ---------------- tcgen05.mma issuer ----------------
+    // ---------------- QK issuer ----------------
     constexpr uint32_t idesc_qk = idesc_bf16(128, 128, false, false);
-    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
     // Descriptor low halves; per step only a constant is added (16-byte
     // units): K-major steps advance 32 B inside a 128-B swizzle row and
-    // jump to the second 64-column box after four steps; V steps advance
-    // 16 key rows (2 KB).
+    // jump to the second 64-column box after four steps.
     const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
-    const uint32_t k_lo = sw128_desc_lo(smem_u32(s_ring), 16);
-    const uint32_t v_lo = sw128_desc_lo(smem_u32(s_ring), kHalfBytes);
+    const uint32_t k_lo = sw128_desc_lo(smem_u32(s_k), 16);
     constexpr uint32_t kTileUnits = kTileBytes >> 4;
-    const uint32_t t_o = tmem + kSBufs * 128;
-    int pos = 0;       // ring positions consumed
-    uint32_t blk = 0;  // blocks whose QK was issued
-    uint32_t r1 = 0, r2 = 0;  // records of blocks blk - 1 and blk - 2
-    // PV(b) with its block's record: V in the next ring slot, P in
-    // S[b % 3].
-    auto issue_pv = [&](uint32_t b, uint32_t rec) -> bool {
+    for (uint32_t b = 0;; ++b) {
+      const int slot = b % kRing;
+      if (!wait_all(&bars[kKFull + slot], (b / kRing) & 1, abort, p.status))
+        break;
+      const uint32_t rec = k_rec[slot];
+      if (rec & kRecEnd) break;
       const uint32_t sb = b % kSBufs;
-      const uint32_t spar = (b / kSBufs) & 1;
-      const bool first = rec & kRecFirst;
-      const int vslot = pos % kRing;
-      // The item's first PV overwrites O: the epilogue must have read the
-      // previous item's.
-      if (first && (rec & kRecLater) &&
-          !wait_all(&bars[kOFree], (rec & kRecItem) ? 0u : 1u, abort,
-                    p.status))
-        return false;
-      if (!wait_both(&bars[kRingFull + vslot], (pos / kRing) & 1,
-                     &bars[kPFull0 + sb], spar, abort, p.status))
-        return false;
-      tc_fence_after();
-      const uint32_t bv = v_lo + vslot * kTileUnits;
-      const uint32_t t_p = tmem + sb * 128;
-      // P of key step kk (16 keys, 8 columns) lies in the first 16 columns
-      // of its key quarter's 32.
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
-                     idesc_pv, (kk > 0 || !first) ? 1u : 0u);
-      if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 4; kk < 8; ++kk)
-        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
-                     idesc_pv, 1u);
-      umma_commit_warp(&bars[kRingEmpty + vslot]);
-      umma_commit_warp(&bars[kPVDone + sb]);
-      if (rec & kRecLast) umma_commit_warp(&bars[kODone]);
-      ++pos;
-      return true;
-    };
-    while (true) {
-      const int slot = pos % kRing;
-      if (!wait_all(&bars[kRingFull + slot], (pos / kRing) & 1, abort,
-                    p.status))
-        break;
-      const uint32_t rec = s_rec[slot];
-      ++pos;
-      if (rec & kRecEnd) {
-        if (blk >= 2 && !issue_pv(blk - 2, r2)) break;
-        if (blk >= 1) issue_pv(blk - 1, r1);
-        break;
-      }
-      // QK(blk) into S[blk % 3].
       const uint32_t qb = (rec & kRecItem) ? 1u : 0u;
+      // S[sb] held P of block b - 3: its PV must have finished.
+      if (b >= kSBufs && !wait_all(&bars[kPVDone + sb],
+                                   ((b / kSBufs) - 1) & 1, abort, p.status))
+        break;
       if ((rec & kRecFirst) &&
           !wait_all(&bars[kQFull + qb], (rec & kRecQPhase) ? 1u : 0u, abort,
                     p.status))
@@ -564,26 +521,68 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_after();
       const uint32_t a = q_lo + qb * kTileUnits;
       const uint32_t b_ = k_lo + slot * kTileUnits;
-      const uint32_t sb = blk % kSBufs;
-      const uint32_t t_s = tmem + sb * 128;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-        umma_ss_warp(t_s, a + off, b_ + off, idesc_qk, kk > 0 ? 1u : 0u);
+        umma_ss_warp(tmem + sb * 128, a + off, b_ + off, idesc_qk,
+                     kk > 0 ? 1u : 0u);
       }
       umma_commit_warp(&bars[kSFull + sb]);
-      umma_commit_warp(&bars[kRingEmpty + slot]);
+      umma_commit_warp(&bars[kKEmpty + slot]);
       if (rec & kRecLast) umma_commit_warp(&bars[kQEmpty + qb]);
-      if (blk >= 2 && !issue_pv(blk - 2, r2)) break;
-      r2 = r1;
-      r1 = rec;
-      ++blk;
     }
     if (*abort) {
       // Let the MMAs in flight finish before TMEM is released.
       volatile int never = 0;
-      umma_commit_warp(&bars[kDrain]);
-      mbar_wait(&bars[kDrain], 0, &never, nullptr);
+      umma_commit_warp(&bars[kDrainQk]);
+      mbar_wait(&bars[kDrainQk], 0, &never, nullptr);
+    }
+  } else if (warp == kPvWarp) {
+    // ---------------- PV issuer ----------------
+    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
+    // V steps advance 16 key rows (2 KB) in the MN-major V tile.
+    const uint32_t v_lo = sw128_desc_lo(smem_u32(s_v), kHalfBytes);
+    constexpr uint32_t kTileUnits = kTileBytes >> 4;
+    const uint32_t t_o = tmem + kSBufs * 128;
+    for (uint32_t b = 0;; ++b) {
+      const int slot = b % kRing;
+      if (!wait_all(&bars[kVFull + slot], (b / kRing) & 1, abort, p.status))
+        break;
+      const uint32_t rec = v_rec[slot];
+      if (rec & kRecEnd) break;
+      const uint32_t sb = b % kSBufs;
+      const uint32_t spar = (b / kSBufs) & 1;
+      const bool first = rec & kRecFirst;
+      // The item's first PV overwrites O: the epilogue must have read the
+      // previous item's.
+      if (first && (rec & kRecLater) &&
+          !wait_all(&bars[kOFree], (rec & kRecItem) ? 0u : 1u, abort,
+                    p.status))
+        break;
+      if (!wait_all(&bars[kPFull0 + sb], spar, abort, p.status)) break;
+      tc_fence_after();
+      const uint32_t bv = v_lo + slot * kTileUnits;
+      const uint32_t t_p = tmem + sb * 128;
+      // P of key step kk (16 keys, 8 columns) lies in the first 16 columns
+      // of its key quarter's 32.
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
+                     idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+      if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 4; kk < 8; ++kk)
+        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
+                     idesc_pv, 1u);
+      umma_commit_warp(&bars[kVEmpty + slot]);
+      umma_commit_warp(&bars[kPVDone + sb]);
+      if (rec & kRecLast) umma_commit_warp(&bars[kODone]);
+    }
+    if (*abort) {
+      volatile int never = 0;
+      umma_commit_warp(&bars[kDrainPv]);
+      mbar_wait(&bars[kDrainPv], 0, &never, nullptr);
     }
   } else {
     // ---------------- softmax + epilogue (warps 0-15) ----------------
