@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
     python bench.py --impl reference ...   # the reference algorithm on CPU
     python bench.py --config cfg5 ...      # the stage-2 training step
+    python bench.py --only backward|heat   # one stage on one head group
 
 One step = one Veda attention layer forward over synthetic q, k, v already
 resident in HBM: permute + pool q/k/v, predictor logits, budgeted top-k
@@ -299,6 +300,11 @@ def main():
     ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--only', choices=['backward', 'heat'], default=None,
+                    help='time one stage on head group 0 of the config '
+                         '(for kernel profiling)')
+    ap.add_argument('--reduce', choices=['sum', 'max'], default='sum',
+                    help="heat reduction for --only heat")
     ap.add_argument('--parallel', choices=['clips', 'ulysses'], default=None,
                     help='multi-GPU mode (default: clips for cfg2, ulysses '
                          'for cfg3/cfg4)')
@@ -309,6 +315,9 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit('use at least 3 warm-up steps')
+    if args.only:
+        run_stage(args, cfg)
+        return
     if cfg.get('train'):
         run_train_step(args, cfg)
         return
@@ -474,6 +483,84 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_stage(args, cfg):
+    """One stage on one GPU, head group 0 of the config: the block-sparse
+    backward (prep, dq, dk/dv) or the teacher heat for every query tile.
+    The line's unit is ms per call of that stage."""
+    from miowtion_b200 import heatmap
+    from miowtion_b200 import kernels
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    student, clip, plan, _ = build_student(cfg, device)
+    q, k, v = synthetic_qkv(cfg, cfg['seq_len'], 0, device)
+    group = plan.head_groups(0, device)[0]
+    tl = clip.get(group.shape)
+    heads = group.heads.numel()
+    if args.only == 'backward':
+        qt, fq = tiling.gather_and_pool(q, tl, group.heads)
+        kt, fk = tiling.gather_and_pool(k, tl, group.heads)
+        vt = tiling.gather_tiles(v, tl, group.heads)
+        del q, k, v
+        with torch.no_grad():
+            logits = student.predictor.layers[0](fq, fk, group.heads)
+            lists = veda_mask.select_block_lists(
+                logits[:, :tl.n_video_tiles], tl, clip.blocks(tl),
+                want_mask=True)
+        t_lists = kernels.index_lists_from_mask(lists.mask, tl)
+        out, lse = kernels.block_sparse_attention_lists(qt, kt, vt, lists, tl,
+                                                        return_lse=True)
+        gen = torch.Generator(device=device).manual_seed(cfg.get('dout_seed',
+                                                                 4))
+        dout = torch.randn(qt.shape, generator=gen, device=device).to(
+            torch.bfloat16)
+        blocks = int((lists.part_cnt.long() + lists.full_cnt.long()).sum())
+        flops = 2.5 * blocks * BLOCK_FLOPS
+
+        def call():
+            kernels.block_sparse_attention_bwd(qt, kt, vt, out, dout, lse,
+                                               lists, t_lists, tl)
+        what = 'block-sparse backward (prep + dq + dk/dv)'
+    else:
+        with torch.no_grad():
+            _, lse = kernels.dense_attention(q, k, v, 128 ** -0.5, True,
+                                             used=cfg['used'])
+        lse_t = tiling.gather_lse(lse, tl, group.heads)
+        qt = tiling.gather_tiles(q, tl, group.heads)
+        kt = tiling.gather_tiles(k, tl, group.heads)
+        del q, k, v, lse
+        rows = torch.arange(tl.n_tiles, device=device)
+        blocks = tl.n_tiles ** 2 * heads
+        flops = 2.0 * blocks * 128 ** 3
+
+        def call():
+            heatmap.teacher_heat(qt, kt, lse_t, tl, rows, args.reduce)
+        what = f'teacher heat (reduce={args.reduce}), all query tiles'
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        call()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    peaks = load_peaks()
+    print(json.dumps({
+        'metric': f'{args.only} ms per call', 'value': ms, 'unit': 'ms',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': False, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': f'{args.config} head group 0 ({heads} heads, '
+                               f'{tl.n_tiles} tiles): {what}'},
+        'blocks': blocks,
+        'tflops': flops / (ms * 1e-3) / 1e12,
+        'frac_of_peak': flops / (ms * 1e-3) / 1e12 / peaks['bf16_tflops'],
+        'flops_accounting': ('2.5 x the forward per computed block (the '
+                             "reference's)" if args.only == 'backward' else
+                             '2 x 128^3 per block of QK^T')}), flush=True)
 
 
 def run_train_step(args, cfg):
