@@ -273,8 +273,12 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* out, int64_t o_sn,
 }
 
 // ---------------------------------------------------------------------------
-// dq: query-major. TMEM: S [0,128) (dS over its columns 0-31 and 64-95),
-// dP [128,256), dQ [256,384).
+// dq: query-major. TMEM: S [0,128), dP [128,256), dQ [256,384), and dS
+// (bf16 pairs, 64 columns) double-buffered at [384,448) and [448,512). The
+// compute warps free S and dP as soon as they have read them, so the MMA
+// warp issues S and dP of block j+1 ahead of dQ of block j and the tensor
+// core works through block j's elementwise phase; at an item's end dQ goes
+// first so the epilogue is not held up.
 // ---------------------------------------------------------------------------
 enum DqBar {
   kQFull = 0,      // Q and dO of the item landed
@@ -282,8 +286,10 @@ enum DqBar {
   kKvFull,         // [2] K and V of the block landed (stage = block parity)
   kKvEmpty = kKvFull + 2,  // [2] the block's MMAs finished reading them
   kSdFull = kKvEmpty + 2,  // S and dP of the block
+  kSdFree,         // the compute warps have read S and dP (8 warps)
   kDsFull,         // dS written (8 warps)
-  kDqDone,         // the item's last dQ MMA finished
+  kDsBufFree,      // [2] the dQ MMA of the block last using the dS buffer
+  kDqDone = kDsBufFree + 2,  // the item's last dQ MMA finished
   kDqFree,         // the epilogue has read dQ (8 warps)
   kDqDrain,
   kDqItemFull,                       // [kQueue]
@@ -316,9 +322,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int lane = tid % 32;
   if (tid == 0) {
     for (int b = 0; b < kDqNumBars; ++b)
-      mbar_init(&bars[b], (b == kDsFull || b == kDqFree) ? 8
-                          : (b >= kDqItemEmpty)         ? kQueueReaders
-                                                        : 1);
+      mbar_init(&bars[b], (b == kSdFree || b == kDsFull || b == kDqFree) ? 8
+                          : (b >= kDqItemEmpty)                      ? kQueueReaders
+                                                                     : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -388,15 +394,51 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t kv_lo = sw128_desc_lo(smem_u32(s_kv), 16);
     const uint32_t kvmn_lo = sw128_desc_lo(smem_u32(s_kv), kHalfBytes);
     const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
+    const uint32_t t_ds = tmem + 384;  // [2] x 64 columns
+    // The block whose dQ MMAs are still to be issued.
+    struct Pending {
+      bool valid, first, last;
+      int ka, blk;
+    } prev{false, false, false, 0, 0};
+    // dQ += dS K of a block (dS in buffer blk & 1, K in stage blk & 1).
+    auto issue_dq = [&](const Pending& d) -> bool {
+      // The item's first dQ overwrites dQ: the epilogue must have read it.
+      if (d.first && d.ka > 0 &&
+          !wait_all(&bars[kDqFree], (d.ka - 1) & 1, abort, p.status))
+        return false;
+      if (!wait_all(&bars[kDsFull], d.blk & 1, abort, p.status)) return false;
+      tc_fence_after();
+      const int stage = d.blk & 1;
+      const uint32_t kmn = kvmn_lo + stage * 2 * kTileUnits;
+      const uint32_t t_a = t_ds + (d.blk & 1) * 64;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_ts_warp(t_dq, t_a + kk * 8, kmn + kk * 128, idesc_bmn,
+                     (kk > 0 || !d.first) ? 1u : 0u);
+      umma_commit_warp(&bars[kKvEmpty + stage]);
+      umma_commit_warp(&bars[kDsBufFree + (d.blk & 1)]);
+      if (d.last) umma_commit_warp(&bars[kDqDone]);
+      return true;
+    };
     ListStream st;
     st.init(&p.lists, &queue, false, false);
-    while (st.valid()) {
+    bool run = true;
+    while (run && st.valid()) {
       const bool first = st.j == 0, last = st.j == st.len - 1;
       const int ka = st.ka;
-      const int stage = st.blk & 1;
+      const int blk = st.blk;
+      const int stage = blk & 1;
+      // At an item's end, the last dQ before the next item's S and dP.
+      if (prev.valid && prev.last) {
+        if (!issue_dq(prev)) break;
+        prev.valid = false;
+      }
       if (first && !wait_all(&bars[kQFull], ka & 1, abort, p.status)) break;
-      if (!wait_all(&bars[kKvFull + stage], (st.blk >> 1) & 1, abort,
-                    p.status))
+      if (!wait_all(&bars[kKvFull + stage], (blk >> 1) & 1, abort, p.status))
+        break;
+      // S and dP of the previous block have been read.
+      if (blk > 0 &&
+          !wait_all(&bars[kSdFree], (blk - 1) & 1, abort, p.status))
         break;
       tc_fence_after();
       const uint32_t k_lo = kv_lo + stage * 2 * kTileUnits;
@@ -413,22 +455,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       umma_commit_warp(&bars[kSdFull]);
       if (last) umma_commit_warp(&bars[kQEmpty]);
-      // dQ += dS K: the first block of an item overwrites dQ, which the
-      // epilogue must have read.
-      if (first && ka > 0 &&
-          !wait_all(&bars[kDqFree], (ka - 1) & 1, abort, p.status))
-        break;
-      if (!wait_all(&bars[kDsFull], st.blk & 1, abort, p.status)) break;
-      tc_fence_after();
-      const uint32_t kmn = kvmn_lo + stage * 2 * kTileUnits;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_ts_warp(t_dq, t_s + packed_col(kk), kmn + kk * 128, idesc_bmn,
-                     (kk > 0 || !first) ? 1u : 0u);
-      umma_commit_warp(&bars[kKvEmpty + stage]);
-      if (last) umma_commit_warp(&bars[kDqDone]);
+      if (prev.valid && !issue_dq(prev)) break;
+      prev = Pending{true, first, last, ka, blk};
       st.next_block();
+      run = st.ok;
     }
+    if (run && prev.valid) issue_dq(prev);
     if (*abort) {
       volatile int never = 0;
       umma_commit_warp(&bars[kDqDrain]);
@@ -467,6 +499,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
+        // dS goes to buffer blk & 1, free once the dQ MMA of block blk - 2
+        // has finished.
+        if (blk >= 2 && !wait_all(&bars[kDsBufFree + (blk & 1)],
+                                  ((blk >> 1) - 1) & 1, abort, p.status)) {
+          ok = false;
+          break;
+        }
+        const uint32_t t_ds = tmem + 384 + (blk & 1) * 64 + lane_base;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int col0 = half * 64 + c * 32;
@@ -474,6 +514,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tmem_ld32(tmem + col0 + lane_base, s);
           tmem_ld32(tmem + 128 + col0 + lane_base, dp);
           tmem_wait_ld();
+          // Both of this block's S and dP reads are done: the MMA warp may
+          // overwrite them with the next block's.
+          if (c == 1) arrive_warp(&bars[kSdFree]);
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -488,9 +531,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             w[i] = pack_bf16(d2[0], d2[1]);
           }
-          // dS of these 32 keys over the first 16 of the 64 columns this
-          // warp owns (already read into registers).
-          tmem_st16(tmem + half * 64 + c * 16 + lane_base, w);
+          // dS of these 32 keys: bf16 pairs, 16 columns of the buffer
+          // (keys 0-63 in columns 0-31, keys 64-127 in 32-63).
+          tmem_st16(t_ds + half * 32 + c * 16, w);
         }
         tmem_wait_st();
         arrive_warp(&bars[kDsFull]);
