@@ -1,18 +1,22 @@
 """Tile plans: which tile shape every (layer, head) uses on one geometry.
 
-Mirror of the reference's `miowtion/veda/plan.py` data format (the JSON of
-`plans/**.json`) and its head grouping. Plan search is out of scope here;
-plans come from the reference's search or are built uniform.
+Mirror of the reference's `miowtion/veda/plan.py`: the JSON format of its
+released plans (`plans/released/*.json`), the head grouping, the mirrored and
+transposed plans and the plan table's selection rule. Plan search itself is
+the reference's (`veda/search.py`); plans come from it or are built uniform.
 """
 
 from __future__ import annotations
 
 import dataclasses
+import glob
 import json
 import os
+from collections.abc import Sequence
 
 import torch
 
+from miowtion_b200 import geometry as veda_geometry
 from miowtion_b200 import tiling
 
 
@@ -85,10 +89,96 @@ class TilePlan:
             return cls.from_json(json.load(f))
 
     @classmethod
-    def uniform(cls, geometry: str, grid: tuple[int, int, int],
+    def uniform(cls, geometry: veda_geometry.Geometry,
                 shape: tiling.TileShape, num_layers: int,
                 num_heads: int) -> TilePlan:
-        """Every head uses one shape (baseline / bootstrap plan)."""
-        return cls(geometry, tuple(grid), [shape],
+        """Every head uses one shape (plan.py:108-114)."""
+        return cls(geometry.name, tuple(geometry.video_grid), [shape],
                    [[0] * num_heads for _ in range(num_layers)],
                    {'source': 'uniform'})
+
+    def mirrored(self) -> TilePlan:
+        """The plan of the H<->W mirrored geometry (plan.py:116-138), e.g.
+        9x16_t37 from 16x9_t37: shapes and grid transposed, the mirrored
+        geometry's name, `mirrored_from` added to the provenance.
+
+        Raises:
+            ValueError: If the mirrored geometry's grid is not this grid
+                transposed (the canvas rounding differs).
+        """
+        aspect, latent_t = self.geometry.split('_t')
+        w, h = aspect.split('x')
+        mirror = veda_geometry.geometry_from_latent_t(f'{h}:{w}',
+                                                      int(latent_t))
+        t, grid_h, grid_w = self.grid
+        if tuple(mirror.video_grid) != (t, grid_w, grid_h):
+            raise ValueError(f'{mirror.name} grid {mirror.video_grid} is not '
+                             f'the transpose of {self.geometry} {self.grid}')
+        return TilePlan(mirror.name, (t, grid_w, grid_h),
+                        [s.transposed() for s in self.shapes],
+                        [list(r) for r in self.head_shape],
+                        {**self.provenance, 'mirrored_from': self.geometry})
+
+    def transposed(self) -> TilePlan:
+        """H<->W transposed plan named '<geometry>_T' (plan.py:140-146)."""
+        t, h, w = self.grid
+        return TilePlan(self.geometry + '_T', (t, w, h),
+                        [s.transposed() for s in self.shapes],
+                        [list(r) for r in self.head_shape],
+                        {**self.provenance, 'transposed_from': self.geometry})
+
+
+class PlanTable:
+    """All searched plans, keyed by geometry name (plan.py:149-188)."""
+
+    def __init__(self, plans: Sequence[TilePlan]):
+        self.plans = {p.geometry: p for p in plans}
+
+    @classmethod
+    def load_dir(cls, directory: str) -> PlanTable:
+        """Every `*.json` plan of a directory, in name order.
+
+        Raises:
+            FileNotFoundError: If the directory holds no plan.
+        """
+        paths = sorted(glob.glob(os.path.join(directory, '*.json')))
+        if not paths:
+            raise FileNotFoundError(f'no plans in {directory}')
+        return cls([TilePlan.load(p) for p in paths])
+
+    def select(self, geometry: veda_geometry.Geometry) -> TilePlan:
+        """The plan for a geometry, by the reference's rule (plan.py:160-188):
+
+        1. the geometry's own plan, if searched;
+        2. else the plan of the same aspect with the nearest latent_t (ties
+           to the shorter one; no interpolation);
+        3. else, only when no plan of this aspect exists, the mirrored
+           aspect's nearest plan or its transpose, whichever pads the
+           target grid less (the untransposed one on a tie).
+
+        Raises:
+            KeyError: If neither this aspect nor its mirror has a plan.
+        """
+        if geometry.name in self.plans:
+            return self.plans[geometry.name]
+
+        def aspect_of(p: TilePlan) -> str:
+            return p.geometry.split('_t')[0]
+
+        key = geometry.aspect.replace(':', 'x')
+        same = [p for p in self.plans.values() if aspect_of(p) == key]
+        if same:
+            return min(same, key=lambda p: (abs(p.grid[0] - geometry.latent_t),
+                                            p.grid[0]))
+        w, h = geometry.aspect.split(':')
+        mirror = [p for p in self.plans.values()
+                  if aspect_of(p) == f'{h}x{w}']
+        if not mirror:
+            raise KeyError(f'no plan for {geometry.name}')
+        nearest = min(mirror, key=lambda p: abs(p.grid[0] - geometry.latent_t))
+        grid = geometry.video_grid
+
+        def padded_tiles(p: TilePlan) -> int:
+            return sum(s.num_tiles(grid) for s in p.shapes)
+
+        return min((nearest, nearest.transposed()), key=padded_tiles)

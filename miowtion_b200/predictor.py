@@ -88,8 +88,6 @@ class LayerPredictor(nn.Module):
         if second_order_rank or count_term:
             raise NotImplementedError(
                 'second-order and count terms have no B200 kernel')
-        if head_dim != 128:
-            raise NotImplementedError('the predictor kernels take head_dim 128')
         self.head_dim = head_dim
         self.second_order_rank = 0
         self.proj_q = nn.Parameter(torch.empty(num_heads, 3 * head_dim,
@@ -101,7 +99,14 @@ class LayerPredictor(nn.Module):
 
     def forward(self, feats_q: torch.Tensor, feats_k: torch.Tensor,
                 heads: torch.Tensor) -> torch.Tensor:
-        """Block logits [H', n_q, n_k] fp32 (predictor.py:299-338)."""
+        """Block logits [H', n_q, n_k] fp32 (predictor.py:299-338).
+
+        Raises:
+            NotImplementedError: For a head_dim other than 128 (the scoring
+                kernel's only size; other sizes load and save, nothing more).
+        """
+        if self.head_dim != 128:
+            raise NotImplementedError('the predictor kernels take head_dim 128')
         return predict_logits(feats_q, feats_k, self.proj_q, self.proj_k,
                               heads)
 
