@@ -271,6 +271,25 @@ int veda_teacher_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                       int64_t n_q, int32_t reduce_sum, float* heat,
                       float softmax_scale, void* stream);
 
+/* ---- (f) tile search: oracle relative error ------------------------------- */
+
+/* Workspace bytes veda_rel_mse needs for n_rows sampled tiles and n_heads. */
+int64_t veda_rel_mse_workspace(int64_t n_rows, int32_t n_heads);
+
+/* The error step of the tile-search oracle, miowtion/veda/search.py:117-126
+ * (`_oracle_rel_mse_kernels`): per head h,
+ *   rel_mse[h] = sum ||o_sparse - o_dense||^2 / max(sum ||o_dense||^2, tiny)
+ * over the real rows of the sampled tiles. o_sparse [n_rows*128, H', 128]
+ * bf16 is the sparse output of the sampled query tiles (slot r*128 + i);
+ * seq_row[slot] is that slot's row in o_dense [S, H, 128] bf16, or -1 for a
+ * padding slot (skipped); head h of o_sparse is head heads[h] of o_dense.
+ * Deterministic (fixed reduction order). */
+int veda_rel_mse(const void* o_sparse, int64_t s_stride_n, int64_t s_stride_h,
+                 const void* o_dense, int64_t d_stride_s, int64_t d_stride_h,
+                 const int64_t* seq_row, const int64_t* heads, int64_t n_rows,
+                 int32_t n_heads, float* rel_mse, void* workspace,
+                 int64_t workspace_bytes, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* One 128x128x128 bf16 tcgen05 MMA per mode, for checking operand and

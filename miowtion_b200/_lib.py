@@ -88,6 +88,9 @@ SIGNATURES = {
     'veda_teacher_heat': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64,
                                   c_ptr, c_i64, c_i64, c_i32, c_i64, c_ptr,
                                   c_ptr, c_i64, c_i32, c_ptr, c_f32, c_ptr]),
+    'veda_rel_mse_workspace': (c_i64, [c_i64, c_i32]),
+    'veda_rel_mse': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_ptr,
+                             c_ptr, c_i64, c_i32, c_ptr, c_ptr, c_i64, c_ptr]),
     'veda_probe_umma': (c_i32, [c_ptr, c_ptr, c_ptr, c_i32, c_ptr]),
 }
 

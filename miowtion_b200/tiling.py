@@ -250,6 +250,37 @@ def gather_tiles(x: torch.Tensor, layout: TileLayout,
     return gather_and_pool(x, layout, heads, pool=False)
 
 
+def tile_rows_perm(layout: TileLayout, rows: torch.Tensor
+                   ) -> tuple[torch.Tensor, torch.Tensor]:
+    """(perm [R * 128], valid_count [R]) of the tiles `rows` alone: the
+    packed row of every slot of those tiles (-1 on padding)."""
+    rows = rows.to(device=layout.perm.device, dtype=torch.int64)
+    perm = layout.perm.view(-1, TILE_SIZE).index_select(0, rows)
+    return (perm.reshape(-1).contiguous(),
+            layout.valid_count.index_select(0, rows).contiguous())
+
+
+def gather_tile_rows(x: torch.Tensor, layout: TileLayout, rows: torch.Tensor,
+                     heads: torch.Tensor | None) -> torch.Tensor:
+    """The tiles `rows` of the tile order only: x [S, H, D] ->
+    [R * 128, H', D], padding slots zero. Equals
+    `gather_tiles(x, layout, heads)` indexed by those tiles' slots, without
+    permuting the rest (the row-subset input of the search's forward)."""
+    _check_rows(x, 'x')
+    heads = _heads_arg(x, heads)
+    perm, valid = tile_rows_perm(layout, rows)
+    n_rows = valid.numel()
+    out = torch.empty(n_rows * TILE_SIZE, heads.numel(), x.shape[-1],
+                      dtype=x.dtype, device=x.device)
+    if n_rows == 0:
+        return out
+    _lib.call('veda_gather_pool', x.data_ptr(), x.stride(0), x.stride(1),
+              perm.data_ptr(), valid.data_ptr(), n_rows, heads.data_ptr(),
+              heads.numel(), out.data_ptr(), out.stride(0), out.stride(1),
+              None, None, None, _lib.stream_ptr(x.device))
+    return out
+
+
 def scatter_tiles_(out: torch.Tensor, tiled: torch.Tensor,
                    layout: TileLayout, heads: torch.Tensor | None) -> None:
     """Writes tile-ordered rows back into out[S + 1, H, D] in place

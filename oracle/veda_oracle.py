@@ -558,6 +558,94 @@ def teacher_heat(q, k, lse, layout: Layout, q_tiles, reduce='max',
 
 
 # ---------------------------------------------------------------------------
+# (f) tile search: oracle relative error (miowtion/veda/search.py:53-175)
+# ---------------------------------------------------------------------------
+
+def _slots(rows) -> np.ndarray:
+    rows = np.asarray(rows, dtype=np.int64)
+    return (rows[:, None] * TILE + np.arange(TILE)[None]).reshape(-1)
+
+
+def _rel_err(o_sparse, o_dense, row_valid) -> np.ndarray:
+    """search.py:122-126: per head sum of squared errors over sum of
+    squares, real rows only (fp32 accumulation)."""
+    diff = ((o_sparse - o_dense) ** 2).sum(-1)[row_valid]      # [rows, H]
+    norm = (o_dense ** 2).sum(-1)[row_valid]
+    tiny = np.finfo(np.float32).tiny
+    return (diff.sum(0) / np.maximum(norm.sum(0), tiny)).astype(np.float32)
+
+
+def oracle_rel_mse_reference(q, k, v, layout: Layout, blocks, rows,
+                             round_scores=True) -> np.ndarray:
+    """search.py:130-175: token-level fp32 restatement, head by head.
+
+    q, k, v [S, H, D] (bf16 values); `rows` the sampled video query tiles.
+    The dense probabilities of the sampled rows give the block score (the
+    max of p inside each block), the selection keeps blocks by the training
+    rules with every global key tile kept, and the sparse output is p
+    renormalised on the kept blocks. `round_scores` rounds q.k to bf16 as
+    the reference's bf16 matmul does.
+    """
+    heads, dim = q.shape[1], q.shape[2]
+    scale = np.float32(1.0 / math.sqrt(dim))
+    valid = layout.slot_valid.astype(bool)
+    slots = _slots(rows)
+    row_valid = valid[slots]
+    n = layout.n_tiles
+    rows = np.asarray(rows, dtype=np.int64)
+    gi = layout.gather_index
+    out = np.zeros(heads, dtype=np.float32)
+    for h in range(heads):
+        qt = q[gi[slots], h].astype(np.float32)
+        kt = k[gi, h].astype(np.float32)
+        vt = v[gi, h].astype(np.float32)
+        s = qt @ kt.T
+        if round_scores:
+            s = round_bf16(s)
+        s = np.where(valid[None, :], s * scale, -np.inf)
+        m = s.max(-1, keepdims=True)
+        p = np.exp(s - m)
+        p /= p.sum(-1, keepdims=True)
+        p[~row_valid] = 0.0
+        o_dense = p @ vt
+        block = p.reshape(rows.size, TILE, n, TILE).max(axis=(1, 3))
+        index, keep = select_video_blocks(block[None], layout, blocks, rows)
+        kept = np.zeros((rows.size, n), dtype=bool)
+        np.put_along_axis(kept, index[0], keep[0], axis=1)
+        kept[:, layout.n_video_tiles:] = True
+        ps = (p.reshape(rows.size, TILE, n, TILE)
+              * kept[:, None, :, None]).reshape(p.shape)
+        ps /= np.maximum(ps.sum(-1, keepdims=True), np.finfo(np.float32).tiny)
+        o_sparse = ps @ vt
+        out[h] = _rel_err(o_sparse[:, None], o_dense[:, None],
+                          row_valid)[0]
+    return out
+
+
+def oracle_rel_mse(q, k, v, layout: Layout, blocks, rows, dense_out,
+                   lse) -> np.ndarray:
+    """search.py:86-127, the kernel path: block scores from the teacher heat
+    (reduce 'max') with the dense LSE, selection without global query rows,
+    the block-sparse forward of the sampled query tiles alone (bf16 output),
+    and the error against the bf16 dense output of those rows."""
+    heads = np.arange(q.shape[1])
+    qt = gather_tiles(q, layout, heads)
+    kt = gather_tiles(k, layout, heads)
+    vt = gather_tiles(v, layout, heads)
+    lse_t = gather_lse(lse, layout, heads)
+    rows = np.asarray(rows, dtype=np.int64)
+    heat = teacher_heat(qt, kt, lse_t, layout, rows, 'max')
+    index, keep = select_video_blocks(heat, layout, blocks, rows)
+    mask = dense_block_mask(index, keep, layout, global_rows=False)
+    slots = _slots(rows)
+    o_sparse = round_bf16(block_sparse_attention(
+        qt[slots], kt, vt, mask, layout.valid_count))
+    o_dense = round_bf16(np.asarray(dense_out, np.float32))[
+        layout.gather_index[slots]]
+    return _rel_err(o_sparse, o_dense, layout.slot_valid.astype(bool)[slots])
+
+
+# ---------------------------------------------------------------------------
 # The whole SparseStudent layer (miowtion/veda/attention.py:724-794)
 # ---------------------------------------------------------------------------
 

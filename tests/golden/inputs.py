@@ -83,3 +83,32 @@ def scores(heads, n_tiles, seed):
 def dout(shape, seed):
     gen = torch.Generator().manual_seed(seed)
     return torch.randn(*shape, generator=gen).to(torch.bfloat16)
+
+
+# Tile search (oracle relative error): text rows, a video grid that three
+# candidate shapes tile differently, bf16 q/k/v, 3 heads of head_dim 128.
+SEARCH = dict(text=200, grid=(4, 16, 24), seq_len=1760, used=1736, heads=3,
+              dim=128, seed=13, ratio=0.3, query_tiles=5, sample_seed=2,
+              candidates=[(2, 8, 8), (1, 8, 16), (4, 4, 8)],
+              # Plan vote: entries of random tables over these candidates.
+              vote_layers=3, vote_entries=4, vote_heads=5, vote_seed=21,
+              vote_grid=(37, 24, 42),
+              vote_candidates=['8x4x4', '2x8x8', '4x4x8', '4x8x4', '8x2x8',
+                               '8x8x2'])
+
+
+def search_rows(n_video: int, count: int, seed: int, layer: int = 0):
+    """Sorted sampled video query tiles, the reference OracleScorer's rule
+    (search.py:227-230)."""
+    gen = torch.Generator().manual_seed(seed * 1000 + layer)
+    rows = torch.randperm(n_video, generator=gen)
+    return rows[:min(count, n_video)].sort().values
+
+
+def vote_tables(spec):
+    """Seeded [C, H] score tables per (entry, layer)."""
+    gen = torch.Generator().manual_seed(spec['vote_seed'])
+    return [[torch.rand(len(spec['vote_candidates']), spec['vote_heads'],
+                        generator=gen)
+             for _ in range(spec['vote_layers'])]
+            for _ in range(spec['vote_entries'])]
