@@ -290,6 +290,39 @@ int veda_rel_mse(const void* o_sparse, int64_t s_stride_n, int64_t s_stride_h,
                  int32_t n_heads, float* rel_mse, void* workspace,
                  int64_t workspace_bytes, void* stream);
 
+/* ---- (f) zero-order compensation ----------------------------------------- */
+
+/* Workspace bytes veda_compensate needs: the bf16 key centroids and value
+ * sums of every key tile, [n_pad, H', 128] each, n_pad = n_kv_tiles rounded
+ * up to a multiple of 128. */
+int64_t veda_compensate_workspace(int32_t n_heads, int64_t n_kv_tiles);
+
+/* Replaces miowtion/kernels/compensation_triton.py:139-226 (`summaries`
+ * and `compensate`) and the torch form miowtion/veda/attention.py:591-689
+ * (`zero_order_compensation`): every key tile a query tile did not keep
+ * (and that has a real row) becomes one virtual key at its centroid mean k
+ * with value sum v and weight B_t (its real row count):
+ *   out = (o_kept + sum_t p_t vsum_t) / (1 + sum_t p_t B_t),
+ *   p_t = exp(q . kmean_t * softmax_scale - L), L = lse_kept of the row
+ *   (0 where not finite).
+ * o_kept [n_q_tiles*128, H', 128] bf16 and lse_kept [H', n_q_tiles*128]
+ * fp32 (row stride 1) are the sparse forward's outputs over the kept tiles,
+ * which are given as that forward's index lists (rows = query tiles of q).
+ * q [n_q_tiles*128, H', 128], k, v [n_kv_tiles*128, H', 128] bf16 tile
+ * ordered, padding slots zero. out may be o_kept (in place). */
+int veda_compensate(const void* o_kept, int64_t ok_stride_n,
+                    int64_t ok_stride_h, const float* lse_kept, const void* q,
+                    int64_t q_stride_n, int64_t q_stride_h, const void* k,
+                    int64_t k_stride_n, int64_t k_stride_h, const void* v,
+                    int64_t v_stride_n, int64_t v_stride_h, int32_t n_heads,
+                    int64_t n_q_tiles, int64_t n_kv_tiles,
+                    const int32_t* valid_count, const int32_t* part_cnt,
+                    const int32_t* part_idx, const int32_t* full_cnt,
+                    const int32_t* full_idx, int64_t ld_idx, void* out,
+                    int64_t out_stride_n, int64_t out_stride_h,
+                    float softmax_scale, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* One 128x128x128 bf16 tcgen05 MMA per mode, for checking operand and

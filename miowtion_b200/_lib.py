@@ -91,6 +91,12 @@ SIGNATURES = {
     'veda_rel_mse_workspace': (c_i64, [c_i64, c_i32]),
     'veda_rel_mse': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_ptr,
                              c_ptr, c_i64, c_i32, c_ptr, c_ptr, c_i64, c_ptr]),
+    'veda_compensate_workspace': (c_i64, [c_i32, c_i64]),
+    'veda_compensate': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_i64,
+                                c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64,
+                                c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr,
+                                c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i64,
+                                c_i64, c_f32, c_ptr, c_i64, c_ptr]),
     'veda_probe_umma': (c_i32, [c_ptr, c_ptr, c_ptr, c_i32, c_ptr]),
 }
 

@@ -20,6 +20,7 @@ import dataclasses
 
 import torch
 
+from miowtion_b200 import compensation
 from miowtion_b200 import kernels
 from miowtion_b200 import mask as veda_mask
 from miowtion_b200 import plan as veda_plan
@@ -40,8 +41,18 @@ class VedaConfig:
     ref_budget: veda_mask.Budget | None = None
     tile_conditions: bool = False
     budget_rule: str = 'topk'
+    # Sol's zero-order term for the dropped tiles (attention.py:70-94). The
+    # torch form and the Triton form are one B200 kernel here
+    # (compensation.py); the INT8 fused arm has none.
+    zero_order_compensation: bool = False
+    fused_compensation: bool = False
+    triton_compensation: bool = False
     dense_layers: frozenset[int] = frozenset()
     collect_bytes: int = DEFAULT_COLLECT_BYTES
+
+    @property
+    def compensated(self) -> bool:
+        return self.zero_order_compensation or self.triton_compensation
 
 
 @dataclasses.dataclass(frozen=True)
@@ -74,6 +85,14 @@ class ClipTiling:
     def __init__(self, layout: PackedLayout, config: VedaConfig,
                  device: torch.device,
                  condition_spans: tuple[tiling.TiledSpan, ...] = ()):
+        chosen = [name for name in ('zero_order_compensation',
+                                    'fused_compensation',
+                                    'triton_compensation')
+                  if getattr(config, name)]
+        if len(chosen) > 1:
+            raise ValueError(
+                f'{" and ".join(chosen)} compute the same term; pick one, '
+                'they are implementations of it')
         if config.budget_rule not in ('topk', 'threshold'):
             raise ValueError("budget_rule must be 'topk' or 'threshold': "
                              f'{config.budget_rule!r}')
@@ -207,6 +226,12 @@ class SparseStudent:
         if clip.config.budget_rule != 'topk':
             raise NotImplementedError("only the 'topk' budget rule has a "
                                       'B200 kernel')
+        if clip.config.fused_compensation:
+            raise NotImplementedError(
+                'fused_compensation is the INT8 Sol kernel (an external '
+                'Triton kernel); use zero_order_compensation or '
+                'triton_compensation, which run the B200 compensation '
+                'kernel')
         self.clip = clip
         self.plan = plan
         self.predictor = predictor
@@ -260,8 +285,16 @@ class SparseStudent:
                 self.clip.blocks(tile_layout))
             ev.stop(t)
         t = ev.start('attention')
-        o_tiles = kernels.block_sparse_attention_lists(
-            q_tiles, k_tiles, v_tiles, lists, tile_layout)
+        if self.clip.config.compensated:
+            o_tiles, lse = kernels.block_sparse_attention_lists(
+                q_tiles, k_tiles, v_tiles, lists, tile_layout,
+                return_lse=True)
+            compensation.compensate_lists(o_tiles, lse, q_tiles, k_tiles,
+                                          v_tiles, lists, tile_layout,
+                                          out=o_tiles)
+        else:
+            o_tiles = kernels.block_sparse_attention_lists(
+                q_tiles, k_tiles, v_tiles, lists, tile_layout)
         ev.stop(t)
         t = ev.start('unpermute')
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
@@ -272,6 +305,10 @@ class SparseStudent:
         """The differentiable layer: per head group, the forward of
         `_attend` inside `_SparseGroup`, plus the transposed lists the
         backward walks (fa4.py:353-359)."""
+        if self.clip.config.compensated:
+            raise NotImplementedError(
+                'the zero-order compensation is an evaluation arm; it has '
+                'no backward')
         parts, all_heads = [], []
         for group in self.plan.head_groups(layer_index, self.clip.device):
             tile_layout = self.clip.get(group.shape)

@@ -558,6 +558,49 @@ def teacher_heat(q, k, lse, layout: Layout, q_tiles, reduce='max',
 
 
 # ---------------------------------------------------------------------------
+# (f) zero-order compensation (miowtion/veda/attention.py:591-689; the Triton
+# form miowtion/kernels/compensation_triton.py:84-245)
+# ---------------------------------------------------------------------------
+
+def zero_order_compensation(o_kept, lse_kept, q_tiles, k_tiles, v_tiles,
+                            block_mask, layout: Layout,
+                            bf16_summaries=False):
+    """attention.py:591-689 (fp32): each dropped key tile with real rows
+    becomes one key at its centroid (mean k over real rows) with value
+    sum v, weighted by its real row count; the reference exponent is the
+    kept LSE (0 where not finite). `bf16_summaries` rounds the centroid and
+    the value sum to bf16 as the Triton form stores them. An empty key tile
+    carries no mass in either form (zero value sum, zero weight).
+    """
+    rows, heads, dim = o_kept.shape
+    n = layout.n_tiles
+    scale = np.float32(1.0 / math.sqrt(dim))
+    counts = layout.valid_count.astype(np.float32)
+    kf = k_tiles.astype(np.float32).reshape(n, TILE, heads, dim)
+    vf = v_tiles.astype(np.float32).reshape(n, TILE, heads, dim)
+    real = (np.arange(TILE)[None, :] < layout.valid_count[:, None])
+    k_mean = (kf * real[:, :, None, None]).sum(1) / np.maximum(
+        counts, 1.0)[:, None, None]                        # [n, H, D]
+    v_sum = (vf * real[:, :, None, None]).sum(1)
+    if bf16_summaries:
+        k_mean, v_sum = round_bf16(k_mean), round_bf16(v_sum)
+    out = np.empty((rows, heads, dim), dtype=np.float32)
+    owner = np.arange(rows) // TILE
+    for h in range(heads):
+        ref = lse_kept[h].astype(np.float32)
+        safe = np.where(np.isfinite(ref), ref, 0.0).astype(np.float32)
+        drop = (~block_mask[h][owner]) & (counts[None, :] > 0)   # [rows, n]
+        s_hat = (q_tiles[:, h].astype(np.float32) @ k_mean[:, h].T) * scale
+        with np.errstate(over='ignore'):
+            p_hat = np.where(drop, np.exp(s_hat - safe[:, None]), 0.0)
+        num = p_hat @ v_sum[:, h]
+        den = p_hat @ counts
+        out[:, h] = (o_kept[:, h].astype(np.float32) + num) / (
+            1.0 + den)[:, None]
+    return out
+
+
+# ---------------------------------------------------------------------------
 # (f) tile search: oracle relative error (miowtion/veda/search.py:53-175)
 # ---------------------------------------------------------------------------
 

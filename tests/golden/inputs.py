@@ -112,3 +112,17 @@ def vote_tables(spec):
                         generator=gen)
              for _ in range(spec['vote_layers'])]
             for _ in range(spec['vote_entries'])]
+
+
+# Zero-order compensation: the padded target grid behind text rows (partial
+# tiles, a partial global tile), head_dim 128 (the kernel's), a random keep
+# mask from block scores, and a fixed projection for row checksums.
+COMPENSATION = dict(spans=[(360, (8, 12, 20), (4, 8, 4))], used=2280,
+                    seq_len=2312, heads=3, dim=128, seed=31, score_seed=32,
+                    ratio=0.3, proj_seed=33, full_tile=5)
+
+
+def projection(dim, seed):
+    """[dim] fp32 weights for per-row checksums out[r, h] . w."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(dim, generator=gen)
