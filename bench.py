@@ -300,11 +300,15 @@ def main():
     ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--only', choices=['backward', 'heat'], default=None,
+    ap.add_argument('--only', choices=['backward', 'heat', 'compensation',
+                                       'search'], default=None,
                     help='time one stage on head group 0 of the config '
                          '(for kernel profiling)')
     ap.add_argument('--reduce', choices=['sum', 'max'], default='sum',
                     help="heat reduction for --only heat")
+    ap.add_argument('--query-tiles', type=int, default=40,
+                    help='sampled query tiles for --only search (the '
+                         "reference's SearchConfig default)")
     ap.add_argument('--parallel', choices=['clips', 'ulysses'], default=None,
                     help='multi-GPU mode (default: clips for cfg2, ulysses '
                          'for cfg3/cfg4)')
@@ -487,8 +491,10 @@ def main():
 
 def run_stage(args, cfg):
     """One stage on one GPU, head group 0 of the config: the block-sparse
-    backward (prep, dq, dk/dv) or the teacher heat for every query tile.
-    The line's unit is ms per call of that stage."""
+    backward (prep, dq, dk/dv), the teacher heat for every query tile, the
+    zero-order compensation of every query tile, or the tile-search oracle
+    error of one candidate shape. The line's unit is ms per call of that
+    stage."""
     from miowtion_b200 import heatmap
     from miowtion_b200 import kernels
     device = torch.device('cuda', 0)
@@ -522,6 +528,50 @@ def run_stage(args, cfg):
             kernels.block_sparse_attention_bwd(qt, kt, vt, out, dout, lse,
                                                lists, t_lists, tl)
         what = 'block-sparse backward (prep + dq + dk/dv)'
+    elif args.only == 'compensation':
+        from miowtion_b200 import compensation
+        qt, fq = tiling.gather_and_pool(q, tl, group.heads)
+        kt, fk = tiling.gather_and_pool(k, tl, group.heads)
+        vt = tiling.gather_tiles(v, tl, group.heads)
+        del q, k, v
+        with torch.no_grad():
+            logits = student.predictor.layers[0](fq, fk, group.heads)
+            lists = veda_mask.select_block_lists(
+                logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
+        o_kept, lse = kernels.block_sparse_attention_lists(
+            qt, kt, vt, lists, tl, return_lse=True)
+        out = torch.empty_like(o_kept)
+        blocks = tl.n_tiles * heads  # (query tile, head) items
+        # Two GEMMs per (query tile, head) against every key centroid.
+        flops = 4.0 * blocks * 128 * tl.n_tiles * 128
+
+        def call():
+            compensation.compensate_lists(o_kept, lse, qt, kt, vt, lists, tl,
+                                          out=out)
+        what = ('zero-order compensation (centroid summaries + tcgen05 '
+                'centroid pass), all query tiles')
+    elif args.only == 'search':
+        from miowtion_b200 import search
+        qg, kg, vg = (t.index_select(1, group.heads).contiguous()
+                      for t in (q, k, v))
+        del q, k, v
+        with torch.no_grad():
+            dense, lse = kernels.dense_attention(qg, kg, vg, 128 ** -0.5,
+                                                 True, used=cfg['used'])
+        gen = torch.Generator().manual_seed(0)
+        count = min(args.query_tiles, tl.n_video_tiles)
+        rows = torch.randperm(tl.n_video_tiles, generator=gen)[:count].sort(
+        ).values.to(device)
+        blocks = count * heads
+        # Heat QK^T of the sampled tiles against every key tile; the sparse
+        # forward of the kept blocks is small beside it.
+        flops = 2.0 * blocks * tl.n_tiles * 128 ** 3
+
+        def call():
+            search.oracle_rel_mse(qg, kg, vg, tl, clip.blocks(tl), rows,
+                                  dense_out=dense, lse=lse)
+        what = (f'tile-search oracle rel-MSE of one candidate, {count} '
+                'sampled query tiles')
     else:
         with torch.no_grad():
             _, lse = kernels.dense_attention(q, k, v, 128 ** -0.5, True,
@@ -558,9 +608,13 @@ def run_stage(args, cfg):
         'blocks': blocks,
         'tflops': flops / (ms * 1e-3) / 1e12,
         'frac_of_peak': flops / (ms * 1e-3) / 1e12 / peaks['bf16_tflops'],
-        'flops_accounting': ('2.5 x the forward per computed block (the '
-                             "reference's)" if args.only == 'backward' else
-                             '2 x 128^3 per block of QK^T')}), flush=True)
+        'flops_accounting': {
+            'backward': "2.5 x the forward per computed block (the "
+                        "reference's)",
+            'heat': '2 x 128^3 per block of QK^T',
+            'compensation': '4 x 128 x n_tiles x 128 per (query tile, head)',
+            'search': '2 x 128^3 per heat block of the sampled tiles',
+        }[args.only]}), flush=True)
 
 
 def run_train_step(args, cfg):

@@ -19,27 +19,35 @@
 //     (the Triton form's precision) in a [n_pad, H, 128] workspace whose
 //     rows n_tiles .. n_pad are zero.
 //  2. `comp_kernel` (tcgen05): per (query tile, head), walk the centroids
-//     in chunks of 128 tiles: S = Q . KC^T (SS MMA into TMEM), eight
-//     compute warps turn S into p (0 where the tile was kept or is empty)
-//     and accumulate the weighted denominator, P goes back over S in TMEM
-//     as bf16, and O += P . VC (TS MMA). The epilogue combines O with
-//     o_kept. Persistent, one CTA per SM; the kept tiles of a query tile
-//     are read from the same full / partial index lists the forward uses.
+//     in chunks of 128 tiles: S = Q . KC^T (SS MMA into one of three TMEM
+//     S buffers), eight compute warps turn S into p (0 where the tile was
+//     kept or is empty) and accumulate the weighted denominator, P goes
+//     back over S in TMEM as bf16, and O += P . VC (TS MMA). The epilogue
+//     combines O with o_kept. Persistent, one CTA per SM, 13 warps:
+//     8 compute, a Q / key-centroid TMA warp, a value-sum TMA warp, an S
+//     issuer (up to three chunks ahead), a P.V issuer, and a prep warp that
+//     builds the next item's per-tile weights (row counts, 0 for the tiles
+//     the forward's index lists kept) and LSE in shared memory.
 #include "common.cuh"
 
 namespace veda {
 
 namespace {
 
-constexpr int kCompWarps = 8;               // compute warps
-constexpr int kCompProducer = kCompWarps;   // TMA
-constexpr int kCompMma = kCompWarps + 1;    // MMA issuer, TMEM owner
-constexpr int kCompThreads = 32 * (kCompWarps + 2);
+constexpr int kCompWarps = 8;                   // compute warps
+constexpr int kCompProducer = kCompWarps;       // TMA: Q, key centroids
+constexpr int kCompSIssuer = kCompWarps + 1;    // S MMAs, TMEM owner
+constexpr int kCompVProducer = kCompWarps + 2;  // TMA: value sums
+constexpr int kCompPvIssuer = kCompWarps + 3;   // P.V MMAs
+constexpr int kCompPrep = kCompWarps + 4;  // weights and LSE of the next item
+constexpr int kCompThreads = 32 * (kCompWarps + 5);
 constexpr uint32_t kTileBytes = 32768;
 constexpr uint32_t kHalfBytes = 16384;
 constexpr uint32_t kTileUnits = kTileBytes >> 4;
-constexpr uint32_t kCompTmemCols = 512;  // S[2] 0..255, O 256..383
-constexpr int kMaxTiles = 16384;          // key tiles (kept map in smem)
+constexpr int kSBufs = 3;                // S / P buffers in TMEM
+constexpr uint32_t kCompTmemCols = 512;  // S[3] 0..383, O 384..511
+// Key tiles: their row counts and two items' weights sit in shared memory.
+constexpr int kMaxTiles = 5120;
 
 enum CompBar {
   kQFull = 0,
@@ -48,12 +56,15 @@ enum CompBar {
   kKcEmpty = kKcFull + 2,
   kVcFull = kKcEmpty + 2,
   kVcEmpty = kVcFull + 2,
-  kSFull = kVcEmpty + 2,
-  kPFull = kSFull + 2,   // [2], 8 warps
-  kPvDone = kPFull + 2,  // [2]
-  kODone = kPvDone + 2,
+  kSFull = kVcEmpty + 2,       // [3]
+  kPFull = kSFull + kSBufs,    // [3], 8 warps
+  kPvDone = kPFull + kSBufs,   // [3]
+  kODone = kPvDone + kSBufs,
   kOFree,  // 8 warps
-  kDrain,
+  kWFull,  // [2] weights and LSE of an item ready (prep warp)
+  kWEmpty = kWFull + 2,  // [2] the compute warps are done with them (8)
+  kDrainS = kWEmpty + 2,
+  kDrainPv,
   kCompBars
 };
 
@@ -151,7 +162,8 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-__global__ void __launch_bounds__(kCompThreads, 1)
+// Thirteen warps: per SMSP at most four, so at most 128 registers each.
+__global__ void __maxnreg__(128)
     comp_kernel(const __grid_constant__ CUtensorMap map_q,
                 const __grid_constant__ CUtensorMap map_kc,
                 const __grid_constant__ CUtensorMap map_vc,
@@ -162,23 +174,29 @@ __global__ void __launch_bounds__(kCompThreads, 1)
   uint8_t* s_q = smem;
   uint8_t* s_kc = s_q + kTileBytes;       // [2]
   uint8_t* s_vc = s_kc + 2 * kTileBytes;  // [2]
-  float* s_w = reinterpret_cast<float*>(s_vc + 2 * kTileBytes);  // [2][128]
-  float* s_den = s_w + 2 * kTile;                                 // [2][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_den + 2 * kTile);
+  const int n_pad = p.n_chunks * kTile;
+  // Weight of every key tile for a query tile: its real row count if
+  // dropped, 0 if kept, empty or past the last tile. [2 items][n_pad],
+  // 1024-byte aligned (read as float4).
+  float* s_w = reinterpret_cast<float*>(s_vc + 2 * kTileBytes);
+  float* s_cnt = s_w + 2 * n_pad;     // [n_pad] real row counts
+  float* s_den = s_cnt + n_pad;       // [2 items][2 halves][128 rows]
+  float* s_lse = s_den + 4 * kTile;   // [2 items][128 rows], log2 units
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_lse + 2 * kTile);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kCompBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint8_t* s_keep = reinterpret_cast<uint8_t*>(tmem_slot + 4);  // [n_tiles]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int b = 0; b < kCompBars; ++b)
-      mbar_init(&bars[b], (b == kPFull || b == kPFull + 1 || b == kOFree)
-                              ? kCompWarps
-                              : 1);
+    for (int b = 0; b < kCompBars; ++b) {
+      const bool by_compute = (b >= kPFull && b < kPFull + kSBufs) ||
+                              b == kOFree || b == kWEmpty || b == kWEmpty + 1;
+      mbar_init(&bars[b], by_compute ? kCompWarps : 1);
+    }
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == kCompMma) {
+  if (warp == kCompSIssuer) {
     tmem_alloc(tmem_slot, kCompTmemCols);
     tmem_relinquish();
   }
@@ -189,26 +207,13 @@ __global__ void __launch_bounds__(kCompThreads, 1)
   const int nc = p.n_chunks;
 
   if (warp == kCompProducer) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: Q and key centroids ----------------
     if (lane == 0) {
       prefetch_tensor_map(&map_q);
       prefetch_tensor_map(&map_kc);
-      prefetch_tensor_map(&map_vc);
     }
-    int g = 0, it = 0, vh = 0, vchunk = 0;
+    int g = 0, it = 0;
     bool ok = true;
-    // Loads the value centroids of chunk gv (head hv, chunk cv).
-    auto load_vc = [&](int gv, int hv, int cv) -> bool {
-      const int s = gv & 1;
-      if (gv >= 2 && !wait_all(&bars[kVcEmpty + s], ((gv >> 1) - 1) & 1,
-                               abort, p.status))
-        return false;
-      if (lane == 0)
-        load_tile(s_vc + s * kTileBytes, &map_vc, &bars[kVcFull + s], hv,
-                  cv * kTile);
-      __syncwarp();
-      return true;
-    };
     for (int item = blockIdx.x; ok && item < p.n_items;
          item += gridDim.x, ++it) {
       const int r = item / p.n_heads, h = item % p.n_heads;
@@ -230,68 +235,61 @@ __global__ void __launch_bounds__(kCompThreads, 1)
           load_tile(s_kc + s * kTileBytes, &map_kc, &bars[kKcFull + s], h,
                     c * kTile);
         __syncwarp();
-        // Values run one chunk behind the keys: they are needed a whole
-        // chunk of compute later.
-        if (g >= 1 && !load_vc(g - 1, vh, vchunk)) {
-          ok = false;
-          break;
-        }
-        vh = h;
-        vchunk = c;
       }
     }
-    if (ok && g >= 1) load_vc(g - 1, vh, vchunk);
     if (lane == 0 && *abort) {
       // Let the copies in flight land before the CTA exits.
       volatile int never = 0;
       for (int b = g - 2; b < g; ++b)
-        if (b >= 0) {
+        if (b >= 0)
           mbar_wait(&bars[kKcFull + (b & 1)], (b >> 1) & 1, &never, nullptr);
-          mbar_wait(&bars[kVcFull + (b & 1)], (b >> 1) & 1, &never, nullptr);
-        }
       if (it > 0) mbar_wait(&bars[kQFull], (it - 1) & 1, &never, nullptr);
     }
-  } else if (warp == kCompMma) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == kCompVProducer) {
+    // ---------------- TMA producer: value sums ----------------
+    // Its own warp, so that a value load waiting for a P.V MMA never holds
+    // up the key loads.
+    if (lane == 0) prefetch_tensor_map(&map_vc);
+    int g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      const int h = item % p.n_heads;
+      for (int c = 0; c < nc; ++c, ++g) {
+        const int s = g & 1;
+        if (g >= 2 && !wait_all(&bars[kVcEmpty + s], ((g >> 1) - 1) & 1,
+                                abort, p.status)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0)
+          load_tile(s_vc + s * kTileBytes, &map_vc, &bars[kVcFull + s], h,
+                    c * kTile);
+        __syncwarp();
+      }
+    }
+    if (lane == 0 && *abort) {
+      volatile int never = 0;
+      for (int b = g - 2; b < g; ++b)
+        if (b >= 0)
+          mbar_wait(&bars[kVcFull + (b & 1)], (b >> 1) & 1, &never, nullptr);
+    }
+  } else if (warp == kCompSIssuer) {
+    // ---------------- S = Q . KC^T, up to three chunks ahead ----------------
     constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);
-    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
     const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
     const uint32_t kc_lo = sw128_desc_lo(smem_u32(s_kc), 16);
-    const uint32_t vc_lo = sw128_desc_lo(smem_u32(s_vc), kHalfBytes);
-    const uint32_t t_o = tmem + 256;
-    // O (+)= P . VC of chunk gg.
-    auto issue_pv = [&](int gg, bool first, bool last, int it) -> bool {
-      const int s = gg & 1;
-      const uint32_t par = (gg >> 1) & 1;
-      if (first && it > 0 &&
-          !wait_all(&bars[kOFree], (it - 1) & 1, abort, p.status))
-        return false;
-      if (!wait_all(&bars[kVcFull + s], par, abort, p.status)) return false;
-      if (!wait_all(&bars[kPFull + s], par, abort, p.status)) return false;
-      tc_fence_after();
-      const uint32_t t_p = tmem + s * 128;
-      const uint32_t bv = vc_lo + s * kTileUnits;
-      // P of keys 16kk .. 16kk + 15: half kk / 4 holds its 64 keys packed
-      // in its first 32 columns.
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_ts_warp(t_o, t_p + (kk >> 2) * 64 + (kk & 3) * 8,
-                     bv + kk * 128, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
-      umma_commit_warp(&bars[kVcEmpty + s]);
-      umma_commit_warp(&bars[kPvDone + s]);
-      if (last) umma_commit_warp(&bars[kODone]);
-      return true;
-    };
     int g = 0, it = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.n_items;
          item += gridDim.x, ++it) {
       if (!wait_all(&bars[kQFull], it & 1, abort, p.status)) break;
       for (int c = 0; c < nc; ++c, ++g) {
-        const int s = g & 1;
+        const int s = g & 1, sb = g % kSBufs;
+        // S buffer sb held P of chunk g - 3: its P.V must have read it.
         if (!wait_all(&bars[kKcFull + s], (g >> 1) & 1, abort, p.status) ||
-            (g >= 2 && !wait_all(&bars[kPvDone + s], ((g >> 1) - 1) & 1,
-                                 abort, p.status))) {
+            (g >= kSBufs &&
+             !wait_all(&bars[kPvDone + sb], (g / kSBufs - 1) & 1, abort,
+                       p.status))) {
           ok = false;
           break;
         }
@@ -300,119 +298,180 @@ __global__ void __launch_bounds__(kCompThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-          umma_ss_warp(tmem + s * 128, q_lo + off, bk + off, idesc_s,
+          umma_ss_warp(tmem + sb * 128, q_lo + off, bk + off, idesc_s,
                        kk > 0 ? 1u : 0u);
         }
         umma_commit_warp(&bars[kKcEmpty + s]);
-        umma_commit_warp(&bars[kSFull + s]);
+        umma_commit_warp(&bars[kSFull + sb]);
         if (c == nc - 1) umma_commit_warp(&bars[kQEmpty]);
-        if (c > 0 && !issue_pv(g - 1, c == 1, false, it)) {
-          ok = false;
-          break;
-        }
       }
-      if (!ok || !issue_pv(g - 1, nc == 1, true, it)) break;
     }
     if (*abort) {
       volatile int never = 0;
-      umma_commit_warp(&bars[kDrain]);
-      mbar_wait(&bars[kDrain], 0, &never, nullptr);
+      umma_commit_warp(&bars[kDrainS]);
+      mbar_wait(&bars[kDrainS], 0, &never, nullptr);
+    }
+  } else if (warp == kCompPvIssuer) {
+    // ---------------- O (+)= P . VC ----------------
+    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
+    const uint32_t vc_lo = sw128_desc_lo(smem_u32(s_vc), kHalfBytes);
+    const uint32_t t_o = tmem + kSBufs * 128;
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.n_items;
+         item += gridDim.x, ++it) {
+      for (int c = 0; c < nc; ++c, ++g) {
+        const int s = g & 1, sb = g % kSBufs;
+        // The item's first P.V overwrites O: the epilogue must have read
+        // the previous item's.
+        if ((c == 0 && it > 0 &&
+             !wait_all(&bars[kOFree], (it - 1) & 1, abort, p.status)) ||
+            !wait_all(&bars[kVcFull + s], (g >> 1) & 1, abort, p.status) ||
+            !wait_all(&bars[kPFull + sb], (g / kSBufs) & 1, abort,
+                      p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_p = tmem + sb * 128;
+        const uint32_t bv = vc_lo + s * kTileUnits;
+        // P of keys 16kk .. 16kk + 15: half kk / 4 holds its 64 keys packed
+        // in its first 32 columns.
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts_warp(t_o, t_p + (kk >> 2) * 64 + (kk & 3) * 8,
+                       bv + kk * 128, idesc_pv, (kk > 0 || c > 0) ? 1u : 0u);
+        umma_commit_warp(&bars[kVcEmpty + s]);
+        umma_commit_warp(&bars[kPvDone + sb]);
+        if (c == nc - 1) umma_commit_warp(&bars[kODone]);
+      }
+    }
+    if (*abort) {
+      volatile int never = 0;
+      umma_commit_warp(&bars[kDrainPv]);
+      mbar_wait(&bars[kDrainPv], 0, &never, nullptr);
+    }
+  } else if (warp == kCompPrep) {
+    // ---------------- prep: weights and LSE, one item ahead ----------------
+    for (int t = lane; t < n_pad; t += 32)
+      s_cnt[t] = t < p.n_kv_tiles ? static_cast<float>(p.valid_count[t])
+                                  : 0.f;
+    __syncwarp();
+    int it = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++it) {
+      const int r = item / p.n_heads, h = item % p.n_heads;
+      const int b = it & 1;
+      if (it >= 2 && !wait_all(&bars[kWEmpty + b], ((it >> 1) - 1) & 1,
+                               abort, p.status))
+        break;
+      float* w = s_w + b * n_pad;
+      for (int t = 4 * lane; t < n_pad; t += 128)
+        *reinterpret_cast<float4*>(w + t) =
+            *reinterpret_cast<const float4*>(s_cnt + t);
+      __syncwarp();
+      const int64_t li = static_cast<int64_t>(h) * p.n_q_tiles + r;
+      const int np = p.part_cnt[li], nf = p.full_cnt[li];
+      for (int e = lane; e < np + nf; e += 32) {
+        const int t = e < np ? p.part_idx[li * p.ld_idx + e]
+                             : p.full_idx[li * p.ld_idx + (e - np)];
+        if (t >= 0 && t < p.n_kv_tiles) w[t] = 0.f;
+      }
+      for (int i = lane; i < kTile; i += 32) {
+        const float l = p.lse[h * p.lse_sh + static_cast<int64_t>(r) * kTile +
+                              i];
+        s_lse[b * kTile + i] = isfinite(l) ? l * 1.4426950408889634f : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kWFull + b]);
     }
   } else {
     // ---------------- compute warps 0-7 ----------------
     const int quarter = warp % 4, half = warp / 4;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int tid = threadIdx.x;  // 0 .. 255
-    const int64_t n_rows_q = static_cast<int64_t>(p.n_q_tiles) * kTile;
     int g = 0, it = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.n_items;
          item += gridDim.x, ++it) {
       const int r = item / p.n_heads, h = item % p.n_heads;
-      // The tiles this query tile kept (both lists), as a byte map.
-      compute_sync();
-      for (int t = tid; t < p.n_kv_tiles; t += 32 * kCompWarps) s_keep[t] = 0;
-      compute_sync();
-      const int64_t li = static_cast<int64_t>(h) * p.n_q_tiles + r;
-      const int np = p.part_cnt[li], nf = p.full_cnt[li];
-      for (int e = tid; e < np + nf; e += 32 * kCompWarps) {
-        const int t = e < np ? p.part_idx[li * p.ld_idx + e]
-                             : p.full_idx[li * p.ld_idx + (e - np)];
-        if (t >= 0 && t < p.n_kv_tiles) s_keep[t] = 1;
-      }
+      const int wb = it & 1;
       const int64_t q_row = static_cast<int64_t>(r) * kTile + row;
-      float lse = p.lse[h * p.lse_sh + q_row];
-      const float l2 = isfinite(lse) ? lse * 1.4426950408889634f : 0.f;
-      float den = 0.f;
+      const __nv_bfloat16* src = p.o_kept + q_row * p.ok_sn + h * p.ok_sh +
+                                 half * 64;
+      // This row's o_kept (one 128-byte line) is read in the epilogue:
+      // bring it into L2 now.
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+      if (!wait_all(&bars[kWFull + wb], (it >> 1) & 1, abort, p.status)) {
+        ok = false;
+        break;
+      }
+      const float l2 = s_lse[wb * kTile + row];
+      // Four partial sums keep the denominator's FMA chain short.
+      float den4[4] = {0.f, 0.f, 0.f, 0.f};
       for (int c = 0; c < nc; ++c, ++g) {
-        const int s = g & 1;
-        compute_sync();  // s_keep written; s_w[s] free (read two chunks ago)
-        if (tid < kTile) {
-          const int t = c * kTile + tid;
-          float w = 0.f;
-          if (t < p.n_kv_tiles && !s_keep[t]) w = static_cast<float>(
-              p.valid_count[t]);
-          s_w[s * kTile + tid] = w;
-        }
-        compute_sync();
-        if (!wait_all(&bars[kSFull + s], (g >> 1) & 1, abort, p.status)) {
+        const int sb = g % kSBufs;
+        if (!wait_all(&bars[kSFull + sb], (g / kSBufs) & 1, abort,
+                      p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float* w_s = s_w + s * kTile;
-#pragma unroll
+        const float* w_s = s_w + wb * n_pad + c * kTile + half * 64;
+        const uint32_t t_s = tmem + sb * 128 + half * 64 + lane_base;
+#pragma unroll 1
         for (int sub = 0; sub < 2; ++sub) {
-          const int col0 = half * 64 + sub * 32;
-          uint32_t x[32];
-          tmem_ld32(tmem + s * 128 + col0 + lane_base, x);
+          uint32_t x[32], pk[16];
+          tmem_ld32(t_s + sub * 32, x);
           tmem_wait_ld();
-          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 w = *reinterpret_cast<const float2*>(w_s + col0 +
-                                                              2 * i);
-            float e0 = ex2_approx(
-                fmaf(__uint_as_float(x[2 * i]), p.scale_log2, -l2));
-            float e1 = ex2_approx(
-                fmaf(__uint_as_float(x[2 * i + 1]), p.scale_log2, -l2));
-            e0 = w.x > 0.f ? e0 : 0.f;
-            e1 = w.y > 0.f ? e1 : 0.f;
-            den = fmaf(e0, w.x, den);
-            den = fmaf(e1, w.y, den);
-            pk[i] = pack_bf16(e0, e1);
+          for (int i = 0; i < 8; ++i) {
+            const float4 w =
+                *reinterpret_cast<const float4*>(w_s + sub * 32 + 4 * i);
+            const float wv[4] = {w.x, w.y, w.z, w.w};
+            float e[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              e[j] = ex2_approx(
+                  fmaf(__uint_as_float(x[4 * i + j]), p.scale_log2, -l2));
+              e[j] = wv[j] > 0.f ? e[j] : 0.f;
+              den4[j] = fmaf(e[j], wv[j], den4[j]);
+            }
+            pk[2 * i] = pack_bf16(e[0], e[1]);
+            pk[2 * i + 1] = pack_bf16(e[2], e[3]);
           }
-          // P of these 32 keys over the first half of the S columns just
-          // read (keys 64 half + 32 sub ... in columns 64 half + 16 sub).
-          tmem_st16(tmem + s * 128 + half * 64 + sub * 16 + lane_base, pk);
+          // P of these 32 keys over the first half of this warp's S
+          // columns (keys 64 half + k in column 64 half + k / 2).
+          tmem_st16(t_s + sub * 16, pk);
         }
         tmem_wait_st();
-        arrive_warp(&bars[kPFull + s]);
+        arrive_warp(&bars[kPFull + sb]);
       }
       if (!ok) break;
+      uint4 okept[8];
+#pragma unroll
+      for (int v8 = 0; v8 < 8; ++v8)
+        okept[v8] = *reinterpret_cast<const uint4*>(src + v8 * 8);
+      // This item's weights and LSE are no longer read.
+      arrive_warp(&bars[kWEmpty + wb]);
       // Epilogue: the two column halves' denominators, then O.
-      s_den[half * kTile + row] = den;
+      float* den_x = s_den + wb * 2 * kTile;
+      den_x[half * kTile + row] = (den4[0] + den4[1]) + (den4[2] + den4[3]);
       compute_sync();
-      const float inv = 1.f / (1.f + s_den[row] + s_den[kTile + row]);
+      const float inv = 1.f / (1.f + den_x[row] + den_x[kTile + row]);
       if (!wait_all(&bars[kODone], it & 1, abort, p.status)) break;
       tc_fence_after();
-      const __nv_bfloat16* src = p.o_kept + q_row * p.ok_sn + h * p.ok_sh +
-                                 half * 64;
       __nv_bfloat16* dst = p.out + q_row * p.out_sn + h * p.out_sh +
                            half * 64;
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         uint32_t o[32];
-        tmem_ld32(tmem + 256 + half * 64 + part * 32 + lane_base, o);
+        tmem_ld32(tmem + kSBufs * 128 + half * 64 + part * 32 + lane_base, o);
         tmem_wait_ld();
         if (part == 1) arrive_warp(&bars[kOFree]);
 #pragma unroll
         for (int v8 = 0; v8 < 4; ++v8) {
-          const int e0 = part * 32 + v8 * 8;
-          const uint4 a = *reinterpret_cast<const uint4*>(src + e0);
           const __nv_bfloat162* pa =
-              reinterpret_cast<const __nv_bfloat162*>(&a);
+              reinterpret_cast<const __nv_bfloat162*>(&okept[part * 4 + v8]);
           uint4 res;
           uint32_t* pr = reinterpret_cast<uint32_t*>(&res);
 #pragma unroll
@@ -422,23 +481,23 @@ __global__ void __launch_bounds__(kCompThreads, 1)
                               (f.y + __uint_as_float(o[v8 * 8 + 2 * e + 1])) *
                                   inv);
           }
-          *reinterpret_cast<uint4*>(dst + e0) = res;
+          *reinterpret_cast<uint4*>(dst + part * 32 + v8 * 8) = res;
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kCompMma) {
+  if (warp == kCompSIssuer) {
     tc_fence_after();
     tmem_dealloc(tmem, kCompTmemCols);
   }
 }
 
 size_t comp_smem_bytes(int64_t n_kv_tiles) {
-  return 1024 + 5 * kTileBytes + 4 * kTile * sizeof(float) +
-         kCompBars * sizeof(uint64_t) + 16 +
-         static_cast<size_t>((n_kv_tiles + 15) / 16 * 16);
+  const int64_t n_pad = (n_kv_tiles + kTile - 1) / kTile * kTile;
+  return 1024 + 5 * kTileBytes + 3 * n_pad * sizeof(float) +
+         6 * kTile * sizeof(float) + kCompBars * sizeof(uint64_t) + 16;
 }
 
 }  // namespace
@@ -471,7 +530,7 @@ extern "C" int veda_compensate(
                "out are required");
   VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535 && n_q_tiles >= 0 &&
                    n_kv_tiles >= 1 && n_kv_tiles <= kMaxTiles,
-               "bad shape (at most 16384 key tiles)");
+               "bad shape (at most 5120 key tiles)");
   VEDA_REQUIRE(ld_idx >= n_kv_tiles, "ld_idx must be >= n_kv_tiles");
   VEDA_REQUIRE(n_q_tiles * n_heads < (int64_t(1) << 30), "too many tiles");
   VEDA_REQUIRE(softmax_scale > 0.f, "softmax_scale must be positive");
