@@ -306,6 +306,10 @@ def main():
                          '(for kernel profiling)')
     ap.add_argument('--reduce', choices=['sum', 'max'], default='sum',
                     help="heat reduction for --only heat")
+    ap.add_argument('--teacher', choices=['fused', 'separate'],
+                    default='fused',
+                    help='cfg5 teacher: one fused dense + LSE + heat pass per '
+                         'head group, or the dense kernel then the heat kernel')
     ap.add_argument('--query-tiles', type=int, default=40,
                     help='sampled query tiles for --only search (the '
                          "reference's SearchConfig default)")
@@ -618,9 +622,15 @@ def run_stage(args, cfg):
 
 
 def run_train_step(args, cfg):
-    """Config 5 on one GPU: the teacher (dense forward with LSE, LSE in tile
-    order, block heat with reduce='sum' for every query tile) and the sparse
-    student forward + backward on the same q, k, v."""
+    """Config 5 on one GPU: the teacher (dense forward with LSE and the
+    block heat with reduce='sum' for every query tile) and the sparse
+    student forward + backward on the same q, k, v.
+
+    `--teacher fused` (default): per head group, q, k, v in tile order, one
+    pass of the fused dense + LSE + heat kernel, and the teacher output
+    scattered back to sequence order. `--teacher separate`: the dense
+    kernel over the packed sequence, the LSE gathered into tile order, and
+    the heat kernel recomputing QK^T."""
     from miowtion_b200 import heatmap
     from miowtion_b200 import kernels
     if int(os.environ.get('WORLD_SIZE', '1')) != 1 or args.gpus != 1:
@@ -635,27 +645,49 @@ def run_train_step(args, cfg):
     scale = 128 ** -0.5
     groups = plan.head_groups(0, device)
     stream = torch.cuda.current_stream()
-    stage_ms = {'dense_fwd_lse': 0.0, 'heat': 0.0, 'student_fwd': 0.0,
-                'student_bwd': 0.0}
+    fused = args.teacher == 'fused'
+    if fused:
+        stage_ms = {'teacher_gather': 0.0, 'teacher_fused': 0.0,
+                    'student_fwd': 0.0, 'student_bwd': 0.0}
+    else:
+        stage_ms = {'dense_fwd_lse': 0.0, 'heat': 0.0, 'student_fwd': 0.0,
+                    'student_bwd': 0.0}
+    teacher_out = torch.empty(cfg['seq_len'] + 1, cfg['heads'], 128,
+                              dtype=torch.bfloat16, device=device)
 
     def step(qs, ks, vs, dos, timed):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
         marks[0].record(stream)
         with torch.no_grad():
-            _, lse = kernels.dense_attention(qs, ks, vs, scale, True,
-                                             used=cfg['used'])
-            marks[1].record(stream)
             heat_sum = 0.0
-            for g in groups:
-                tl = clip.get(g.shape)
-                lse_t = tiling.gather_lse(lse, tl, g.heads)
-                qt = tiling.gather_tiles(qs, tl, g.heads)
-                kt = tiling.gather_tiles(ks, tl, g.heads)
-                heat = heatmap.teacher_heat(
-                    qt, kt, lse_t, tl,
-                    torch.arange(tl.n_tiles, device=device), 'sum')
-                heat_sum = heat_sum + heat.sum()
-                del qt, kt, lse_t
+            if fused:
+                tiles = []
+                for g in groups:
+                    tl = clip.get(g.shape)
+                    tiles.append([tiling.gather_tiles(t, tl, g.heads)
+                                  for t in (qs, ks, vs)])
+                marks[1].record(stream)
+                for g, (qt, kt, vt) in zip(groups, tiles):
+                    tl = clip.get(g.shape)
+                    out_t, _, heat = heatmap.fused_dense_heat(qt, kt, vt, tl,
+                                                              'sum')
+                    tiling.scatter_tiles_(teacher_out, out_t, tl, g.heads)
+                    heat_sum = heat_sum + heat.sum()
+                del tiles
+            else:
+                _, lse = kernels.dense_attention(qs, ks, vs, scale, True,
+                                                 used=cfg['used'])
+                marks[1].record(stream)
+                for g in groups:
+                    tl = clip.get(g.shape)
+                    lse_t = tiling.gather_lse(lse, tl, g.heads)
+                    qt = tiling.gather_tiles(qs, tl, g.heads)
+                    kt = tiling.gather_tiles(ks, tl, g.heads)
+                    heat = heatmap.teacher_heat(
+                        qt, kt, lse_t, tl,
+                        torch.arange(tl.n_tiles, device=device), 'sum')
+                    heat_sum = heat_sum + heat.sum()
+                    del qt, kt, lse_t
             marks[2].record(stream)
         leaves = [t.detach().requires_grad_(True) for t in (qs, ks, vs)]
         with torch.enable_grad():
@@ -720,10 +752,35 @@ def run_train_step(args, cfg):
     heat_flops = sum(2.0 * (clip.get(g.shape).n_tiles * 128) ** 2 * 128 *
                      g.heads.numel() for g in groups)
     dense_flops = 4.0 * used ** 2 * 128 * heads
+    # The fused pass runs the dense attention over the tile-ordered rows
+    # (padding slots included) and no second QK^T.
+    fused_exec_flops = sum(4.0 * (clip.get(g.shape).n_tiles * 128) ** 2 *
+                           128 * g.heads.numel() for g in groups)
     sparse_flops = 3.5 * blocks * BLOCK_FLOPS  # fwd + bwd (2.5x fwd)
     total = dense_flops + heat_flops + sparse_flops
     peaks = load_peaks()
     peak = peaks['bf16_tflops']
+    bwd_tflops = 2.5 * blocks * BLOCK_FLOPS / stages['student_bwd'] / 1e9
+    if fused:
+        achieved = fused_exec_flops / stages['teacher_fused'] / 1e9
+        stage_tflops = {
+            'teacher_fused_executed': achieved,
+            'teacher_reference_accounting': (dense_flops + heat_flops) /
+                                            stages['teacher_fused'] / 1e9,
+            'student_bwd_attention_equiv': bwd_tflops}
+        kernel = ('bsa_fwd_kernel<heat> (fused dense + LSE + heat, '
+                  'executed FLOPs over tile-ordered rows)')
+    else:
+        achieved = dense_flops / stages['dense_fwd_lse'] / 1e9
+        stage_tflops = {
+            'dense_fwd_lse': achieved,
+            'heat': heat_flops / stages['heat'] / 1e9,
+            'student_bwd_attention_equiv': bwd_tflops}
+        kernel = 'bsa_fwd_kernel (dense mode)'
+    roofline = {'bound': 'tensor', 'kernel': kernel, 'achieved': achieved,
+                'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
+                'traffic': None,
+                'peak_source': f'{peaks["source"]} bf16 burst'}
     line = {
         'metric': METRIC, 'value': ms, 'unit': 'ms/step', 'n_gpus': 1,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
@@ -740,26 +797,21 @@ def run_train_step(args, cfg):
         'algorithmic_tflop': total / 1e12,
         'effective_tflops': total / (ms * 1e-3) / 1e12,
         'frac_of_peak': total / (ms * 1e-3) / 1e12 / peak,
-        'stage_tflops': {
-            'dense_fwd_lse': dense_flops / stages['dense_fwd_lse'] / 1e9,
-            'heat': heat_flops / stages['heat'] / 1e9,
-            'student_bwd_attention_equiv': 2.5 * blocks * BLOCK_FLOPS /
-                                           stages['student_bwd'] / 1e9},
-        'roofline': {
-            'bound': 'tensor', 'kernel': 'bsa_fwd_kernel (dense mode)',
-            'achieved': dense_flops / stages['dense_fwd_lse'] / 1e9,
-            'peak': peak, 'unit': 'TFLOP/s',
-            'frac': dense_flops / stages['dense_fwd_lse'] / 1e9 / peak,
-            'traffic': None,
-            'peak_source': f'{peaks["source"]} bf16 burst'},
+        'teacher': args.teacher,
+        'stage_tflops': stage_tflops,
+        'roofline': roofline,
         'e2e': {'value': e2e_ms, 'unit': 'ms/step', 'steps': e2e_steps,
                 'h2d_bytes_per_step': 4 * q.numel() * 2,
                 'd2h_bytes_per_step': 4},
-        # Ours per step: dense fwd; per group gather_lse, gather q, k, heat
-        # (4), student fwd gather+pool q, k, embed, logits, select, transposed
+        # Ours per step. Teacher, separate: dense fwd, then per group
+        # gather_lse, gather q, k, heat (1 + 4 per group); fused: per group
+        # gather q, k, v, keep-all lists, fused pass, scatter (6). Student
+        # per group: fwd gather+pool q, k, embed, logits, select, transposed
         # lists, gather v, attention, scatter (9 + 1), backward gather dO,
         # prep, dq, dkdv, scatter x3 (7).
-        'gpu_launches': args.steps * (1 + 21 * len(groups)),
+        'gpu_launches': args.steps * (
+            (6 * len(groups)) if fused else (1 + 4 * len(groups))) +
+            args.steps * 17 * len(groups),
         'clocks': clocks.summary(),
         'query_tile_heads': n_tiles,
     }

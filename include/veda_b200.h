@@ -271,6 +271,36 @@ int veda_teacher_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                       int64_t n_q, int32_t reduce_sum, float* heat,
                       float softmax_scale, void* stream);
 
+/* ---- (f) fused dense forward + LSE + teacher heat -------------------------- */
+
+/* Workspace bytes veda_bsa_fwd_heat needs (one [n_tiles][128] fp32 scratch
+ * per SM of the current device). */
+int64_t veda_bsa_fwd_heat_workspace(int64_t n_tiles);
+
+/* The fused teacher pass the reference plans in
+ * docs/features/veda_kernel.md:285-288: dense attention of one head group in
+ * tile order (every query tile against the key tiles of the given lists,
+ * normally all non-empty tiles), writing out, the natural-log LSE
+ * [H', n_tiles*128] (row stride 1) and the teacher heat [H', n_tiles,
+ * n_tiles] of every (query tile, key tile) block in the same pass
+ * (miowtion/veda/heatmap.py:36-99 semantics): reduce_sum == 0 gives
+ * max_r exp(bf16(max_k q.k) * scale - L_r) (the reference's rounding of the
+ * scores, applied to the row maximum, which is the same by monotonicity);
+ * reduce_sum != 0 gives sum_r sum_k exp(q.k * scale - L_r) from the fp32
+ * scores the softmax already has. Padding query rows contribute nothing;
+ * blocks not walked keep whatever heat holds (the caller zeroes it). The
+ * lists are those of veda_bsa_fwd with R = n_tiles. */
+int veda_bsa_fwd_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                      const void* k, int64_t k_stride_n, int64_t k_stride_h,
+                      const void* v, int64_t v_stride_n, int64_t v_stride_h,
+                      int32_t n_heads, int64_t n_tiles,
+                      const int32_t* valid_count, const int32_t* part_cnt,
+                      const int32_t* part_idx, const int32_t* full_cnt,
+                      const int32_t* full_idx, int64_t ld_idx, void* out,
+                      int64_t out_stride_n, int64_t out_stride_h, float* lse,
+                      int32_t reduce_sum, float* heat, float softmax_scale,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ---- (f) tile search: oracle relative error ------------------------------- */
 
 /* Workspace bytes veda_rel_mse needs for n_rows sampled tiles and n_heads. */

@@ -88,6 +88,12 @@ SIGNATURES = {
     'veda_teacher_heat': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64,
                                   c_ptr, c_i64, c_i64, c_i32, c_i64, c_ptr,
                                   c_ptr, c_i64, c_i32, c_ptr, c_f32, c_ptr]),
+    'veda_bsa_fwd_heat_workspace': (c_i64, [c_i64]),
+    'veda_bsa_fwd_heat': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64,
+                                  c_ptr, c_i64, c_i64, c_i32, c_i64, c_ptr,
+                                  c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
+                                  c_i64, c_i64, c_ptr, c_i32, c_ptr, c_f32,
+                                  c_ptr, c_i64, c_ptr]),
     'veda_rel_mse_workspace': (c_i64, [c_i64, c_i32]),
     'veda_rel_mse': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_i64, c_ptr,
                              c_ptr, c_i64, c_i32, c_ptr, c_ptr, c_i64, c_ptr]),

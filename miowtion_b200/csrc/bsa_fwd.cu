@@ -64,8 +64,10 @@ constexpr uint32_t kTmemCols = 512;
 // are read from global memory).
 constexpr int kListCap = 1024;
 // Exchange between the four warps of a row: partial maxima [block parity][4
-// key quarters][128 rows] and partial sums [4 key quarters][128 rows].
-constexpr int kExchangeFloats = 2 * 4 * 128 + 4 * 128;
+// key quarters][128 rows] and partial sums [4 key quarters][128 rows]; for
+// the fused heat, the partial sums of each block [block parity][4][128] and
+// the rows' log-sum-exp [128].
+constexpr int kExchangeFloats = 2 * 4 * 128 + 4 * 128 + 2 * 4 * 128 + 128;
 constexpr int kSmemBytes = (2 + 2 * kRing) * kTileBytes + kListCap * 4 +
                            kExchangeFloats * 4 + 512 + 1024;
 
@@ -92,7 +94,9 @@ enum Bar {
   kOFree = 25,      // the epilogue has read O (16 warps)
   kDrainQk = 26,    // MMAs in flight after an abort, per issuer
   kDrainPv = 27,
-  kNumBars = 28
+  kHeatIn = 28,     // fused heat: an item's row maxima / sums stored (16)
+  kHeatOut = 29,    // fused heat: the item's heat written (16)
+  kNumBars = 30
 };
 
 struct FwdParams {
@@ -113,6 +117,14 @@ struct FwdParams {
   float scale_log2;
   int dense;     // dense mode: every key tile [0, n_kv_tiles), keys < used
   int64_t used;  // dense mode only
+  // Fused teacher heat (the kHeat kernel): heat [H, n_q, n_kv] at
+  // h * heat_sh + qt * heat_sq + kv; per CTA a [n_kv][128] scratch of each
+  // (block, row): the bf16-rounded raw score maximum (max mode) or the
+  // log2 of the row's exponential sum over the block (sum mode).
+  float* heat;
+  int64_t heat_sh, heat_sq;
+  float* heat_scratch;
+  int heat_sum;
   unsigned int* status;
 };
 
@@ -314,6 +326,7 @@ __device__ __forceinline__ uint32_t block_record(const Block& b) {
          (b.ka >= 1 ? kRecLater : 0u);
 }
 
+template <bool kHeat>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                    const __grid_constant__ CUtensorMap map_k,
@@ -343,7 +356,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int b = 0; b < kNumBars; ++b) {
       uint32_t count = 1;
       if (b >= kPFull0 && b < kPFull1 + kSBufs) count = kSoftmaxWarps / 2;
-      if (b == kOFree) count = kSoftmaxWarps;
+      if (b == kOFree || b == kHeatIn || b == kHeatOut) count = kSoftmaxWarps;
       mbar_init(&bars[b], count);
     }
     *abort = 0;
@@ -592,6 +605,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     float* xmax = s_xchg;            // [block parity][key quarter][row]
     float* xsum = s_xchg + 2 * 512;  // [key quarter][row]
+    float* xbs = xsum + 512;         // [block parity][key quarter][row]
+    float* s_hl = xbs + 2 * 512;     // [row] log2-sum-exp (fused heat)
+    // Fused heat: this CTA's scratch, the previous block's partial sum and
+    // the reference maximum it used, and the items whose heat was written.
+    float* hs = nullptr;
+    if constexpr (kHeat)
+      hs = p.heat_scratch +
+           static_cast<int64_t>(blockIdx.x) * p.n_kv_tiles * kTile;
+    float bsum_prev = 0.f, mref_prev = 0.f;
+    int heat_items = 0;
     const uint32_t t_o = tmem + kSBufs * 128 + kq * 32 + lane_base;
     Stream st;
     st.init(p, blockIdx.x, gridDim.x, true);
@@ -653,9 +676,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float pm = row_max32(sc);
         float* xm = xmax + xb * 512 + row;
         xm[kq * 128] = pm;
+        if constexpr (kHeat) {
+          // The previous block's partial sum travels with this block's max.
+          if (p.heat_sum && j > 0) xbs[(xb ^ 1) * 512 + kq * 128 + row] =
+              bsum_prev;
+        }
         row_sync(1 + quarter);
-        const float mb = max3(fmaxf(xm[0], xm[128]), xm[256], xm[384]) *
-                         p.scale_log2;
+        const float raw_max = max3(fmaxf(xm[0], xm[128]), xm[256], xm[384]);
+        const float mb = raw_max * p.scale_log2;
+        if constexpr (kHeat) {
+          if (kq == 0) {
+            if (!p.heat_sum) {
+              // The reference rounds every score to bf16 before its max;
+              // rounding is monotonic, so rounding the max is the same.
+              hs[j * kTile + row] = __bfloat162float(__float2bfloat16_rn(
+                  raw_max));
+            } else if (j > 0) {
+              const float* xs = xbs + (xb ^ 1) * 512 + row;
+              hs[(j - 1) * kTile + row] =
+                  mref_prev +
+                  lg2_approx((xs[0] + xs[128]) + (xs[256] + xs[384]));
+            }
+          }
+        }
         bool rescale = false;
         float alpha = 1.0f;
         if (j == 0) {
@@ -690,14 +733,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[(kq < 2 ? kPFull0 : kPFull1) + sb]);
         l += sum.x + sum.y;
+        if constexpr (kHeat) {
+          bsum_prev = sum.x + sum.y;
+          mref_prev = m_ref;
+        }
       }
       if (!ok) break;
       // ---------------- epilogue of the item ----------------
       float l_row = 0.f;
       if (len > 0) {
         xsum[kq * 128 + row] = l;
+        const int last_par = (st.blk - 1) & 1;
+        if constexpr (kHeat) {
+          if (p.heat_sum) xbs[last_par * 512 + kq * 128 + row] = bsum_prev;
+        }
         row_sync(1 + quarter);
         l_row = (xsum[row] + xsum[128 + row]) + (xsum[256 + row] + xsum[384 + row]);
+        if constexpr (kHeat) {
+          if (kq == 0) {
+            if (p.heat_sum) {
+              const float* xs = xbs + last_par * 512 + row;
+              hs[(len - 1) * kTile + row] =
+                  mref_prev +
+                  lg2_approx((xs[0] + xs[128]) + (xs[256] + xs[384]));
+            }
+            // Padding query rows carry no heat.
+            s_hl[row] = row < p.valid_count[qt]
+                            ? m_ref + lg2_approx(l_row)
+                            : INFINITY;
+          }
+        }
         if (!wait_all(&bars[kODone], ka & 1, abort, p.status)) {
           ok = false;
           break;
@@ -740,6 +805,47 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     : -INFINITY;
         p.lse[q_row * p.lse_stride_row + h * p.lse_stride_h] = lse;
       }
+      if constexpr (kHeat) {
+        if (len > 0) {
+          // Every row's maxima or sums and log-sum-exp are stored: warp w
+          // reduces blocks w, w + 16, ... over the 128 rows.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kHeatIn]);
+          if (!wait_all(&bars[kHeatIn], heat_items & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          float* dst = p.heat + h * p.heat_sh + qt * p.heat_sq;
+          for (int jj = warp; jj < len; jj += kSoftmaxWarps) {
+            float acc = p.heat_sum ? 0.f : -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = lane + 32 * i;
+              const float v = hs[jj * kTile + r];
+              if (p.heat_sum)
+                acc += ex2_approx(v - s_hl[r]);
+              else
+                acc = fmaxf(acc, fmaf(v, p.scale_log2, -s_hl[r]));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+              const float o2 = __shfl_xor_sync(0xffffffffu, acc, off);
+              acc = p.heat_sum ? acc + o2 : fmaxf(acc, o2);
+            }
+            if (lane == 0)
+              dst[st.kv_global(p, jj)] = p.heat_sum ? acc : ex2_approx(acc);
+          }
+          // The scratch and the LSE rows are free for the next item.
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kHeatOut]);
+          if (!wait_all(&bars[kHeatOut], heat_items & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          ++heat_items;
+        }
+      }
       st.next_item(p, true);
     }
   }
@@ -767,22 +873,35 @@ __global__ void zero_rows_kernel(__nv_bfloat16* out, int64_t stride_s,
   if (lse != nullptr && c8 == 0) lse[r * ls + h * lh] = 0.f;
 }
 
-int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk,
-               const CUtensorMap& mv, const FwdParams& p,
-               cudaStream_t stream) {
+int sm_count() {
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;
-    VEDA_CUDA(cudaGetDevice(&dev));
-    VEDA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount,
-                                     dev));
-    VEDA_CUDA(cudaFuncSetAttribute(bsa_fwd_kernel,
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+            cudaSuccess)
+      sms = 0;
+  }
+  return sms;
+}
+
+template <bool kHeat>
+int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk,
+               const CUtensorMap& mv, const FwdParams& p,
+               cudaStream_t stream) {
+  static bool configured = false;
+  const int sms = sm_count();
+  if (sms == 0) return set_error(VEDA_ERR_CUDA, "no CUDA device");
+  if (!configured) {
+    VEDA_CUDA(cudaFuncSetAttribute(bsa_fwd_kernel<kHeat>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemBytes));
+    configured = true;
   }
   if (p.n_items == 0) return VEDA_OK;
   const int grid = p.n_items < sms ? p.n_items : sms;
-  bsa_fwd_kernel<<<grid, kFwdThreads, kSmemBytes, stream>>>(mq, mk, mv, p);
+  bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(mq, mk, mv,
+                                                                  p);
   return check_launch("bsa_fwd_kernel");
 }
 
@@ -848,7 +967,74 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   p.dense = 0;
   p.used = 0;
   p.status = device_status_ptr();
-  return launch_fwd(mq, mk, mv, p, as_stream(stream));
+  return launch_fwd<false>(mq, mk, mv, p, as_stream(stream));
+}
+
+extern "C" int64_t veda_bsa_fwd_heat_workspace(int64_t n_kv_tiles) {
+  return static_cast<int64_t>(sm_count()) * n_kv_tiles * kTile *
+         static_cast<int64_t>(sizeof(float));
+}
+
+extern "C" int veda_bsa_fwd_heat(
+    const void* q, int64_t q_stride_n, int64_t q_stride_h, const void* k,
+    int64_t k_stride_n, int64_t k_stride_h, const void* v, int64_t v_stride_n,
+    int64_t v_stride_h, int32_t n_heads, int64_t n_tiles,
+    const int32_t* valid_count, const int32_t* part_cnt,
+    const int32_t* part_idx, const int32_t* full_cnt, const int32_t* full_idx,
+    int64_t ld_idx, void* out, int64_t out_stride_n, int64_t out_stride_h,
+    float* lse, int32_t reduce_sum, float* heat, float softmax_scale,
+    void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = require_sm100("veda_bsa_fwd_heat");
+  if (rc != VEDA_OK) return rc;
+  VEDA_REQUIRE(q && k && v && out && valid_count && part_cnt && part_idx &&
+                   full_cnt && full_idx && heat,
+               "q, k, v, out, valid_count, the four lists and heat are "
+               "required");
+  VEDA_REQUIRE(n_heads >= 1 && n_tiles >= 1, "bad shape");
+  VEDA_REQUIRE(ld_idx >= n_tiles, "ld_idx must be >= n_tiles");
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 30), "too many tiles");
+  VEDA_REQUIRE(softmax_scale > 0.f, "softmax_scale must be positive");
+  VEDA_REQUIRE(reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   out_stride_n % 8 == 0 && out_stride_h % 8 == 0,
+               "out must be 16-byte aligned with strides multiple of 8");
+  VEDA_REQUIRE(workspace != nullptr &&
+                   workspace_bytes >= veda_bsa_fwd_heat_workspace(n_tiles),
+               "workspace too small (veda_bsa_fwd_heat_workspace)");
+  CUtensorMap mq, mk, mv;
+  rc = make_tile_map(&mq, q, n_tiles * kTile, n_heads, q_stride_n,
+                     q_stride_h, "q");
+  if (rc == VEDA_OK)
+    rc = make_tile_map(&mk, k, n_tiles * kTile, n_heads, k_stride_n,
+                       k_stride_h, "k");
+  if (rc == VEDA_OK)
+    rc = make_tile_map(&mv, v, n_tiles * kTile, n_heads, v_stride_n,
+                       v_stride_h, "v");
+  if (rc != VEDA_OK) return rc;
+  FwdParams p{};
+  p.n_heads = n_heads;
+  p.n_q_tiles = static_cast<int>(n_tiles);
+  p.n_kv_tiles = static_cast<int>(n_tiles);
+  p.n_items = static_cast<int>(n_tiles * n_heads);
+  p.valid_count = valid_count;
+  p.part_cnt = part_cnt;
+  p.part_idx = part_idx;
+  p.full_cnt = full_cnt;
+  p.full_idx = full_idx;
+  p.ld_idx = ld_idx;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_n = out_stride_n;
+  p.out_stride_h = out_stride_h;
+  p.lse = lse;
+  p.lse_stride_row = 1;
+  p.lse_stride_h = n_tiles * kTile;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.heat = heat;
+  p.heat_sh = n_tiles * n_tiles;
+  p.heat_sq = n_tiles;
+  p.heat_scratch = static_cast<float*>(workspace);
+  p.heat_sum = reduce_sum != 0;
+  p.status = device_status_ptr();
+  return launch_fwd<true>(mq, mk, mv, p, as_stream(stream));
 }
 
 extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
@@ -901,5 +1087,5 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
   p.dense = 1;
   p.used = used;
   p.status = device_status_ptr();
-  return launch_fwd(mq, mk, mv, p, as_stream(stream));
+  return launch_fwd<false>(mq, mk, mv, p, as_stream(stream));
 }

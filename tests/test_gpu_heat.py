@@ -94,3 +94,53 @@ def test_heat_rejects_bad_reduce(teacher):
     with pytest.raises(ValueError):
         heatmap.teacher_heat(qt, kt, torch.from_numpy(lse_t).to(DEV), lay,
                              torch.arange(2), 'mean')
+
+
+@pytest.fixture(scope='module')
+def fused_case():
+    """The padded layout with v too, and the oracle's dense teacher in tile
+    order."""
+    spec = dict(inputs.PADDED, heads=4, group_heads=[0, 2, 3])
+    lay = tiling.build_tile_layout(
+        [tiling.TiledSpan(s, tuple(g), tiling.TileShape(*sh))
+         for s, g, sh in spec['spans']], spec['used'], spec['seq_len'], DEV)
+    ref = vo.build_tile_layout(
+        [vo.Span(s, tuple(g), tuple(sh)) for s, g, sh in spec['spans']],
+        spec['used'], spec['seq_len'])
+    q, k, v = inputs.qkv(spec['seq_len'], spec['heads'], 128, spec['seed'],
+                         torch.bfloat16)
+    heads = spec['group_heads']
+    out, lse = vo.dense_attention(np32(q), np32(k), np32(v), spec['used'],
+                                  return_lse=True)
+    hd = torch.tensor(heads, device=DEV)
+    qt, kt, vt = (tiling.gather_tiles(t.to(DEV), lay, hd) for t in (q, k, v))
+    out_t = vo.gather_tiles(out, ref, heads)
+    lse_t = vo.gather_lse(lse, ref, heads)
+    return lay, ref, qt, kt, vt, out_t, lse_t
+
+
+@pytest.mark.parametrize('reduce', ['max', 'sum'])
+def test_fused_dense_heat_matches_oracle(fused_case, reduce):
+    """One pass gives the dense teacher (out, LSE) and the heat. The max
+    mode follows the reference's bf16 score rounding exactly (it rounds the
+    row maximum); the sum mode uses the fp32 scores of the softmax, so it
+    is compared with the unrounded oracle."""
+    lay, ref, qt, kt, vt, out_t, lse_t = fused_case
+    out, lse, heat = heatmap.fused_dense_heat(qt, kt, vt, lay, reduce)
+    valid = ref.slot_valid.astype(bool)
+    np.testing.assert_allclose(np32(out)[valid], out_t[valid], rtol=2e-2,
+                               atol=2e-2)
+    np.testing.assert_allclose(np32(lse).T[valid], lse_t[valid], atol=2e-3)
+    want = vo.teacher_heat(np32(qt), np32(kt), lse_t, ref,
+                           np.arange(lay.n_tiles), reduce,
+                           round_scores=(reduce == 'max'))
+    atol = 1e-5 if reduce == 'max' else 1e-4
+    np.testing.assert_allclose(heat.cpu().numpy(), want, rtol=3e-2,
+                               atol=atol)
+    # The separate heat kernel on the fused pass's own LSE agrees closely.
+    sep = heatmap.teacher_heat(qt, kt, lse.T.contiguous(), lay,
+                               torch.arange(lay.n_tiles), reduce)
+    if reduce == 'max':
+        torch.testing.assert_close(heat, sep, rtol=1e-3, atol=1e-6)
+    else:
+        torch.testing.assert_close(heat, sep, rtol=3e-2, atol=1e-4)
