@@ -21,6 +21,7 @@ import dataclasses
 import torch
 
 from miowtion_b200 import compensation
+from miowtion_b200 import heatmap
 from miowtion_b200 import kernels
 from miowtion_b200 import mask as veda_mask
 from miowtion_b200 import plan as veda_plan
@@ -335,3 +336,118 @@ class SparseStudent:
                              f'{q.shape[1]}')
         out = torch.zeros_like(q)
         return out.index_copy(1, heads, torch.cat(parts, 1))
+
+
+DENSE_BACKENDS = ('auto', 'b200', 'fa4', 'sdpa')
+
+
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    used: int, return_lse: bool = False,
+                    backend: str = 'auto'
+                    ) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Full attention of rows [0, used) among themselves, the reference's
+    `h3.attention.dense_attention` (h3/attention.py:28-102): out [S, H, D]
+    zero on padding rows, lse [S, H] fp32 natural log (0 on padding rows).
+
+    Every CUDA backend name runs the B200 dense kernel; 'math' (the
+    reference's fp32 CPU path) has none here.
+
+    Raises:
+        ValueError: On an unknown backend.
+        NotImplementedError: For 'math', or off B200.
+    """
+    if backend == 'math':
+        raise NotImplementedError("backend 'math' is the reference's fp32 "
+                                  'CPU path; this package runs on B200 only')
+    if backend not in DENSE_BACKENDS:
+        raise ValueError(f'unknown dense backend {backend!r}')
+    return kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5, return_lse,
+                                   used=used)
+
+
+class DenseAttention:
+    """The dense teacher AttentionFn (h3/model.py:48-58)."""
+
+    def __init__(self, used: int, backend: str = 'auto'):
+        self.used = used
+        self.backend = backend
+
+    def __call__(self, q, k, v, layer_index):
+        del layer_index
+        return dense_attention(q, k, v, self.used, backend=self.backend)[0]
+
+
+ORACLE_TARGETS = ('mass', 'max', 'mean')
+
+
+class OracleStudent:
+    """Block sparsity masked by the true block statistic instead of a
+    predictor (attention.py:474-588): an upper bound for the router.
+
+    Targets: 'mass' (the block's summed attention probability), 'max' (its
+    peak probability), 'mean' (mass per real key row). Per head group, one
+    fused pass gives the dense teacher's normalisation and the block heat of
+    every query tile (`heatmap.fused_dense_heat`; its dense output is not
+    used), the training rules select the blocks from the video rows' heat,
+    and the sparse kernel attends over them. Cost is dense plus sparse per
+    layer: an analysis mode, never an inference path.
+
+    `allow_reference_kernel` is accepted for the reference's signature; there
+    is no reference kernel here, so it changes nothing.
+    """
+
+    def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
+                 target: str = 'mass', allow_reference_kernel: bool = False):
+        del allow_reference_kernel
+        if target not in ORACLE_TARGETS:
+            raise ValueError(f'target must be one of {ORACLE_TARGETS}: '
+                             f'{target!r}')
+        reason = kernels.unavailable_reason(clip.device)
+        if reason is not None:
+            raise RuntimeError(
+                f'OracleStudent needs the B200 block-sparse kernels '
+                f'({reason}); refusing to fall back silently')
+        if clip.config.budget_rule != 'topk':
+            raise NotImplementedError("only the 'topk' budget rule has a "
+                                      'B200 kernel')
+        self.clip = clip
+        self.plan = plan
+        self.target = target
+        self.calls = {'sparse': 0, 'dense': 0}
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 layer_index: int) -> torch.Tensor:
+        used = self.clip.layout.used
+        if layer_index in self.clip.config.dense_layers:
+            self.calls['dense'] += 1
+            return dense_attention(q, k, v, used)[0]
+        self.calls['sparse'] += 1
+        seq_len = q.shape[0]
+        out = torch.empty_like(q)
+        if used < seq_len:
+            out[used:] = 0
+        for group in self.plan.head_groups(layer_index, self.clip.device):
+            tile_layout = self.clip.get(group.shape)
+            for heads in group.heads.split(
+                    _chunk_heads(tile_layout, self.clip.config.collect_bytes)):
+                self._attend(q, k, v, tile_layout, heads, out)
+        return out
+
+    @torch.no_grad()
+    def _attend(self, q, k, v, tile_layout: tiling.TileLayout,
+                heads: torch.Tensor, out: torch.Tensor) -> None:
+        q_tiles = tiling.gather_tiles(q, tile_layout, heads)
+        k_tiles = tiling.gather_tiles(k, tile_layout, heads)
+        v_tiles = tiling.gather_tiles(v, tile_layout, heads)
+        reduce = 'max' if self.target == 'max' else 'sum'
+        _, _, heat = heatmap.fused_dense_heat(q_tiles, k_tiles, v_tiles,
+                                              tile_layout, reduce)
+        heat = heat[:, :tile_layout.n_video_tiles]
+        if self.target == 'mean':
+            counts = tile_layout.valid_count.clamp(min=1).to(heat.dtype)
+            heat = heat / counts[None, None, :]
+        lists = veda_mask.select_block_lists(heat, tile_layout,
+                                             self.clip.blocks(tile_layout))
+        o_tiles = kernels.block_sparse_attention_lists(
+            q_tiles, k_tiles, v_tiles, lists, tile_layout)
+        tiling.scatter_rows_(out, o_tiles, tile_layout, heads)

@@ -557,17 +557,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// dkdv: key-major. TMEM: S^T [0,128) (P^T over columns 0-31 and 64-95),
-// dP^T [128,256) (dS^T likewise), dV [256,384), dK [384,512).
+// dkdv: key-major. Each block's 128 query columns run as two halves of 64
+// so that one half's elementwise work overlaps the other half's MMAs.
+// TMEM, per half h: S^T [128h, 128h+64) (P^T over its columns 0-15 and
+// 32-47), dP^T [128h+64, 128h+128) (dS^T likewise); dV [256,384),
+// dK [384,512).
 // ---------------------------------------------------------------------------
 enum KvBar {
   kKtFull = 0,     // K and V of the key tile landed
   kKtEmpty,        // the item's last S^T and dP^T MMAs finished
   kQdFull,         // [2] Q, dO, L and D of the block landed (block parity)
   kQdEmpty = kQdFull + 2,  // [2] the block's MMAs finished reading them
-  kStFull = kQdEmpty + 2,  // S^T and dP^T of the block
-  kPdsFull,        // P^T and dS^T written (8 warps)
-  kKvDone,         // the item's last dV/dK MMAs finished
+  kStFull = kQdEmpty + 2,  // [2 halves] S^T and dP^T of the block's half
+  kPdsFull = kStFull + 2,  // [2 halves] P^T and dS^T written (8 warps)
+  kKvDone = kPdsFull + 2,  // the item's last dV/dK MMAs finished
   kKvFree,         // the epilogue has read dV and dK (8 warps)
   kKvDrain,
   kKvItemFull,                       // [kQueue]
@@ -604,9 +607,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int64_t n_rows_q = static_cast<int64_t>(p.n_q_tiles) * kTile;
   if (tid == 0) {
     for (int b = 0; b < kKvNumBars; ++b)
-      mbar_init(&bars[b], (b == kPdsFull || b == kKvFree) ? 8
-                          : (b >= kKvItemEmpty)         ? kQueueReaders
-                                                        : 1);
+      mbar_init(&bars[b], (b == kPdsFull || b == kPdsFull + 1 || b == kKvFree)
+                              ? 8
+                          : (b >= kKvItemEmpty) ? kQueueReaders
+                                                : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -675,59 +679,110 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mbar_wait(&bars[kQdFull + (b & 1)], (b >> 1) & 1, &never, nullptr);
     }
   } else if (warp == kMma) {
-    constexpr uint32_t idesc_kmaj = idesc_bf16(128, 128, false, false);
+    // Per block j, halves a (queries 0-63) and b (64-127):
+    //   S^T_a, dP^T_a, S^T_b, dP^T_b of block 0 of the item, then for each j
+    //   dV, dK += half a of j; S^T_a, dP^T_a of j + 1;
+    //   dV, dK += half b of j; S^T_b, dP^T_b of j + 1,
+    // so the tensor core has the other half's MMAs while the compute warps
+    // turn one half's S^T, dP^T into P^T, dS^T.
+    constexpr uint32_t idesc_st = idesc_bf16(128, 64, false, false);
     constexpr uint32_t idesc_bmn = idesc_bf16(128, 128, false, true);
     const uint32_t k_lo = sw128_desc_lo(smem_u32(s_k), 16);
     const uint32_t v_lo = sw128_desc_lo(smem_u32(s_v), 16);
     const uint32_t qd_lo = sw128_desc_lo(smem_u32(s_qd), 16);
     const uint32_t qdmn_lo = sw128_desc_lo(smem_u32(s_qd), kHalfBytes);
-    const uint32_t t_s = tmem, t_dp = tmem + 128;
     const uint32_t t_dv = tmem + 256, t_dk = tmem + 384;
+    // S^T and dP^T of half h of the block in stage `stage` (query rows
+    // 64h .. 64h + 63 of the Q and dO tiles: 8 KB into each 64-column box).
+    auto issue_st = [&](int stage, int h) {
+      const uint32_t q_lo = qd_lo + stage * 2 * kTileUnits + h * (8192 >> 4);
+      const uint32_t do_lo = q_lo + kTileUnits;
+      const uint32_t t_s = tmem + h * 128, t_dp = t_s + 64;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+        umma_ss_warp(t_s, k_lo + off, q_lo + off, idesc_st, kk > 0);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+        umma_ss_warp(t_dp, v_lo + off, do_lo + off, idesc_st, kk > 0);
+      }
+      umma_commit_warp(&bars[kStFull + h]);
+    };
+    // dV += P^T dO and dK += dS^T Q over half h's 64 queries (4 K-steps
+    // each; P^T of queries 16kk' .. lies in columns 32(kk'/2) + 8(kk'%2)).
+    auto issue_acc = [&](int stage, int h, bool first) {
+      const uint32_t qmn = qdmn_lo + stage * 2 * kTileUnits;
+      const uint32_t domn = qmn + kTileUnits;
+      const uint32_t t_p = tmem + h * 128, t_ds = t_p + 64;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_ts_warp(t_dv, t_p + (kk >> 1) * 32 + (kk & 1) * 8,
+                     domn + (4 * h + kk) * 128, idesc_bmn,
+                     (kk > 0 || h > 0 || !first) ? 1u : 0u);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_ts_warp(t_dk, t_ds + (kk >> 1) * 32 + (kk & 1) * 8,
+                     qmn + (4 * h + kk) * 128, idesc_bmn,
+                     (kk > 0 || h > 0 || !first) ? 1u : 0u);
+    };
     ListStream st;
     st.init(&p.lists, &queue, false, false);
-    while (st.valid()) {
-      const bool first = st.j == 0, last = st.j == st.len - 1;
-      const int ka = st.ka;
-      const int stage = st.blk & 1;
-      if (first && !wait_all(&bars[kKtFull], ka & 1, abort, p.status)) break;
-      if (!wait_all(&bars[kQdFull + stage], (st.blk >> 1) & 1, abort,
+    bool run = true;
+    while (run && st.valid()) {
+      const int ka = st.ka, len = st.len;
+      const int blk0 = st.blk;
+      if (!wait_all(&bars[kKtFull], ka & 1, abort, p.status) ||
+          !wait_all(&bars[kQdFull + (blk0 & 1)], (blk0 >> 1) & 1, abort,
                     p.status))
         break;
       tc_fence_after();
-      const uint32_t q_lo = qd_lo + stage * 2 * kTileUnits;
-      const uint32_t do_lo = q_lo + kTileUnits;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-        umma_ss_warp(t_s, k_lo + off, q_lo + off, idesc_kmaj, kk > 0);
+      issue_st(blk0 & 1, 0);
+      issue_st(blk0 & 1, 1);
+      if (len == 1) umma_commit_warp(&bars[kKtEmpty]);
+      for (int j = 0; j < len; ++j) {
+        const int blk = blk0 + j;
+        const int stage = blk & 1;
+        const bool first = j == 0, last = j == len - 1;
+        // The item's first dV/dK overwrite the accumulators, which the
+        // epilogue must have read.
+        if (first && ka > 0 &&
+            !wait_all(&bars[kKvFree], (ka - 1) & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        if (!wait_all(&bars[kPdsFull + 0], blk & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        issue_acc(stage, 0, first);
+        if (!last) {
+          if (!wait_all(&bars[kQdFull + ((blk + 1) & 1)],
+                        ((blk + 1) >> 1) & 1, abort, p.status)) {
+            run = false;
+            break;
+          }
+          tc_fence_after();
+          issue_st((blk + 1) & 1, 0);
+        }
+        if (!wait_all(&bars[kPdsFull + 1], blk & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        issue_acc(stage, 1, first);
+        umma_commit_warp(&bars[kQdEmpty + stage]);
+        if (!last) {
+          issue_st((blk + 1) & 1, 1);
+          if (j + 1 == len - 1) umma_commit_warp(&bars[kKtEmpty]);
+        } else {
+          umma_commit_warp(&bars[kKvDone]);
+        }
       }
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-        umma_ss_warp(t_dp, v_lo + off, do_lo + off, idesc_kmaj, kk > 0);
-      }
-      umma_commit_warp(&bars[kStFull]);
-      if (last) umma_commit_warp(&bars[kKtEmpty]);
-      // dV += P^T dO, dK += dS^T Q: the first block of an item overwrites
-      // the accumulators, which the epilogue must have read.
-      if (first && ka > 0 &&
-          !wait_all(&bars[kKvFree], (ka - 1) & 1, abort, p.status))
-        break;
-      if (!wait_all(&bars[kPdsFull], st.blk & 1, abort, p.status)) break;
-      tc_fence_after();
-      const uint32_t qmn = qdmn_lo + stage * 2 * kTileUnits;
-      const uint32_t domn = qmn + kTileUnits;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_ts_warp(t_dv, t_s + packed_col(kk), domn + kk * 128, idesc_bmn,
-                     (kk > 0 || !first) ? 1u : 0u);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_ts_warp(t_dk, t_dp + packed_col(kk), qmn + kk * 128, idesc_bmn,
-                     (kk > 0 || !first) ? 1u : 0u);
-      umma_commit_warp(&bars[kQdEmpty + stage]);
-      if (last) umma_commit_warp(&bars[kKvDone]);
-      st.next_block();
+      if (!run) break;
+      for (int j = 0; j < len; ++j) st.next_block();
     }
     if (*abort) {
       volatile int never = 0;
@@ -759,30 +814,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       // Keys past the tile's valid prefix take no part: P = dS = 0.
       const bool key_ok = row < p.valid_count[kt];
-      for (int j = 0; j < len; ++j) {
+      // Warp (wq, quarter) takes queries 32 wq .. 32 wq + 31 of each half.
+      const int wq = half;
+      for (int j = 0; j < len && ok; ++j) {
         const int blk = st.blk;
         st.j += 1;
         st.blk += 1;
-        if (!wait_all(&bars[kStFull], blk & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const float* vl = s_vec + (blk & 1) * 256;  // L*log2e, then D
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int col0 = half * 64 + c * 32;
+        for (int h = 0; h < 2; ++h) {
+          if (!wait_all(&bars[kStFull + h], blk & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int q0 = h * 64 + wq * 32;  // query column of the block
+          const uint32_t t_s = tmem + h * 128 + wq * 32 + lane_base;
+          const uint32_t t_dp = t_s + 64;
           uint32_t s[32], dp[32];
-          tmem_ld32(tmem + col0 + lane_base, s);
-          tmem_ld32(tmem + 128 + col0 + lane_base, dp);
+          tmem_ld32(t_s, s);
+          tmem_ld32(t_dp, dp);
           tmem_wait_ld();
           uint32_t wp[16], wd[16];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 l4 =
-                *reinterpret_cast<const float4*>(vl + col0 + 4 * i);
+            const float4 l4 = *reinterpret_cast<const float4*>(vl + q0 + 4 * i);
             const float4 d4 =
-                *reinterpret_cast<const float4*>(vl + 128 + col0 + 4 * i);
+                *reinterpret_cast<const float4*>(vl + 128 + q0 + 4 * i);
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
             const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
             float pr[4], ds[4];
@@ -799,11 +857,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             wd[2 * i] = pack_bf16(ds[0], ds[1]);
             wd[2 * i + 1] = pack_bf16(ds[2], ds[3]);
           }
-          tmem_st16(tmem + half * 64 + c * 16 + lane_base, wp);
-          tmem_st16(tmem + 128 + half * 64 + c * 16 + lane_base, wd);
+          // P^T and dS^T of these 32 queries over the first 16 of this
+          // warp's own 32 columns of S^T and dP^T.
+          tmem_st16(t_s, wp);
+          tmem_st16(t_dp, wd);
+          tmem_wait_st();
+          arrive_warp(&bars[kPdsFull + h]);
         }
-        tmem_wait_st();
-        arrive_warp(&bars[kPdsFull]);
       }
       if (!ok) break;
       if (!wait_all(&bars[kKvDone], ka & 1, abort, p.status)) break;

@@ -140,3 +140,67 @@ def test_student_backward_matches_oracle():
                                    err_msg=f'd{name}')
         assert (g[used:] == 0).all()
         assert not (g[:used] == 0).all()
+
+
+@pytest.mark.parametrize('target', ['max', 'mass', 'mean'])
+def test_oracle_student_matches_oracle(target):
+    """OracleStudent (attention.py:474-588): blocks chosen by the true block
+    statistic of the dense teacher, then the sparse kernel. The oracle
+    follows the same steps (heat of every video query tile, the training
+    selection rules, block-sparse attention, scatter); the heat's sum mode
+    is the unrounded one the fused pass computes."""
+    from miowtion_b200 import attention as veda_attention
+    from miowtion_b200 import mask as veda_mask
+    from miowtion_b200 import plan as veda_plan
+    spec = dict(inputs.PADDED, heads=3)
+    (start, grid, shape), = spec['spans']
+    packed = veda_attention.PackedLayout(
+        spec['seq_len'], spec['used'],
+        (veda_attention.VideoSpan(start, tuple(grid)),))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=spec['ratio']))
+    clip = veda_attention.ClipTiling(packed, config, DEV)
+    plan = veda_plan.TilePlan('o', tuple(grid), [tiling.TileShape(*shape)],
+                              [[0] * spec['heads']])
+    q, k, v = inputs.qkv(spec['seq_len'], spec['heads'], 128, spec['seed'],
+                         torch.bfloat16)
+    student = veda_attention.OracleStudent(clip, plan, target)
+    got = student(*(t.to(DEV) for t in (q, k, v)), 0)
+    ref = vo.build_tile_layout([vo.Span(start, tuple(grid), tuple(shape))],
+                               spec['used'], spec['seq_len'])
+    qf, kf, vf = (t.float().numpy() for t in (q, k, v))
+    _, lse = vo.dense_attention(qf, kf, vf, spec['used'], return_lse=True)
+    heads = np.arange(spec['heads'])
+    qt, kt, vt = (vo.gather_tiles(x, ref, heads) for x in (qf, kf, vf))
+    rows = np.arange(ref.n_video_tiles)
+    heat = vo.teacher_heat(qt, kt, vo.gather_lse(lse, ref, heads), ref, rows,
+                           'max' if target == 'max' else 'sum',
+                           round_scores=(target == 'max'))
+    if target == 'mean':
+        heat = heat / np.maximum(ref.valid_count, 1)[None, None, :]
+    blocks = vo.column_blocks(ref, vo.Budget(ratio=spec['ratio']))
+    index, keep = vo.select_video_blocks(heat, ref, blocks, rows)
+    mask = vo.dense_block_mask(index, keep, ref)
+    ot = vo.block_sparse_attention(qt, kt, vt, mask, ref.valid_count)
+    want = np.zeros((spec['seq_len'] + 1, spec['heads'], 128), np.float32)
+    vo.scatter_tiles(want, ot, ref, heads)
+    used = spec['used']
+    np.testing.assert_allclose(got.float().cpu().numpy()[:used], want[:used],
+                               rtol=2e-2, atol=2e-2)
+    assert student.calls == {'sparse': 1, 'dense': 0}
+
+
+def test_dense_attention_fn_matches_oracle():
+    from miowtion_b200 import attention as veda_attention
+    spec = inputs.PADDED
+    q, k, v = inputs.qkv(spec['seq_len'], 2, 128, spec['seed'],
+                         torch.bfloat16)
+    fn = veda_attention.DenseAttention(spec['used'])
+    got = fn(*(t.to(DEV) for t in (q, k, v)), 3)
+    want, _ = vo.dense_attention(*(t.float().numpy() for t in (q, k, v)),
+                                 spec['used'])
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=2e-2,
+                               atol=2e-2)
+    with pytest.raises(ValueError):
+        veda_attention.dense_attention(q.to(DEV), k.to(DEV), v.to(DEV),
+                                       spec['used'], backend='nope')
