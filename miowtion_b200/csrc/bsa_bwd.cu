@@ -273,23 +273,19 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* out, int64_t o_sn,
 }
 
 // ---------------------------------------------------------------------------
-// dq: query-major. TMEM: S [0,128), dP [128,256), dQ [256,384), and dS
-// (bf16 pairs, 64 columns) double-buffered at [384,448) and [448,512). The
-// compute warps free S and dP as soon as they have read them, so the MMA
-// warp issues S and dP of block j+1 ahead of dQ of block j and the tensor
-// core works through block j's elementwise phase; at an item's end dQ goes
-// first so the epilogue is not held up.
+// dq: query-major. Each block's 128 key columns run as two halves of 64 so
+// that one half's elementwise work overlaps the other half's MMAs. TMEM, per
+// half h: S [128h, 128h+64) (dS over its columns 0-15 and 32-47), dP
+// [128h+64, 128h+128); dQ [256,384).
 // ---------------------------------------------------------------------------
 enum DqBar {
   kQFull = 0,      // Q and dO of the item landed
   kQEmpty,         // the item's last S and dP MMAs finished
   kKvFull,         // [2] K and V of the block landed (stage = block parity)
   kKvEmpty = kKvFull + 2,  // [2] the block's MMAs finished reading them
-  kSdFull = kKvEmpty + 2,  // S and dP of the block
-  kSdFree,         // the compute warps have read S and dP (8 warps)
-  kDsFull,         // dS written (8 warps)
-  kDsBufFree,      // [2] the dQ MMA of the block last using the dS buffer
-  kDqDone = kDsBufFree + 2,  // the item's last dQ MMA finished
+  kSdFull = kKvEmpty + 2,  // [2 halves] S and dP of the block's half
+  kDsFull = kSdFull + 2,   // [2 halves] dS written (8 warps)
+  kDqDone = kDsFull + 2,   // the item's last dQ MMA finished
   kDqFree,         // the epilogue has read dQ (8 warps)
   kDqDrain,
   kDqItemFull,                       // [kQueue]
@@ -322,9 +318,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int lane = tid % 32;
   if (tid == 0) {
     for (int b = 0; b < kDqNumBars; ++b)
-      mbar_init(&bars[b], (b == kSdFree || b == kDsFull || b == kDqFree) ? 8
-                          : (b >= kDqItemEmpty)                      ? kQueueReaders
-                                                                     : 1);
+      mbar_init(&bars[b], (b == kDsFull || b == kDsFull + 1 || b == kDqFree)
+                              ? 8
+                          : (b >= kDqItemEmpty) ? kQueueReaders
+                                                : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -387,80 +384,102 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mbar_wait(&bars[kKvFull + (b & 1)], (b >> 1) & 1, &never, nullptr);
     }
   } else if (warp == kMma) {
-    constexpr uint32_t idesc_kmaj = idesc_bf16(128, 128, false, false);
+    // Per block j, halves a (keys 0-63) and b (64-127):
+    //   S_a, dP_a, S_b, dP_b of block 0 of the item, then for each j
+    //   dQ += half a of j; S_a, dP_a of j + 1;
+    //   dQ += half b of j; S_b, dP_b of j + 1.
+    constexpr uint32_t idesc_sd = idesc_bf16(128, 64, false, false);
     constexpr uint32_t idesc_bmn = idesc_bf16(128, 128, false, true);
     const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
     const uint32_t do_lo = sw128_desc_lo(smem_u32(s_do), 16);
     const uint32_t kv_lo = sw128_desc_lo(smem_u32(s_kv), 16);
     const uint32_t kvmn_lo = sw128_desc_lo(smem_u32(s_kv), kHalfBytes);
-    const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
-    const uint32_t t_ds = tmem + 384;  // [2] x 64 columns
-    // The block whose dQ MMAs are still to be issued.
-    struct Pending {
-      bool valid, first, last;
-      int ka, blk;
-    } prev{false, false, false, 0, 0};
-    // dQ += dS K of a block (dS in buffer blk & 1, K in stage blk & 1).
-    auto issue_dq = [&](const Pending& d) -> bool {
-      // The item's first dQ overwrites dQ: the epilogue must have read it.
-      if (d.first && d.ka > 0 &&
-          !wait_all(&bars[kDqFree], (d.ka - 1) & 1, abort, p.status))
-        return false;
-      if (!wait_all(&bars[kDsFull], d.blk & 1, abort, p.status)) return false;
-      tc_fence_after();
-      const int stage = d.blk & 1;
-      const uint32_t kmn = kvmn_lo + stage * 2 * kTileUnits;
-      const uint32_t t_a = t_ds + (d.blk & 1) * 64;
+    const uint32_t t_dq = tmem + 256;
+    // S and dP of key half h of the tiles in stage `stage` (key rows
+    // 64h .. 64h + 63: 8 KB into each 64-column box).
+    auto issue_sd = [&](int stage, int h) {
+      const uint32_t k_lo = kv_lo + stage * 2 * kTileUnits + h * (8192 >> 4);
+      const uint32_t v_lo = k_lo + kTileUnits;
+      const uint32_t t_s = tmem + h * 128, t_dp = t_s + 64;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_ts_warp(t_dq, t_a + kk * 8, kmn + kk * 128, idesc_bmn,
-                     (kk > 0 || !d.first) ? 1u : 0u);
-      umma_commit_warp(&bars[kKvEmpty + stage]);
-      umma_commit_warp(&bars[kDsBufFree + (d.blk & 1)]);
-      if (d.last) umma_commit_warp(&bars[kDqDone]);
-      return true;
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+        umma_ss_warp(t_s, q_lo + off, k_lo + off, idesc_sd, kk > 0);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+        umma_ss_warp(t_dp, do_lo + off, v_lo + off, idesc_sd, kk > 0);
+      }
+      umma_commit_warp(&bars[kSdFull + h]);
+    };
+    // dQ += dS K over half h's 64 keys (4 K-steps; dS of keys 16kk' ..
+    // lies in columns 32(kk'/2) + 8(kk'%2) of the half's S).
+    auto issue_dq = [&](int stage, int h, bool first) {
+      const uint32_t kmn = kvmn_lo + stage * 2 * kTileUnits;
+      const uint32_t t_a = tmem + h * 128;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_ts_warp(t_dq, t_a + (kk >> 1) * 32 + (kk & 1) * 8,
+                     kmn + (4 * h + kk) * 128, idesc_bmn,
+                     (kk > 0 || h > 0 || !first) ? 1u : 0u);
     };
     ListStream st;
     st.init(&p.lists, &queue, false, false);
     bool run = true;
     while (run && st.valid()) {
-      const bool first = st.j == 0, last = st.j == st.len - 1;
-      const int ka = st.ka;
-      const int blk = st.blk;
-      const int stage = blk & 1;
-      // At an item's end, the last dQ before the next item's S and dP.
-      if (prev.valid && prev.last) {
-        if (!issue_dq(prev)) break;
-        prev.valid = false;
-      }
-      if (first && !wait_all(&bars[kQFull], ka & 1, abort, p.status)) break;
-      if (!wait_all(&bars[kKvFull + stage], (blk >> 1) & 1, abort, p.status))
-        break;
-      // S and dP of the previous block have been read.
-      if (blk > 0 &&
-          !wait_all(&bars[kSdFree], (blk - 1) & 1, abort, p.status))
+      const int ka = st.ka, len = st.len;
+      const int blk0 = st.blk;
+      if (!wait_all(&bars[kQFull], ka & 1, abort, p.status) ||
+          !wait_all(&bars[kKvFull + (blk0 & 1)], (blk0 >> 1) & 1, abort,
+                    p.status))
         break;
       tc_fence_after();
-      const uint32_t k_lo = kv_lo + stage * 2 * kTileUnits;
-      const uint32_t v_lo = k_lo + kTileUnits;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-        umma_ss_warp(t_s, q_lo + off, k_lo + off, idesc_kmaj, kk > 0);
+      issue_sd(blk0 & 1, 0);
+      issue_sd(blk0 & 1, 1);
+      if (len == 1) umma_commit_warp(&bars[kQEmpty]);
+      for (int j = 0; j < len; ++j) {
+        const int blk = blk0 + j;
+        const int stage = blk & 1;
+        const bool first = j == 0, last = j == len - 1;
+        // The item's first dQ overwrites dQ: the epilogue must have read it.
+        if (first && ka > 0 &&
+            !wait_all(&bars[kDqFree], (ka - 1) & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        if (!wait_all(&bars[kDsFull + 0], blk & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        issue_dq(stage, 0, first);
+        if (!last) {
+          if (!wait_all(&bars[kKvFull + ((blk + 1) & 1)],
+                        ((blk + 1) >> 1) & 1, abort, p.status)) {
+            run = false;
+            break;
+          }
+          tc_fence_after();
+          issue_sd((blk + 1) & 1, 0);
+        }
+        if (!wait_all(&bars[kDsFull + 1], blk & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        issue_dq(stage, 1, first);
+        umma_commit_warp(&bars[kKvEmpty + stage]);
+        if (!last) {
+          issue_sd((blk + 1) & 1, 1);
+          if (j + 1 == len - 1) umma_commit_warp(&bars[kQEmpty]);
+        } else {
+          umma_commit_warp(&bars[kDqDone]);
+        }
       }
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
-        umma_ss_warp(t_dp, do_lo + off, v_lo + off, idesc_kmaj, kk > 0);
-      }
-      umma_commit_warp(&bars[kSdFull]);
-      if (last) umma_commit_warp(&bars[kQEmpty]);
-      if (prev.valid && !issue_dq(prev)) break;
-      prev = Pending{true, first, last, ka, blk};
-      st.next_block();
-      run = st.ok;
+      if (!run) break;
+      for (int j = 0; j < len; ++j) st.next_block();
     }
-    if (run && prev.valid) issue_dq(prev);
     if (*abort) {
       volatile int never = 0;
       umma_commit_warp(&bars[kDqDrain]);
@@ -489,34 +508,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       const float l2 = p.lse2[h * n_rows_q + q_row];
       const float dlt = p.delta[h * n_rows_q + q_row];
-      for (int j = 0; j < len; ++j) {
+      // Warp (wq, quarter) takes keys 32 wq .. 32 wq + 31 of each half.
+      const int wq = half;
+      for (int j = 0; j < len && ok; ++j) {
         const int blk = st.blk;
         const int valid = j < st.pc ? p.valid_count[st.entry(j)] : kTile;
         st.j += 1;
         st.blk += 1;
-        if (!wait_all(&bars[kSdFull], blk & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // dS goes to buffer blk & 1, free once the dQ MMA of block blk - 2
-        // has finished.
-        if (blk >= 2 && !wait_all(&bars[kDsBufFree + (blk & 1)],
-                                  ((blk >> 1) - 1) & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        const uint32_t t_ds = tmem + 384 + (blk & 1) * 64 + lane_base;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int col0 = half * 64 + c * 32;
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!wait_all(&bars[kSdFull + hh], blk & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int key0 = hh * 64 + wq * 32;  // key column of the block
+          const uint32_t t_s = tmem + hh * 128 + wq * 32 + lane_base;
           uint32_t s[32], dp[32];
-          tmem_ld32(tmem + col0 + lane_base, s);
-          tmem_ld32(tmem + 128 + col0 + lane_base, dp);
+          tmem_ld32(t_s, s);
+          tmem_ld32(t_s + 64, dp);
           tmem_wait_ld();
-          // Both of this block's S and dP reads are done: the MMA warp may
-          // overwrite them with the next block's.
-          if (c == 1) arrive_warp(&bars[kSdFree]);
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -526,17 +537,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               const int cc = 2 * i + e;
               float pr = ex2_approx(
                   fmaf(__uint_as_float(s[cc]), p.scale_log2, -l2));
-              if (col0 + cc >= valid) pr = 0.f;
+              if (key0 + cc >= valid) pr = 0.f;
               d2[e] = pr * (__uint_as_float(dp[cc]) - dlt);
             }
             w[i] = pack_bf16(d2[0], d2[1]);
           }
-          // dS of these 32 keys: bf16 pairs, 16 columns of the buffer
-          // (keys 0-63 in columns 0-31, keys 64-127 in 32-63).
-          tmem_st16(t_ds + half * 32 + c * 16, w);
+          // dS of these 32 keys over the first 16 of this warp's own 32
+          // columns of S.
+          tmem_st16(t_s, w);
+          tmem_wait_st();
+          arrive_warp(&bars[kDsFull + hh]);
         }
-        tmem_wait_st();
-        arrive_warp(&bars[kDsFull]);
       }
       if (!ok) break;
       if (!wait_all(&bars[kDqDone], ka & 1, abort, p.status)) break;
