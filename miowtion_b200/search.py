@@ -10,7 +10,8 @@ errors). For every scored layer, candidate shape and head
 3. block score = the peak probability of each (query tile, key tile) block,
    from the dense teacher's LSE (`teacher_heat`, reduce 'max');
 4. keep blocks by the training rules (budget, Bresenham, diagonal, column
-   blocks; global key tiles always kept), without global query rows;
+   blocks; global key tiles always kept), without global query rows, as
+   the block lists of the sampled rows (`select_block_lists`);
 5. the sparse output of the sampled query tiles alone (the row-subset
    forward of `block_sparse_attention`);
 6. rel_mse = sum ||o_sparse - o_dense||^2 / sum ||o_dense||^2 over their real
@@ -129,14 +130,15 @@ def _oracle_rel_mse_kernels(q, k, v, dense_out, lse, tile_layout, blocks,
         lse_t = tiling.gather_lse(lse, tile_layout, heads)
         heat = heatmap.teacher_heat(q_t, k_t, lse_t, tile_layout, rows)
         del q_t
-        selection = veda_mask.select_video_blocks(heat, tile_layout, blocks,
-                                                  rows)
-        block_mask = veda_mask.dense_block_mask(selection, tile_layout,
-                                                global_rows=False)
+        # The selection's block lists of the sampled rows, without global
+        # query rows (dense_block_mask(global_rows=False) then index_lists,
+        # in one kernel).
+        lists = veda_mask.select_block_lists(heat, tile_layout, blocks, rows,
+                                             global_rows=False)
         # The sampled query tiles alone, straight from the packed rows.
         q_s = tiling.gather_tile_rows(q, tile_layout, rows, heads)
-        o_sparse = kernels.block_sparse_attention(q_s, k_t, v_t, block_mask,
-                                                  tile_layout)
+        o_sparse = kernels.block_sparse_attention_lists(q_s, k_t, v_t, lists,
+                                                        tile_layout)
         errors.append(rel_mse(o_sparse, dense_out, seq_row, heads))
     return torch.cat(errors)
 
