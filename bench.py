@@ -425,6 +425,8 @@ def main():
         barrier()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
+        dense = dense_comparison(cfg, q, k, v) if world == 1 else None
+
     vals = torch.tensor([ms, e2e_ms, stages.get('attention', 0.0),
                          float(blocks)], dtype=torch.float64, device=device)
     if world > 1:
@@ -469,7 +471,9 @@ def main():
             'roofline': {
                 'bound': 'tensor', 'kernel': 'bsa_fwd_kernel',
                 'achieved': attn_tflops, 'peak': peak, 'unit': 'TFLOP/s',
-                'frac': attn_tflops / peak, 'traffic': None,
+                'frac': attn_tflops / peak,
+                'traffic': FWD_TRAFFIC.get(args.config) if world == 1
+                           else None,
                 'peak_source': f'{peaks["source"]} bf16 burst'},
             # Bytes of all ranks per step (each rank copies its q, k, v in
             # and its output back).
@@ -479,6 +483,15 @@ def main():
             'gpu_launches': args.steps * launches_per_step(plan, world),
             'clocks': clk,
         }
+        if dense is not None:
+            best = min(dense, key=dense.get)
+            line['dense'] = {
+                'ms': dense, 'unit': 'ms/layer', 'fastest': best,
+                'speedup_vs_fastest_dense': dense[best] / ms,
+                'note': 'dense attention of the same q, k, v over the used '
+                        'rows (no permutation, predictor or top-k), timed '
+                        'with CUDA events; the sparse layer is the whole '
+                        'Veda path'}
         if world == 1 and not args.no_cpu_baseline:
             cpu_ms, n_heads, threads, _ = cpu_baseline(cfg)
             line['cpu_baseline'] = {
@@ -491,6 +504,55 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# DRAM bytes (read + write) of one bsa_fwd_kernel launch, from one ncu
+# capture of the kernel at config 2 (dram__bytes_read.sum +
+# dram__bytes_write.sum). Other configs have no capture: null.
+FWD_TRAFFIC = {'cfg2': 863.3e6}
+
+
+def dense_comparison(cfg, q, k, v, reps=3):
+    """ms per call of dense attention of the same q, k, v over the used rows:
+    this library's dense kernel and torch's fused SDPA backends (cuDNN,
+    flash) where they run on this device. Each backend is timed after one
+    warm-up call; backends that raise are left out."""
+    from miowtion_b200 import kernels
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    used = cfg['used']
+    out = {}
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    with torch.no_grad():
+        out['b200_dense_kernel'] = timed(
+            lambda: kernels.dense_attention(q, k, v, 128 ** -0.5, False,
+                                            used=used))
+        # [1, H, used, D] views in the layout SDPA wants (copies made once,
+        # outside the timed calls).
+        qs, ks, vs = (t[:used].permute(1, 0, 2).unsqueeze(0).contiguous()
+                      for t in (q, k, v))
+        for name, backend in (('sdpa_cudnn', SDPBackend.CUDNN_ATTENTION),
+                              ('sdpa_flash', SDPBackend.FLASH_ATTENTION)):
+            try:
+                with sdpa_kernel(backend):
+                    out[name] = timed(lambda: F.scaled_dot_product_attention(
+                        qs, ks, vs))
+            except RuntimeError:
+                continue
+        del qs, ks, vs
+    return out
 
 
 def run_stage(args, cfg):
