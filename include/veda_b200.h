@@ -78,6 +78,19 @@ int veda_build_layout(const veda_span_t* spans, int32_t n_spans,
                       int64_t used, int64_t seq_len, int64_t n_tiles,
                       int64_t* perm, int32_t* valid_count, void* stream);
 
+/* The same permutation in box order, for attention that reads the packed
+ * tensors in place (veda_bsa_fwd_packed). Replaces the gather index of
+ * miowtion/veda/tiling.py:214-275 on that path: box_perm[n_tiles*128]
+ * (int64) holds, for slot `pos` of a video tile, the packed row at position
+ * (pos / (sh*sw), (pos / sw) % sh, pos % sw) of the tile's (st, sh, sw) box
+ * (-1 outside the grid); global tiles keep perm's prefix order.
+ * key_mask[n_tiles*4] (uint32) has bit (slot % 32) of word slot / 32 set
+ * for every real row. */
+int veda_build_box_layout(const veda_span_t* spans, int32_t n_spans,
+                          int64_t used, int64_t seq_len, int64_t n_tiles,
+                          int64_t* box_perm, uint32_t* key_mask,
+                          void* stream);
+
 /* ---- a2/a3/a12/a14: permutation, pooling, inverse ---------------------- */
 
 /* Replaces miowtion/kernels/tile_gather_triton.py:156-209 (gather_tiles /
@@ -92,6 +105,19 @@ int veda_gather_pool(const void* x, int64_t x_stride_s, int64_t x_stride_h,
                      int64_t n_tiles, const int64_t* heads, int32_t n_heads,
                      void* out, int64_t out_stride_n, int64_t out_stride_h,
                      float* feats, float* sq, float* var, void* stream);
+
+/* veda_gather_pool with the tile-ordered rows written as shared-memory
+ * images, the key / value input of veda_bsa_fwd_packed (kv_tile_order 2):
+ * image [H', n_tiles, 2, 128, 64] bf16, tile (h, t) a contiguous 32 KB
+ * block of two 64-column halves, each 128 rows x 128 bytes whose 16-byte
+ * chunk c of row r sits at position c ^ (r % 8) (the 128-byte swizzle a
+ * TMA load writes to shared memory). Padding rows are zero. feats as for
+ * veda_gather_pool (NULL to skip). */
+int veda_gather_pool_images(const void* x, int64_t x_stride_s,
+                            int64_t x_stride_h, const int64_t* perm,
+                            const int32_t* valid_count, int64_t n_tiles,
+                            const int64_t* heads, int32_t n_heads,
+                            void* image, float* feats, void* stream);
 
 /* Replaces miowtion/kernels/tile_gather_triton.py:212-224 (scatter_tiles_):
  *   out[perm[slot], heads[h], :] = tiled[slot, h, :] for perm[slot] >= 0. */
@@ -200,6 +226,50 @@ int veda_bsa_fwd(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                  const int32_t* full_idx, int64_t ld_idx, void* out,
                  int64_t out_stride_n, int64_t out_stride_h, float* lse,
                  float softmax_scale, void* stream);
+
+/* The same forward reading the packed tensors in place, for one head group
+ * of miowtion/veda/attention.py:724-743: one launch replaces the gather of
+ * q (miowtion/veda/tiling.py:278-297), the forward
+ * (miowtion/kernels/fa4.py:299-377) and the scatter of the output
+ * (miowtion/veda/tiling.py:300-312).
+ *   q [S, H, D] bf16 (row stride stride_s, head stride stride_h,
+ *   total_heads heads): the video tiles of the spans (at most 2, as given
+ *   to veda_build_layout) are read as 5D TMA boxes (t, h, w, head, d), the
+ *   layout's global tiles from q_glob [n_global*128, H', D] (tile order,
+ *   strides glob_stride_n / glob_stride_h; NULL when n_tiles == n_video);
+ *   k, v: with kv_tile_order == 1, tile-ordered [n_tiles*128, H', D]
+ *   (strides kv_stride_n / kv_stride_h, as veda_gather_pool writes them);
+ *   with kv_tile_order == 2, tile images [H', n_tiles, 32 KB] as
+ *   veda_gather_pool_images writes them, each loaded with one bulk copy
+ *   (the fastest form; partial tiles in both masked by valid_count); with
+ *   kv_tile_order == 0, packed like q and read in place too (global tiles
+ *   from k_glob / v_glob, partial tiles masked by key_mask; no copies, but
+ *   the 5D loads make the kernel about a third slower);
+ *   heads[H'] (device int64): the packed head of each head of the group,
+ *   in [0, total_heads) (a head outside reads zeros and writes nothing);
+ *   box_perm, key_mask: veda_build_box_layout of the same spans;
+ *   lists as for veda_bsa_fwd with rows = all n_tiles query tiles (tile ids
+ *   are those of the tile order);
+ *   out [S, H, D] (strides out_stride_s, out_stride_h): the rows
+ *   box_perm >= 0 of heads[] are written, nothing else.
+ * Rows of a partial video tile sit in box order rather than as a prefix;
+ * the masked softmax is the same, so only the fp32 summation order differs
+ * from veda_bsa_fwd. */
+int veda_bsa_fwd_packed(const void* q, const void* k, const void* v,
+                        int64_t stride_s, int64_t stride_h, int64_t seq_len,
+                        int32_t total_heads, int32_t kv_tile_order,
+                        int64_t kv_stride_n, int64_t kv_stride_h,
+                        const void* q_glob, const void* k_glob,
+                        const void* v_glob, int64_t glob_stride_n,
+                        int64_t glob_stride_h, const veda_span_t* spans,
+                        int32_t n_spans, int64_t n_tiles, int64_t n_video,
+                        const int64_t* heads, int32_t n_heads,
+                        const int64_t* box_perm, const uint32_t* key_mask,
+                        const int32_t* valid_count, const int32_t* part_cnt,
+                        const int32_t* part_idx, const int32_t* full_cnt,
+                        const int32_t* full_idx, int64_t ld_idx, void* out,
+                        int64_t out_stride_s, int64_t out_stride_h,
+                        float softmax_scale, void* stream);
 
 /* Replaces miowtion/kernels/fa4.py:185-205 (dense_attention) and the
  * row-subset contract of miowtion/h3/attention.py:28-102: full attention of
@@ -362,6 +432,16 @@ int veda_compensate(const void* o_kept, int64_t ok_stride_n,
  * fp32 row-major. */
 int veda_probe_umma(const void* a, const void* b, float* d, int32_t mode,
                     void* stream);
+
+/* Failure-detection check; the reference has no device-side waits and so no
+ * counterpart. Launches one CTA of two warps that wait on mbarriers nothing
+ * ever completes, through the same bounded wait every kernel here uses:
+ * warp 0 with a limit of limit_ns (1 ms .. 4 s), warp 1 with the library's
+ * 4 s limit, which it leaves as soon as warp 0 raises the CTA's abort flag.
+ * The kernel records VEDA_ERR_TIMEOUT in the device status word and returns;
+ * completed[2] (device int32) receives 1 for each warp whose wait completed
+ * (0 expected). No fault and no hang: the context stays usable. */
+int veda_expire_wait(int64_t limit_ns, int32_t* completed, void* stream);
 
 #ifdef __cplusplus
 }

@@ -50,9 +50,14 @@ SIGNATURES = {
     'veda_supported_device': (c_i32, []),
     'veda_build_layout': (c_i32, [ctypes.POINTER(Span), c_i32, c_i64, c_i64,
                                   c_i64, c_ptr, c_ptr, c_ptr]),
+    'veda_build_box_layout': (c_i32, [ctypes.POINTER(Span), c_i32, c_i64,
+                                      c_i64, c_i64, c_ptr, c_ptr, c_ptr]),
     'veda_gather_pool': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_i64,
                                  c_ptr, c_i32, c_ptr, c_i64, c_i64, c_ptr,
                                  c_ptr, c_ptr, c_ptr]),
+    'veda_gather_pool_images': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_ptr,
+                                        c_i64, c_ptr, c_i32, c_ptr, c_ptr,
+                                        c_ptr]),
     'veda_scatter': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_i32,
                              c_ptr, c_i64, c_i64, c_ptr]),
     'veda_gather_lse': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr,
@@ -74,6 +79,13 @@ SIGNATURES = {
                              c_i64, c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr,
                              c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i64, c_i64,
                              c_ptr, c_f32, c_ptr]),
+    'veda_bsa_fwd_packed': (c_i32, [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64,
+                                    c_i32, c_i32, c_i64, c_i64, c_ptr, c_ptr,
+                                    c_ptr, c_i64, c_i64, ctypes.POINTER(Span),
+                                    c_i32, c_i64, c_i64, c_ptr, c_i32, c_ptr,
+                                    c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
+                                    c_i64, c_ptr, c_i64, c_i64, c_f32,
+                                    c_ptr]),
     'veda_dense_fwd': (c_i32, [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64,
                                c_i64, c_i32, c_ptr, c_i64, c_i64, c_ptr,
                                c_i64, c_i64, c_f32, c_ptr]),
@@ -104,6 +116,7 @@ SIGNATURES = {
                                 c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i64,
                                 c_i64, c_f32, c_ptr, c_i64, c_ptr]),
     'veda_probe_umma': (c_i32, [c_ptr, c_ptr, c_ptr, c_i32, c_ptr]),
+    'veda_expire_wait': (c_i32, [c_i64, c_ptr, c_ptr]),
 }
 
 _LOCK = threading.Lock()
@@ -157,6 +170,18 @@ def device_status(reset: bool = True) -> int:
     status = c_i32(0)
     call('veda_device_status', ctypes.byref(status), 1 if reset else 0)
     return status.value
+
+
+def raise_on_device_status() -> None:
+    """Reads and clears the device status word; raises RuntimeError when a
+    kernel's bounded wait expired since the last read (the kernel returned
+    early, so its outputs are not to be trusted)."""
+    status = device_status(reset=True)
+    if status == VEDA_ERR_TIMEOUT:
+        raise RuntimeError('a Veda kernel wait timed out on the device; its '
+                           'outputs are incomplete')
+    if status != 0:
+        raise RuntimeError(f'device status word holds {status}')
 
 
 def stream_ptr(device: torch.device | None = None) -> int:

@@ -269,6 +269,10 @@ class SparseStudent:
                 tile_layout: tiling.TileLayout, heads: torch.Tensor,
                 out: torch.Tensor) -> None:
         """Sparse attention of some heads of one group, scattered to out."""
+        if (not self.clip.config.compensated
+                and kernels.packed_supported(tile_layout)):
+            self._attend_packed(q, k, v, layer_index, tile_layout, heads, out)
+            return
         ev = self.events
         t = ev.start('permute_pool')
         q_tiles, feats_q = tiling.gather_and_pool(q, tile_layout, heads)
@@ -299,6 +303,38 @@ class SparseStudent:
         ev.stop(t)
         t = ev.start('unpermute')
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
+        ev.stop(t)
+        self.last_lists = lists
+
+    def _attend_packed(self, q, k, v, layer_index: int,
+                       tile_layout: tiling.TileLayout, heads: torch.Tensor,
+                       out: torch.Tensor) -> None:
+        """`_attend` without the tile-ordered q and output: pooling reads q
+        in place, and the attention kernel reads query tiles as boxes of the
+        packed q and writes out directly (no gather of q, no scatter). Key
+        and value tiles are gathered once into shared-memory images, which
+        the kernel loads with one bulk copy each."""
+        ev = self.events
+        t = ev.start('permute_pool')
+        feats_q = tiling.pool_features(q, tile_layout, heads)
+        k_img, feats_k = tiling.gather_images(k, tile_layout, heads,
+                                              pool=True)
+        v_img = tiling.gather_images(v, tile_layout, heads)
+        ev.stop(t)
+        with torch.no_grad():
+            t = ev.start('score')
+            logits = self.predictor.layers[layer_index](feats_q, feats_k,
+                                                        heads)
+            ev.stop(t)
+            t = ev.start('topk')
+            lists = veda_mask.select_block_lists(
+                logits[:, :tile_layout.n_video_tiles], tile_layout,
+                self.clip.blocks(tile_layout))
+            ev.stop(t)
+        t = ev.start('attention')
+        kernels.block_sparse_attention_packed(q, k_img, v_img, lists,
+                                              tile_layout, heads, out,
+                                              kv_tiles='images')
         ev.stop(t)
         self.last_lists = lists
 

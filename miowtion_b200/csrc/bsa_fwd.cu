@@ -79,6 +79,9 @@ constexpr int kPolyCols = 8;
 
 constexpr int kSBufs = 3;
 
+// Video spans the packed mode reads in place (one 5D tensor map each).
+constexpr int kMaxPackedSpans = 2;
+
 enum Bar {
   kQFull = 0,       // [2] per Q buffer (item parity)
   kQEmpty = 2,      // [2] the item's last QK finished reading Q
@@ -125,8 +128,89 @@ struct FwdParams {
   int64_t heat_sh, heat_sq;
   float* heat_scratch;
   int heat_sum;
+  // Packed mode (veda_bsa_fwd_packed): the output goes to row
+  // box_perm[slot], head head_ids[h], of the packed [S, H, D] tensor, and
+  // query tiles are read in place (box_q); key and value tiles either from
+  // tile-ordered copies or in place too (box_kv). Read in place, a video
+  // tile is a box of the packed tensor through a 5D map, one per span
+  // (maps.x[1 + s]), and a global tile comes from the gathered copies of
+  // the global tiles (maps.x[0], head h); partial key tiles are masked by
+  // key_mask words (the box order is not a prefix).
+  int packed;
+  int box_kv;
+  int total_heads;  // heads of the packed tensors
+  int n_video;
+  int n_spans;
+  int span_begin[kMaxPackedSpans + 1];
+  int span_nbt[kMaxPackedSpans], span_nbw[kMaxPackedSpans];
+  int span_shape[kMaxPackedSpans][3];
+  // Key and value tiles as shared-memory images (veda_gather_tile_images):
+  // tile (h, kv) is 32 KB at (h * n_kv_tiles + kv) * 32 KB, loaded with one
+  // bulk copy. nullptr: through the tensor maps.
+  const uint8_t* k_img;
+  const uint8_t* v_img;
+  const int64_t* head_ids;
+  const int64_t* box_perm;
+  const uint32_t* key_mask;
   unsigned int* status;
 };
+
+// Tensor maps of q, k and v: [0] the tile-ordered tensors (or, in packed
+// mode, the global tiles), [1 + s] the box map of span s (packed mode).
+struct FwdMaps {
+  CUtensorMap q[1 + kMaxPackedSpans];
+  CUtensorMap k[1 + kMaxPackedSpans];
+  CUtensorMap v[1 + kMaxPackedSpans];
+};
+
+// TMA coordinates of tile `tile` of one tensor (head h of the item, hg its
+// packed head): the map index (0: tile order or global tiles, 1 + s: box map
+// of span s) and the coordinates after the head-dim one.
+struct TileCoords {
+  int map, c1, c2, c3, c4;
+};
+
+__device__ __forceinline__ TileCoords tile_coords(const FwdParams& p, int h,
+                                                  int hg, int tile,
+                                                  bool boxed) {
+  TileCoords c;
+  if (boxed && tile < p.n_video) {
+    const int s = (p.n_spans > 1 && tile >= p.span_begin[1]) ? 1 : 0;
+    const int lt = tile - p.span_begin[s];
+    const int nbt = p.span_nbt[s];
+    const int rest = lt / nbt;
+    const int bh = rest / p.span_nbw[s];
+    c.map = 1 + s;
+    c.c1 = hg;
+    c.c2 = (rest - bh * p.span_nbw[s]) * p.span_shape[s][2];  // w0
+    c.c3 = bh * p.span_shape[s][1];                          // h0
+    c.c4 = (lt - rest * nbt) * p.span_shape[s][0];           // t0
+  } else {
+    c.map = 0;
+    c.c1 = h;
+    c.c2 = (tile - (boxed ? p.n_video : 0)) * kTile;
+    c.c3 = c.c4 = 0;
+  }
+  return c;
+}
+
+// Issues the two 64-column TMA boxes of tile `tile` of one tensor (head h
+// of the item, hg its packed head) into dst, completing on bar.
+__device__ __forceinline__ void load_tile(uint8_t* dst,
+                                          const CUtensorMap* maps,
+                                          uint64_t* bar, const FwdParams& p,
+                                          int h, int hg, int tile,
+                                          bool boxed) {
+  const TileCoords c = tile_coords(p, h, hg, tile, boxed);
+  if (c.map > 0) {
+    tma_load_5d(dst, &maps[c.map], bar, 0, c.c1, c.c2, c.c3, c.c4);
+    tma_load_5d(dst + kHalfBytes, &maps[c.map], bar, 64, c.c1, c.c2, c.c3,
+                c.c4);
+  } else {
+    tma_load_3d(dst, &maps[0], bar, 0, c.c1, c.c2);
+    tma_load_3d(dst + kHalfBytes, &maps[0], bar, 64, c.c1, c.c2);
+  }
+}
 
 // One key block of a slot's stream.
 struct Block {
@@ -328,9 +412,7 @@ __device__ __forceinline__ uint32_t block_record(const Block& b) {
 
 template <bool kHeat>
 __global__ void __launch_bounds__(kFwdThreads, 1)
-    bsa_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
-                   const __grid_constant__ CUtensorMap map_k,
-                   const __grid_constant__ CUtensorMap map_v, FwdParams p) {
+    bsa_fwd_kernel(const __grid_constant__ FwdMaps maps, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -378,17 +460,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // before its first K; end records after the last tiles. The whole warp
     // walks the stream (it copies each item's list to shared memory) and
     // waits converged; lane 0 issues the copies.
-    if (lane == 0) {
-      prefetch_tensor_map(&map_q);
-      prefetch_tensor_map(&map_k);
-      prefetch_tensor_map(&map_v);
+    if (lane < 3 * (1 + kMaxPackedSpans)) {
+      const int m = lane % (1 + kMaxPackedSpans);
+      const bool boxed = lane < 1 + kMaxPackedSpans ? p.packed : p.box_kv;
+      const bool used = boxed ? (m == 0 ? p.n_video < p.n_q_tiles
+                                        : m <= p.n_spans)
+                              : m == 0;
+      const CUtensorMap* base = lane < 1 + kMaxPackedSpans ? maps.q
+                                : lane < 2 * (1 + kMaxPackedSpans) ? maps.k
+                                                                 : maps.v;
+      if (used) prefetch_tensor_map(&base[m]);
     }
     Stream st;
     st.init(p, blockIdx.x, gridDim.x, false);
     int nk = 0, nv = 0;  // K and V tiles loaded
     int q_issued = 0;    // items whose Q was loaded
-    // Key tile, head and record of blocks b - 1 and b - 2.
-    int kv1 = 0, h1 = 0, kv2 = 0, h2 = 0;
+    // Key tile, head (local and packed) and record of blocks b - 1 and
+    // b - 2; the packed head of the current item.
+    int kv1 = 0, h1 = 0, kv2 = 0, h2 = 0, g1 = 0, g2 = 0, hg = 0;
     uint32_t r1 = 0, r2 = 0;
     bool run = true;
     // Waits for a free slot of a ring (n tiles loaded so far); -1 on abort.
@@ -399,20 +488,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         return -1;
       return slot;
     };
-    auto load = [&](const CUtensorMap* map, uint8_t* ring, int full_bar,
-                    int slot, int h, int kv) {
+    auto load = [&](const CUtensorMap* map, const uint8_t* img,
+                    uint8_t* ring, int full_bar, int slot, int h, int g,
+                    int kv) {
       uint8_t* dst = ring + slot * kTileBytes;
       mbar_arrive_expect_tx(&bars[full_bar + slot], kTileBytes);
-      tma_load_3d(dst, map, &bars[full_bar + slot], 0, h, kv * kTile);
-      tma_load_3d(dst + kHalfBytes, map, &bars[full_bar + slot], 64, h,
-                  kv * kTile);
+      if (img != nullptr)
+        bulk_load(dst,
+                  img + (static_cast<int64_t>(h) * p.n_kv_tiles + kv) *
+                            static_cast<int64_t>(kTileBytes),
+                  kTileBytes, &bars[full_bar + slot]);
+      else
+        load_tile(dst, map, &bars[full_bar + slot], p, h, g, kv, p.box_kv);
     };
-    auto load_v = [&](int h, int kv, uint32_t rec) -> bool {
+    auto load_v = [&](int h, int g, int kv, uint32_t rec) -> bool {
       const int slot = slot_of(nv, kVEmpty);
       if (slot < 0) return false;
       if (lane == 0) {
         v_rec[slot] = rec;
-        load(&map_v, s_v, kVFull, slot, h, kv);
+        load(maps.v, p.v_img, s_v, kVFull, slot, h, g, kv);
       }
       __syncwarp();
       ++nv;
@@ -425,6 +519,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int jj = lane; jj < st.len; jj += 32)
             s_list[jj] = st.kv_global(p, jj);
         __syncwarp();
+        hg = p.packed ? static_cast<int>(p.head_ids[b.h]) : b.h;
         // The Q buffer frees after the last QK of the item two back.
         const int qb = b.ka & 1;
         if (b.ka >= 2 && !wait_all(&bars[kQEmpty + qb],
@@ -435,9 +530,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (lane == 0) {
           uint8_t* dst = s_q + qb * kTileBytes;
           mbar_arrive_expect_tx(&bars[kQFull + qb], kTileBytes);
-          tma_load_3d(dst, &map_q, &bars[kQFull + qb], 0, b.h, b.qt * kTile);
-          tma_load_3d(dst + kHalfBytes, &map_q, &bars[kQFull + qb], 64, b.h,
-                      b.qt * kTile);
+          load_tile(dst, maps.q, &bars[kQFull + qb], p, b.h, hg, b.qt,
+                    p.packed);
         }
         __syncwarp();
         q_issued = b.ka + 1;
@@ -453,27 +547,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       if (lane == 0) {
         k_rec[slot] = rec;
-        load(&map_k, s_k, kKFull, slot, b.h, kv);
+        load(maps.k, p.k_img, s_k, kKFull, slot, b.h, hg, kv);
       }
       __syncwarp();
       ++nk;
-      if (nk >= 3 && !load_v(h2, kv2, r2)) {
+      if (nk >= 3 && !load_v(h2, g2, kv2, r2)) {
         run = false;
         break;
       }
       kv2 = kv1;
       h2 = h1;
+      g2 = g1;
       r2 = r1;
       kv1 = kv;
       h1 = b.h;
+      g1 = hg;
       r1 = rec;
       st.next_block(p);
     }
     if (run) {
       // The last V tiles, then an end record in each ring (completing the
       // slot's full barrier without a copy).
-      if (nk >= 2) run = load_v(h2, kv2, r2);
-      if (run && nk >= 1) run = load_v(h1, kv1, r1);
+      if (nk >= 2) run = load_v(h2, g2, kv2, r2);
+      if (run && nk >= 1) run = load_v(h1, g1, kv1, r1);
       int slot = run ? slot_of(nk, kKEmpty) : -1;
       if (slot >= 0) {
         if (lane == 0) {
@@ -623,33 +719,59 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     auto part_kv = [&](int jj) -> int {
       return p.part_idx[st.off + (st.pc - 1 - jj)];
     };
-    auto dense_valid = [&](int jj) -> int {
+    // Valid keys among this warp's 32 of a key tile, as a bit mask: the
+    // first `valid - 32 kq` of a prefix tile, or the packed mode's box mask.
+    auto count_word = [&](int valid) -> uint32_t {
+      const int n = valid - kq * 32;
+      return n >= 32 ? ~0u : (n <= 0 ? 0u : (1u << n) - 1u);
+    };
+    auto tile_word = [&](int kv) -> uint32_t {
+      return p.key_mask != nullptr ? p.key_mask[kv * 4 + kq]
+                                   : count_word(p.valid_count[kv]);
+    };
+    auto dense_word = [&](int jj) -> uint32_t {
       const int64_t rest = p.used - static_cast<int64_t>(jj) * kTile;
-      return rest < kTile ? static_cast<int>(rest) : kTile;
+      return count_word(rest < kTile ? static_cast<int>(rest) : kTile);
     };
     bool ok = true;
     while (ok && st.valid(p)) {
       const int h = st.h, qt = st.qt, len = st.len, ka = st.ka, pc = st.pc;
       float m_ref = -INFINITY;  // running max, in log2 units
       float l = 0.f;            // this warp's part of the row sum
-      // Pipeline: v0 = valid count of block j, v1 of block j + 1 (load in
+      // Output row of this thread's query row (packed mode: from the box
+      // layout, loaded here so that the epilogue does not wait for it).
+      const int64_t slot_row = static_cast<int64_t>(qt) * kTile + row;
+      int64_t out_off = -1;  // element offset of the row's output; -1: none
+      if (p.packed) {
+        const int64_t r = p.box_perm[slot_row];
+        const int64_t hg = p.head_ids[h];
+        // A head outside the tensors reads zeros (TMA bounds) and writes
+        // nothing.
+        if (r >= 0 && hg >= 0 && hg < p.total_heads)
+          out_off = r * p.out_stride_n + hg * p.out_stride_h;
+      } else if (!p.dense || slot_row < p.used) {
+        // Dense mode: rows >= used keep the zeros written before the launch.
+        out_off = slot_row * p.out_stride_n + h * p.out_stride_h;
+      }
+      // Pipeline: v0 = key mask word of block j, v1 of block j + 1 (load in
       // flight), k2 = key tile of block j + 2 if it is partial.
-      int v0 = kTile, v1 = kTile, k2 = 0;
+      uint32_t v0 = ~0u, v1 = ~0u;
+      int k2 = 0;
       if (p.dense) {
-        v0 = dense_valid(0);
-        v1 = dense_valid(1);
+        v0 = dense_word(0);
+        v1 = dense_word(1);
       } else {
-        if (pc > 0) v0 = p.valid_count[part_kv(0)];
-        if (pc > 1) v1 = p.valid_count[part_kv(1)];
+        if (pc > 0) v0 = tile_word(part_kv(0));
+        if (pc > 1) v1 = tile_word(part_kv(1));
         if (pc > 2) k2 = part_kv(2);
       }
       for (int j = 0; j < len; ++j) {
-        const int valid = v0;
+        const uint32_t kmask = v0;
         v0 = v1;
         if (p.dense) {
-          v1 = dense_valid(j + 2);
+          v1 = dense_word(j + 2);
         } else {
-          v1 = j + 2 < pc ? p.valid_count[k2] : kTile;
+          v1 = j + 2 < pc ? tile_word(k2) : ~0u;
           if (j + 3 < pc) k2 = part_kv(j + 3);
         }
         const int blk = st.blk;
@@ -668,10 +790,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld32(t_s, r);
         tmem_wait_ld();
         float* sc = reinterpret_cast<float*>(r);
-        if (valid < kTile) {
+        if (kmask != ~0u) {
 #pragma unroll
           for (int c = 0; c < 32; ++c)
-            if (kq * 32 + c >= valid) sc[c] = -INFINITY;
+            if (!((kmask >> c) & 1u)) sc[c] = -INFINITY;
         }
         const float pm = row_max32(sc);
         float* xm = xmax + xb * 512 + row;
@@ -769,9 +891,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         tc_fence_after();
       }
-      const int64_t q_row = static_cast<int64_t>(qt) * kTile + row;
-      // Dense mode: rows >= used keep the zeros written before the launch.
-      const bool write = !p.dense || q_row < p.used;
+      const int64_t q_row = slot_row;
+      const bool write = out_off >= 0;
       const float inv_l = len > 0 ? 1.0f / l_row : 0.f;
       uint32_t o[32];
       if (len > 0) {
@@ -785,8 +906,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i = 0; i < 32; ++i) o[i] = 0u;
       }
       if (write) {
-        uint4* d4 = reinterpret_cast<uint4*>(p.out + q_row * p.out_stride_n +
-                                             h * p.out_stride_h + kq * 32);
+        uint4* d4 = reinterpret_cast<uint4*>(p.out + out_off + kq * 32);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           d4[i] = make_uint4(
@@ -886,9 +1006,7 @@ int sm_count() {
 }
 
 template <bool kHeat>
-int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk,
-               const CUtensorMap& mv, const FwdParams& p,
-               cudaStream_t stream) {
+int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
   static bool configured = false;
   const int sms = sm_count();
   if (sms == 0) return set_error(VEDA_ERR_CUDA, "no CUDA device");
@@ -900,8 +1018,7 @@ int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk,
   }
   if (p.n_items == 0) return VEDA_OK;
   const int grid = p.n_items < sms ? p.n_items : sms;
-  bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(mq, mk, mv,
-                                                                  p);
+  bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(maps, p);
   return check_launch("bsa_fwd_kernel");
 }
 
@@ -936,7 +1053,8 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   VEDA_REQUIRE(reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
                    out_stride_n % 8 == 0 && out_stride_h % 8 == 0,
                "out must be 16-byte aligned with strides multiple of 8");
-  CUtensorMap mq, mk, mv;
+  FwdMaps maps{};
+  CUtensorMap &mq = maps.q[0], &mk = maps.k[0], &mv = maps.v[0];
   rc = make_tile_map(&mq, q, n_q_tiles * kTile, n_heads, q_stride_n,
                      q_stride_h, "q");
   if (rc == VEDA_OK)
@@ -967,7 +1085,7 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   p.dense = 0;
   p.used = 0;
   p.status = device_status_ptr();
-  return launch_fwd<false>(mq, mk, mv, p, as_stream(stream));
+  return launch_fwd<false>(maps, p, as_stream(stream));
 }
 
 extern "C" int64_t veda_bsa_fwd_heat_workspace(int64_t n_kv_tiles) {
@@ -1000,7 +1118,8 @@ extern "C" int veda_bsa_fwd_heat(
   VEDA_REQUIRE(workspace != nullptr &&
                    workspace_bytes >= veda_bsa_fwd_heat_workspace(n_tiles),
                "workspace too small (veda_bsa_fwd_heat_workspace)");
-  CUtensorMap mq, mk, mv;
+  FwdMaps maps{};
+  CUtensorMap &mq = maps.q[0], &mk = maps.k[0], &mv = maps.v[0];
   rc = make_tile_map(&mq, q, n_tiles * kTile, n_heads, q_stride_n,
                      q_stride_h, "q");
   if (rc == VEDA_OK)
@@ -1034,7 +1153,7 @@ extern "C" int veda_bsa_fwd_heat(
   p.heat_scratch = static_cast<float*>(workspace);
   p.heat_sum = reduce_sum != 0;
   p.status = device_status_ptr();
-  return launch_fwd<true>(mq, mk, mv, p, as_stream(stream));
+  return launch_fwd<true>(maps, p, as_stream(stream));
 }
 
 extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
@@ -1065,7 +1184,8 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
     if (rc != VEDA_OK) return rc;
   }
   if (tiles == 0) return VEDA_OK;
-  CUtensorMap mq, mk, mv;
+  FwdMaps maps{};
+  CUtensorMap &mq = maps.q[0], &mk = maps.k[0], &mv = maps.v[0];
   rc = make_tile_map(&mq, q, seq_len, n_heads, stride_s, stride_h, "q");
   if (rc == VEDA_OK)
     rc = make_tile_map(&mk, k, seq_len, n_heads, stride_s, stride_h, "k");
@@ -1087,5 +1207,130 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
   p.dense = 1;
   p.used = used;
   p.status = device_status_ptr();
-  return launch_fwd<false>(mq, mk, mv, p, as_stream(stream));
+  return launch_fwd<false>(maps, p, as_stream(stream));
+}
+
+extern "C" int veda_bsa_fwd_packed(
+    const void* q, const void* k, const void* v, int64_t stride_s,
+    int64_t stride_h, int64_t seq_len, int32_t total_heads,
+    int32_t kv_tile_order, int64_t kv_stride_n, int64_t kv_stride_h,
+    const void* q_glob, const void* k_glob, const void* v_glob,
+    int64_t glob_stride_n, int64_t glob_stride_h, const veda_span_t* spans,
+    int32_t n_spans, int64_t n_tiles, int64_t n_video, const int64_t* heads,
+    int32_t n_heads, const int64_t* box_perm, const uint32_t* key_mask,
+    const int32_t* valid_count, const int32_t* part_cnt,
+    const int32_t* part_idx, const int32_t* full_cnt,
+    const int32_t* full_idx, int64_t ld_idx, void* out, int64_t out_stride_s,
+    int64_t out_stride_h, float softmax_scale, void* stream) {
+  int rc = require_sm100("veda_bsa_fwd_packed");
+  if (rc != VEDA_OK) return rc;
+  VEDA_REQUIRE(q && k && v && out && heads && box_perm && part_cnt &&
+                   part_idx && full_cnt && full_idx && spans,
+               "q, k, v, out, heads, box_perm, spans and the four lists are "
+               "required");
+  VEDA_REQUIRE(kv_tile_order ? valid_count != nullptr : key_mask != nullptr,
+               "tile-ordered k/v need valid_count; packed k/v need key_mask");
+  VEDA_REQUIRE(n_spans >= 1 && n_spans <= kMaxPackedSpans,
+               "the packed forward reads at most 2 tiled spans in place");
+  VEDA_REQUIRE(n_heads >= 1 && total_heads >= n_heads && seq_len >= 1,
+               "bad shape");
+  VEDA_REQUIRE(n_video >= 1 && n_tiles >= n_video, "bad tile counts");
+  VEDA_REQUIRE(n_tiles == n_video ||
+                   (q_glob && (kv_tile_order || (k_glob && v_glob))),
+               "the layout has global tiles: their gathered copies are "
+               "required");
+  VEDA_REQUIRE(ld_idx >= n_tiles, "ld_idx must be >= n_tiles");
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 30), "too many tiles");
+  VEDA_REQUIRE(softmax_scale > 0.f, "softmax_scale must be positive");
+  VEDA_REQUIRE(reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   out_stride_s % 8 == 0 && out_stride_h % 8 == 0,
+               "out must be 16-byte aligned with strides multiple of 8");
+  FwdMaps maps{};
+  FwdParams p{};
+  int64_t tiles = 0;
+  for (int s = 0; s < n_spans; ++s) {
+    const veda_span_t& sp = spans[s];
+    int64_t vol = 1, n = 1;
+    for (int a = 0; a < 3; ++a) {
+      VEDA_REQUIRE(sp.grid[a] > 0 && sp.shape[a] > 0,
+                   "span grid and tile shape must be positive");
+      vol *= sp.shape[a];
+      n *= (sp.grid[a] + sp.shape[a] - 1) / sp.shape[a];
+      p.span_shape[s][a] = sp.shape[a];
+    }
+    VEDA_REQUIRE(vol == kTile, "tile shape does not hold 128 tokens");
+    VEDA_REQUIRE(sp.start >= 0 && sp.start + static_cast<int64_t>(sp.grid[0]) *
+                                                  sp.grid[1] * sp.grid[2] <=
+                                              seq_len,
+                 "span exceeds the sequence");
+    p.span_begin[s] = static_cast<int>(tiles);
+    p.span_nbt[s] = (sp.grid[0] + sp.shape[0] - 1) / sp.shape[0];
+    p.span_nbw[s] = (sp.grid[2] + sp.shape[2] - 1) / sp.shape[2];
+    const char* names[3] = {"q span", "k span", "v span"};
+    const void* bases[3] = {q, k, v};
+    CUtensorMap* dst[3] = {&maps.q[1 + s], &maps.k[1 + s], &maps.v[1 + s]};
+    for (int t = 0; t < (kv_tile_order ? 1 : 3); ++t) {
+      const void* base = static_cast<const __nv_bfloat16*>(bases[t]) +
+                         sp.start * stride_s;
+      rc = make_box_map(dst[t], base, sp.grid, sp.shape, total_heads,
+                        stride_s, stride_h, names[t]);
+      if (rc != VEDA_OK) return rc;
+    }
+    tiles += n;
+  }
+  VEDA_REQUIRE(tiles == n_video, "n_video does not match the spans");
+  p.span_begin[n_spans] = static_cast<int>(tiles);
+  const int64_t n_global = n_tiles - n_video;
+  if (n_global > 0) {
+    rc = make_tile_map(&maps.q[0], q_glob, n_global * kTile, n_heads,
+                       glob_stride_n, glob_stride_h, "q_glob");
+    if (rc == VEDA_OK && !kv_tile_order)
+      rc = make_tile_map(&maps.k[0], k_glob, n_global * kTile, n_heads,
+                         glob_stride_n, glob_stride_h, "k_glob");
+    if (rc == VEDA_OK && !kv_tile_order)
+      rc = make_tile_map(&maps.v[0], v_glob, n_global * kTile, n_heads,
+                         glob_stride_n, glob_stride_h, "v_glob");
+    if (rc != VEDA_OK) return rc;
+  }
+  if (kv_tile_order == 2) {
+    VEDA_REQUIRE(reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(v) % 16 == 0,
+                 "tile images must be 16-byte aligned");
+    p.k_img = static_cast<const uint8_t*>(k);
+    p.v_img = static_cast<const uint8_t*>(v);
+  } else if (kv_tile_order) {
+    rc = make_tile_map(&maps.k[0], k, n_tiles * kTile, n_heads, kv_stride_n,
+                       kv_stride_h, "k");
+    if (rc == VEDA_OK)
+      rc = make_tile_map(&maps.v[0], v, n_tiles * kTile, n_heads,
+                         kv_stride_n, kv_stride_h, "v");
+    if (rc != VEDA_OK) return rc;
+  }
+  p.n_heads = n_heads;
+  p.n_q_tiles = static_cast<int>(n_tiles);
+  p.n_kv_tiles = static_cast<int>(n_tiles);
+  p.n_items = static_cast<int>(n_tiles * n_heads);
+  p.valid_count = kv_tile_order ? valid_count : nullptr;
+  p.part_cnt = part_cnt;
+  p.part_idx = part_idx;
+  p.full_cnt = full_cnt;
+  p.full_idx = full_idx;
+  p.ld_idx = ld_idx;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_n = out_stride_s;
+  p.out_stride_h = out_stride_h;
+  p.lse = nullptr;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.dense = 0;
+  p.used = 0;
+  p.packed = 1;
+  p.box_kv = kv_tile_order ? 0 : 1;
+  p.total_heads = total_heads;
+  p.n_video = static_cast<int>(n_video);
+  p.n_spans = n_spans;
+  p.head_ids = heads;
+  p.box_perm = box_perm;
+  p.key_mask = kv_tile_order ? nullptr : key_mask;
+  p.status = device_status_ptr();
+  return launch_fwd<false>(maps, p, as_stream(stream));
 }

@@ -127,6 +127,52 @@ int make_tile_map(CUtensorMap* map, const void* base, int64_t rows,
   return VEDA_OK;
 }
 
+int make_box_map(CUtensorMap* map, const void* base, const int grid[3],
+                 const int shape[3], int64_t heads, int64_t stride_row,
+                 int64_t stride_head, const char* name) {
+  auto fn = encode_fn();
+  if (fn == nullptr)
+    return set_error(VEDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const auto addr = reinterpret_cast<uintptr_t>(base);
+  if (addr % 16 != 0 || (stride_row * 2) % 16 != 0 ||
+      (stride_head * 2) % 16 != 0)
+    return set_error(VEDA_ERR_INVALID,
+                     std::string(name) +
+                         ": base address and row/head strides must be "
+                         "16-byte aligned for TMA");
+  const int T = grid[0], Hh = grid[1], W = grid[2];
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(kHeadDim),
+                        static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(W),
+                        static_cast<cuuint64_t>(Hh),
+                        static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[4] = {
+      static_cast<cuuint64_t>(stride_head * 2),
+      static_cast<cuuint64_t>(stride_row * 2),
+      static_cast<cuuint64_t>(stride_row * 2) * static_cast<cuuint64_t>(W),
+      static_cast<cuuint64_t>(stride_row * 2) * static_cast<cuuint64_t>(W) *
+          static_cast<cuuint64_t>(Hh)};
+  cuuint32_t box[5] = {64, 1, static_cast<cuuint32_t>(shape[2]),
+                       static_cast<cuuint32_t>(shape[1]),
+                       static_cast<cuuint32_t>(shape[0])};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5,
+                  const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "%s: cuTensorMapEncodeTiled failed (%d) for grid=(%d,%d,%d) "
+             "box=(%d,%d,%d) heads=%lld",
+             name, static_cast<int>(r), T, Hh, W, shape[0], shape[1],
+             shape[2], static_cast<long long>(heads));
+    return set_error(VEDA_ERR_INVALID, buf);
+  }
+  return VEDA_OK;
+}
+
 // ---------------------------------------------------------------------------
 // UMMA layout probe: one 128x128x128 MMA, operands as the attention kernels
 // stage them (TMA with 128-byte swizzle; P through tensor memory).
@@ -228,6 +274,28 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// Two warps wait on mbarriers that nothing completes: warp 0 with the given
+// limit, warp 1 with the library's, leaving on warp 0's abort flag.
+__global__ void __launch_bounds__(64, 1)
+    expire_wait_kernel(unsigned long long limit_ns, int32_t* completed,
+                       unsigned int* status) {
+  __shared__ uint64_t bars[2];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort = &abort_flag;
+  const bool ok = warp == 0
+                      ? mbar_wait(&bars[0], 0, abort, status, limit_ns)
+                      : mbar_wait(&bars[1], 0, abort, status);
+  if (threadIdx.x % 32 == 0) completed[warp] = ok ? 1 : 0;
+}
+
 }  // namespace veda
 
 using namespace veda;
@@ -273,4 +341,19 @@ extern "C" int veda_probe_umma(const void* a, const void* b, float* d,
       ma, mb, static_cast<const __nv_bfloat16*>(a), d, mode,
       device_status_ptr());
   return check_launch("probe_umma_kernel");
+}
+
+extern "C" int veda_expire_wait(int64_t limit_ns, int32_t* completed,
+                                void* stream) {
+  int rc = require_sm100("veda_expire_wait");
+  if (rc != VEDA_OK) return rc;
+  VEDA_REQUIRE(limit_ns >= 1000000 &&
+                   limit_ns <= static_cast<int64_t>(kWaitTimeoutNs),
+               "limit_ns must lie in [1 ms, 4 s]");
+  VEDA_REQUIRE(completed != nullptr, "completed[2] is required");
+  unsigned int* status = device_status_ptr();
+  if (status == nullptr) return set_error(VEDA_ERR_CUDA, "no device status word");
+  expire_wait_kernel<<<1, 64, 0, as_stream(stream)>>>(
+      static_cast<unsigned long long>(limit_ns), completed, status);
+  return check_launch("expire_wait_kernel");
 }

@@ -47,6 +47,16 @@ int make_tile_map(CUtensorMap* map, const void* base, int64_t rows,
                   int64_t heads, int64_t stride_row, int64_t stride_head,
                   const char* name);
 
+// 5D bf16 tensor map over the (T, Hh, W) grid of a span of a packed
+// [rows, heads, 128] tensor (base = the span's first row): dimensions
+// (d, head, w, h, t), box (64, 1, sw, sh, st) with 128-byte swizzle, so a
+// box lands in shared memory exactly like a (64, 1, 128) box of tile-ordered
+// rows, its rows in the tile's (t, h, w) row-major order. Coordinates are
+// (d0 in {0, 64}, head, w0, h0, t0); rows outside the grid read as zero.
+int make_box_map(CUtensorMap* map, const void* base, const int grid[3],
+                 const int shape[3], int64_t heads, int64_t stride_row,
+                 int64_t stride_head, const char* name);
+
 constexpr int kTile = 128;
 constexpr int kHeadDim = 128;
 
@@ -110,18 +120,18 @@ __device__ __forceinline__ void raise_status(unsigned int* status,
 }
 
 // Waits for the phase of `bar` with the given parity. Gives up when another
-// role of the CTA already gave up (*abort != 0) or after kWaitTimeoutNs,
-// which it records in *abort and in the device status word. Returns true
-// when the phase completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort,
-                                          unsigned int* status) {
+// role of the CTA already gave up (*abort != 0) or after `limit_ns`
+// (kWaitTimeoutNs unless a caller asks for less), which it records in *abort
+// and in the device status word. Returns true when the phase completed.
+__device__ __forceinline__ bool mbar_wait(
+    uint64_t* bar, uint32_t parity, volatile int* abort, unsigned int* status,
+    unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_timer() - t0 > kWaitTimeoutNs) {
+    if (global_timer() - t0 > limit_ns) {
       *abort = 1;
       raise_status(status, VEDA_ERR_TIMEOUT);
       return false;
@@ -138,6 +148,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0),
       "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// TMA: 5D tiled bulk tensor load (a box of the packed tensor, see
+// make_box_map), completing on `bar`.
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map,
+                                            uint64_t* bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0),
+      "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
 

@@ -33,6 +33,12 @@ struct GatherParams {
   const int64_t* heads;  // nullptr: head h
   __nv_bfloat16* out;    // nullptr: pool only
   int64_t out_stride_n, out_stride_h;
+  // out holds shared-memory images of the tiles instead of rows: tile
+  // (h, tile) is 32 KB at (h * n_tiles + tile) * 32 KB, two 64-column halves
+  // of 128 rows x 128 bytes, the 16-byte chunks of row r in the order of the
+  // 128-byte swizzle (chunk c at position c ^ (r % 8)), exactly what a TMA
+  // load of the two boxes with 128-byte swizzle writes to shared memory.
+  int image;
   float* feats;  // [H', n, 3D] or nullptr
   float* sq;     // [H', n, D] or nullptr
   float* var;    // [H', n, D] or nullptr
@@ -40,9 +46,11 @@ struct GatherParams {
 };
 
 __global__ void __launch_bounds__(kPoolThreads)
-    gather_pool_kernel(GatherParams p) {
-  const int64_t tile = blockIdx.x;
-  const int h = blockIdx.y;
+    gather_pool_kernel(GatherParams p, int64_t n_tiles) {
+  // Tiles vary fastest across the grid: the CTAs in flight write one head's
+  // tiles contiguously (measured faster than all heads of a tile at once).
+  const int64_t tile = blockIdx.x % n_tiles;
+  const int h = static_cast<int>(blockIdx.x / n_tiles);
   const int tid = threadIdx.x;
   const int c8 = tid & 15;   // column group: columns [8*c8, 8*c8 + 8)
   const int rg = tid >> 4;   // row group: rows rg + 16*i
@@ -67,7 +75,17 @@ __global__ void __launch_bounds__(kPoolThreads)
       vals[i] = __ldg(reinterpret_cast<const uint4*>(
           p.x + src * p.x_stride_s + head * p.x_stride_h + 8 * c8));
   }
-  if (p.out != nullptr) {
+  if (p.out != nullptr && p.image) {
+    __nv_bfloat16* img = p.out + (static_cast<int64_t>(h) * p.n_tiles + tile) *
+                                     (kTile * kHeadDim) +
+                         (c8 >> 3) * (kTile * 64);
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      const int r = rg + 16 * i;
+      *reinterpret_cast<uint4*>(img + r * 64 + (((c8 & 7) ^ (r & 7)) * 8)) =
+          vals[i];
+    }
+  } else if (p.out != nullptr) {
 #pragma unroll
     for (int i = 0; i < kRowsPerThread; ++i) {
       const int64_t slot = tile * kTile + rg + 16 * i;
@@ -202,9 +220,9 @@ struct ScatterParams {
 };
 
 __global__ void __launch_bounds__(kPoolThreads)
-    scatter_kernel(ScatterParams p) {
-  const int64_t tile = blockIdx.x;
-  const int h = blockIdx.y;
+    scatter_kernel(ScatterParams p, int64_t n_tiles) {
+  const int64_t tile = blockIdx.x % n_tiles;
+  const int h = static_cast<int>(blockIdx.x / n_tiles);
   const int tid = threadIdx.x;
   const int c8 = tid & 15;
   const int rg = tid >> 4;
@@ -292,8 +310,42 @@ extern "C" int veda_gather_pool(const void* x, int64_t x_stride_s,
   p.sq = sq;
   p.var = var;
   p.n_tiles = n_tiles;
-  dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_heads));
-  gather_pool_kernel<<<grid, kPoolThreads, 0, as_stream(stream)>>>(p);
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
+  gather_pool_kernel<<<static_cast<unsigned>(n_tiles * n_heads), kPoolThreads,
+                       0, as_stream(stream)>>>(p, n_tiles);
+  return check_launch("gather_pool_kernel");
+}
+
+extern "C" int veda_gather_pool_images(const void* x, int64_t x_stride_s,
+                                       int64_t x_stride_h,
+                                       const int64_t* perm,
+                                       const int32_t* valid_count,
+                                       int64_t n_tiles, const int64_t* heads,
+                                       int32_t n_heads, void* image,
+                                       float* feats, void* stream) {
+  VEDA_REQUIRE(x != nullptr && perm != nullptr && valid_count != nullptr &&
+                   heads != nullptr && image != nullptr,
+               "x, perm, valid_count, heads and image are required");
+  VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
+  VEDA_REQUIRE(reinterpret_cast<uintptr_t>(image) % 16 == 0,
+               "image must be 16-byte aligned");
+  int rc = check_rows(x, x_stride_s, x_stride_h, "x");
+  if (rc != VEDA_OK) return rc;
+  if (n_tiles == 0) return VEDA_OK;
+  GatherParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.x_stride_s = x_stride_s;
+  p.x_stride_h = x_stride_h;
+  p.perm = perm;
+  p.valid_count = valid_count;
+  p.heads = heads;
+  p.out = static_cast<__nv_bfloat16*>(image);
+  p.image = 1;
+  p.feats = feats;
+  p.n_tiles = n_tiles;
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
+  gather_pool_kernel<<<static_cast<unsigned>(n_tiles * n_heads), kPoolThreads,
+                       0, as_stream(stream)>>>(p, n_tiles);
   return check_launch("gather_pool_kernel");
 }
 
@@ -319,8 +371,9 @@ extern "C" int veda_scatter(const void* tiled, int64_t t_stride_n,
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_s = out_stride_s;
   p.out_stride_h = out_stride_h;
-  dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_heads));
-  scatter_kernel<<<grid, kPoolThreads, 0, as_stream(stream)>>>(p);
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
+  scatter_kernel<<<static_cast<unsigned>(n_tiles * n_heads), kPoolThreads, 0,
+                   as_stream(stream)>>>(p, n_tiles);
   return check_launch("scatter_kernel");
 }
 

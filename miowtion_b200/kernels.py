@@ -162,6 +162,87 @@ def block_sparse_attention_lists(q: torch.Tensor, k: torch.Tensor,
     return (out, lse) if return_lse else out
 
 
+# Video spans the packed forward reads in place (one tensor map each).
+PACKED_MAX_SPANS = 2
+
+
+def packed_supported(layout: tiling.TileLayout) -> bool:
+    """Whether `block_sparse_attention_packed` can run this layout."""
+    return 1 <= len(layout.spans) <= PACKED_MAX_SPANS
+
+
+def block_sparse_attention_packed(q: torch.Tensor, k: torch.Tensor,
+                                  v: torch.Tensor,
+                                  lists: veda_mask.BlockLists,
+                                  layout: tiling.TileLayout,
+                                  heads: torch.Tensor,
+                                  out: torch.Tensor,
+                                  kv_tiles: bool = False) -> None:
+    """Forward of the heads `heads` of one tile layout, with the queries
+    read from and the output written to the packed tensors in place:
+    q [S, H, D] -> rows [0, used) of out [S, H, D] for those heads. Equals
+    `gather_tiles`, then `block_sparse_attention_lists` over all query
+    tiles, then `scatter_rows_` (veda/attention.py:724-743), in one kernel
+    without the tile-ordered q or output. k and v are the group's
+    tile-ordered copies [N, H', D] with `kv_tiles` (as `gather_and_pool`
+    writes them), else packed [S, H, D] like q and read in place too."""
+    _require(q, 'block_sparse_attention')
+    for name, t in ((('q', q), ('out', out)) if kv_tiles == 'images' else
+                    (('q', q), ('k', k), ('v', v), ('out', out))):
+        tiling._check_rows(t, name)  # pylint: disable=protected-access
+    if kv_tiles == 'images' and (k.dtype != torch.bfloat16
+                                 or v.dtype != torch.bfloat16):
+        raise NotImplementedError('tile images hold bf16')
+    if not packed_supported(layout):
+        raise ValueError(f'the packed forward reads at most '
+                         f'{PACKED_MAX_SPANS} spans, the layout has '
+                         f'{len(layout.spans)}')
+    heads = tiling._heads_arg(q, heads)  # pylint: disable=protected-access
+    n_heads = heads.numel()
+    if out.shape != q.shape:
+        raise ValueError('q and out must share [S, H, D]')
+    if kv_tiles == 'images':
+        if k.shape != (n_heads, layout.n_tiles, 2, 128, 64) or (
+                v.shape != k.shape) or not (k.is_contiguous()
+                                            and v.is_contiguous()):
+            raise ValueError('tile images must be [len(heads), n_tiles, 2, '
+                             '128, 64] contiguous')
+    elif kv_tiles:
+        if k.shape != (layout.num_slots, n_heads, q.shape[-1]) or (
+                v.shape != k.shape or v.stride() != k.stride()):
+            raise ValueError('tile-ordered k and v must be [num_slots, '
+                             'len(heads), D] with equal strides')
+    elif k.shape != q.shape or v.shape != q.shape or (
+            k.stride() != q.stride() or v.stride() != q.stride()):
+        raise ValueError('packed q, k and v must share [S, H, D] and strides')
+    if lists.part_cnt.shape != (n_heads, layout.n_tiles):
+        raise ValueError(f'lists cover {tuple(lists.part_cnt.shape)} '
+                         f'(heads, query tiles), expected '
+                         f'{(n_heads, layout.n_tiles)}')
+    glob = [None, None, None]
+    if layout.n_global_tiles:
+        rows = torch.arange(layout.n_video_tiles, layout.n_tiles,
+                            device=q.device)
+        glob = [tiling.gather_tile_rows(t, layout, rows, heads)
+                for t in ((q,) if kv_tiles else (q, k, v))]
+        glob += [None] * (3 - len(glob))
+    g_stride = glob[0].stride() if glob[0] is not None else (0, 0)
+    _lib.call('veda_bsa_fwd_packed', q.data_ptr(), k.data_ptr(),
+              v.data_ptr(), q.stride(0), q.stride(1), q.shape[0], q.shape[1],
+              2 if kv_tiles == 'images' else (1 if kv_tiles else 0),
+              k.stride(0), k.stride(1),
+              *(_lib.ptr(t) for t in glob), g_stride[0], g_stride[1],
+              tiling.span_array(layout.spans), len(layout.spans),
+              layout.n_tiles, layout.n_video_tiles, heads.data_ptr(), n_heads,
+              layout.box_perm.data_ptr(), layout.key_mask.data_ptr(),
+              layout.valid_count.data_ptr(),
+              lists.part_cnt.data_ptr(), lists.part_idx.data_ptr(),
+              lists.full_cnt.data_ptr(), lists.full_idx.data_ptr(),
+              lists.part_idx.shape[-1], out.data_ptr(), out.stride(0),
+              out.stride(1), 1.0 / math.sqrt(q.shape[-1]),
+              _lib.stream_ptr(q.device))
+
+
 def block_sparse_attention_bwd(q: torch.Tensor, k: torch.Tensor,
                                v: torch.Tensor, out: torch.Tensor,
                                dout: torch.Tensor, lse: torch.Tensor,

@@ -123,6 +123,14 @@ class TileLayout:
     kv_ok: torch.Tensor
     full_tile: torch.Tensor
     slot_valid: torch.Tensor
+    # The spans this layout tiles, and the same tiles in box order for the
+    # attention that reads the packed tensors in place: box_perm
+    # [n_tiles * 128] int64 (packed row of every box slot, -1 outside the
+    # grid; global tiles as in perm) and key_mask [n_tiles * 4] int32 (bit
+    # slot % 32 of word slot // 32 set for real rows).
+    spans: tuple = ()
+    box_perm: torch.Tensor | None = None
+    key_mask: torch.Tensor | None = None
 
     @property
     def n_tiles(self) -> int:
@@ -152,6 +160,16 @@ def layout_counts(spans: Sequence[TiledSpan], used: int) -> tuple[int, ...]:
     return sum(counts), sum(counts[:-1]), n_global
 
 
+def span_array(spans: Sequence[TiledSpan]):
+    """The spans as a ctypes veda_span_t array."""
+    arr = (_lib.Span * len(spans))()
+    for i, s in enumerate(spans):
+        arr[i].start = s.start
+        arr[i].grid[:] = list(s.grid)
+        arr[i].shape[:] = [s.shape.t, s.shape.h, s.shape.w]
+    return arr
+
+
 def build_tile_layout(spans: Sequence[TiledSpan], used: int, seq_len: int,
                       device: torch.device | str = 'cuda') -> TileLayout:
     """Builds the permutation for tiled spans on a CUDA device
@@ -167,16 +185,17 @@ def build_tile_layout(spans: Sequence[TiledSpan], used: int, seq_len: int,
         raise RuntimeError('build_tile_layout runs on a CUDA device; '
                            f'{device} has no kernel (no CPU fallback)')
     n_tiles = n_video + n_global
-    arr = (_lib.Span * len(spans))()
-    for i, s in enumerate(spans):
-        arr[i].start = s.start
-        arr[i].grid[:] = list(s.grid)
-        arr[i].shape[:] = [s.shape.t, s.shape.h, s.shape.w]
+    arr = span_array(spans)
     perm = torch.empty(n_tiles * TILE_SIZE, dtype=torch.int64, device=device)
     valid_count = torch.empty(n_tiles, dtype=torch.int32, device=device)
+    box_perm = torch.empty_like(perm)
+    key_mask = torch.empty(n_tiles * 4, dtype=torch.int32, device=device)
     with torch.cuda.device(device):
         _lib.call('veda_build_layout', arr, len(spans), used, seq_len,
                   n_tiles, perm.data_ptr(), valid_count.data_ptr(),
+                  _lib.stream_ptr(device))
+        _lib.call('veda_build_box_layout', arr, len(spans), used, seq_len,
+                  n_tiles, box_perm.data_ptr(), key_mask.data_ptr(),
                   _lib.stream_ptr(device))
     return TileLayout(
         perm=perm, valid_count=valid_count, n_video_tiles=n_video,
@@ -190,7 +209,8 @@ def build_tile_layout(spans: Sequence[TiledSpan], used: int, seq_len: int,
             (valid_count > 0) & (valid_count < TILE_SIZE)).view(-1),
         kv_ok=valid_count > 0,
         full_tile=valid_count == TILE_SIZE,
-        slot_valid=(perm >= 0).to(torch.int32))
+        slot_valid=(perm >= 0).to(torch.int32),
+        spans=tuple(spans), box_perm=box_perm, key_mask=key_mask)
 
 
 def _heads_arg(x: torch.Tensor, heads: torch.Tensor | None):
@@ -241,6 +261,46 @@ def gather_and_pool(x: torch.Tensor, layout: TileLayout,
     if not pool:
         return out
     return (out, feats, sq, var) if second else (out, feats)
+
+
+def gather_images(x: torch.Tensor, layout: TileLayout,
+                  heads: torch.Tensor | None, pool: bool = False):
+    """`gather_and_pool` with the tiles written as shared-memory images
+    [H', n_tiles, 2, 128, 64] bf16 (one contiguous 32 KB block per tile
+    and head, its 128-byte rows swizzled as a TMA load lays them out): the
+    key / value input of `kernels.block_sparse_attention_packed`. With
+    `pool`, also returns the features [H', n, 3D]."""
+    _check_rows(x, 'x')
+    heads = _heads_arg(x, heads)
+    n_heads = heads.numel()
+    image = torch.empty(n_heads, layout.n_tiles, 2, TILE_SIZE, 64,
+                        dtype=x.dtype, device=x.device)
+    feats = (torch.empty(n_heads, layout.n_tiles, 3 * x.shape[-1],
+                         dtype=torch.float32, device=x.device)
+             if pool else None)
+    _lib.call('veda_gather_pool_images', x.data_ptr(), x.stride(0),
+              x.stride(1), layout.perm.data_ptr(),
+              layout.valid_count.data_ptr(), layout.n_tiles, heads.data_ptr(),
+              n_heads, image.data_ptr(), _lib.ptr(feats),
+              _lib.stream_ptr(x.device))
+    return (image, feats) if pool else image
+
+
+def pool_features(x: torch.Tensor, layout: TileLayout,
+                  heads: torch.Tensor | None) -> torch.Tensor:
+    """predictor.pool_tiles of x [S, H, D] read in place: features
+    [H', n, 3D] fp32 (masked mean | max | min per tile), without writing a
+    tile-ordered copy (the input of the packed attention path)."""
+    _check_rows(x, 'x')
+    heads = _heads_arg(x, heads)
+    n_heads = heads.numel()
+    feats = torch.empty(n_heads, layout.n_tiles, 3 * x.shape[-1],
+                        dtype=torch.float32, device=x.device)
+    _lib.call('veda_gather_pool', x.data_ptr(), x.stride(0), x.stride(1),
+              layout.perm.data_ptr(), layout.valid_count.data_ptr(),
+              layout.n_tiles, heads.data_ptr(), n_heads, None, 0, 0,
+              feats.data_ptr(), None, None, _lib.stream_ptr(x.device))
+    return feats
 
 
 def gather_tiles(x: torch.Tensor, layout: TileLayout,
