@@ -42,6 +42,7 @@ from miowtion_b200 import mask as veda_mask  # noqa: E402
 from miowtion_b200 import plan as veda_plan  # noqa: E402
 from miowtion_b200 import predictor as veda_predictor  # noqa: E402
 from miowtion_b200 import tiling  # noqa: E402
+from miowtion_b200.pipeline import HostPipeline  # noqa: E402
 from miowtion_b200 import ulysses  # noqa: E402
 
 METRIC = ('sparse-attn ms/layer @90% sparsity; effective TFLOP/s; '
@@ -403,24 +404,24 @@ def main():
                 logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
             blocks += int(lists.part_cnt.sum() + lists.full_cnt.sum())
             del qt, kt
-        # End to end through the public API with host buffers: H2D of this
-        # step's q, k, v shard, the layer, D2H of the output.
+        # End to end through the public API with host buffers: every step
+        # copies its q, k, v shard from pinned host memory, runs the layer
+        # and copies the output back (HostPipeline: step i + 1's inputs and
+        # step i - 1's output move while step i computes).
         host = [t.cpu().pin_memory() for t in (q, k, v)]
         out_host = torch.empty_like(host[0]).pin_memory()
-        dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+        pipe = HostPipeline(fn, q.shape, q.dtype, device)
         e2e_steps = min(args.steps, 30)
         for _ in range(2):
-            for d, h in zip((dq, dk, dv), host):
-                d.copy_(h, non_blocking=True)
-            out_host.copy_(fn(dq, dk, dv, 0), non_blocking=True)
+            pipe(*host, 0, out_host)
+        pipe.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0.record(pipe.h2d)
         for _ in range(e2e_steps):
-            for d, h in zip((dq, dk, dv), host):
-                d.copy_(h, non_blocking=True)
-            out_host.copy_(fn(dq, dk, dv, 0), non_blocking=True)
+            pipe(*host, 0, out_host)
+        pipe.wait_on(stream)
         e1.record(stream)
         barrier()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
