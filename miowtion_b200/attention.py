@@ -36,8 +36,24 @@ DEFAULT_COLLECT_BYTES = 64 * 2**30
 @dataclasses.dataclass(frozen=True)
 class VedaConfig:
     """Sparsity settings (attention.py:37-135; the fields the sparse path
-    reads)."""
+    and the stage-1 teacher read).
 
+    The teacher's supervision: `heat_reduce` ('max' peak probability or
+    'sum' mass per block), `kl_weight` and `kl_direction` of the seer KL,
+    `teacher_q_tiles` (supervised video query tiles per layer and head
+    group: a fraction of the video tiles when <= 1, else a count) and
+    `recall_every` (diagnostics on every n-th layer). `transport_weight`
+    and `gauge_kl_weight` select the reference's ablation objectives, which
+    this package does not provide (TeacherCollector raises when they are
+    non-zero)."""
+
+    heat_reduce: str = 'max'
+    transport_weight: float = 0.0
+    gauge_kl_weight: float = 0.0
+    kl_weight: float = 1.0
+    kl_direction: str = 'forward'
+    teacher_q_tiles: float = 1.0
+    recall_every: int = 1
     target_budget: veda_mask.Budget = veda_mask.Budget(ratio=0.1)
     ref_budget: veda_mask.Budget | None = None
     tile_conditions: bool = False
@@ -121,6 +137,14 @@ class ClipTiling:
                ) -> list[veda_mask.ColumnBlock]:
         return veda_mask.column_blocks(tile_layout, self.config.target_budget,
                                        self.config.ref_budget)
+
+    def num_supervised(self, tile_layout: tiling.TileLayout) -> int:
+        """Supervised video query tiles per layer and head group
+        (attention.py:193-197)."""
+        n_video = tile_layout.n_video_tiles
+        value = self.config.teacher_q_tiles
+        count = round(value * n_video) if value <= 1 else int(value)
+        return max(1, min(n_video, count))
 
 
 _HEAD_DIM_BYTES = 128 * 2
@@ -209,6 +233,139 @@ class _SparseGroup(torch.autograd.Function):
             tiling.scatter_rows_(full, g, layout, heads)
             outs.append(full)
         return (*outs, None, None, None, None, None, None)
+
+
+# Diagnostic fields of LayerStats in the order resolve() transfers them
+# (attention.py:308-310).
+STAT_FIELDS = ('kl', 'topk_bce', 'transport', 'logit_std', 'recall',
+               'gauge_kl', 'heat_kept', 'heat_ceiling', 'retained')
+
+
+@dataclasses.dataclass
+class LayerStats:
+    """Stage-1 diagnostics kept on the device until `resolve()`
+    (attention.py:313-347): `kl` one entry per layer, the others one per
+    layer and head group (the diagnostics only on the layers they ran)."""
+
+    kl: list = dataclasses.field(default_factory=list)
+    topk_bce: list = dataclasses.field(default_factory=list)
+    transport: list = dataclasses.field(default_factory=list)
+    gauge_kl: list = dataclasses.field(default_factory=list)
+    retained: list = dataclasses.field(default_factory=list)
+    logit_std: list = dataclasses.field(default_factory=list)
+    recall: list = dataclasses.field(default_factory=list)
+    heat_kept: list = dataclasses.field(default_factory=list)
+    heat_ceiling: list = dataclasses.field(default_factory=list)
+
+    def resolve(self) -> dict[str, list[float]]:
+        """Host values of every field, in one device-to-host transfer."""
+        fields = {name: getattr(self, name) for name in STAT_FIELDS}
+        flat = [t for values in fields.values() for t in values]
+        if not flat:
+            return {name: [] for name in fields}
+        host = torch.stack([t.detach().float().reshape(())
+                            for t in flat]).cpu().tolist()
+        out, start = {}, 0
+        for name, values in fields.items():
+            out[name] = host[start:start + len(values)]
+            start += len(values)
+        return out
+
+
+class TeacherCollector:
+    """Stage-1 attention (attention.py:350-470): returns the dense output
+    and, per layer and head group, trains the predictor against the
+    teacher's block heat right away.
+
+    Per call: the dense attention with its LSE over all heads (the B200
+    dense kernel); per head group of the plan, a seeded sample of video
+    query tiles, the group's q and k gathered and pooled, the heat of the
+    sampled tiles (`veda_teacher_heat`, reduce `config.heat_reduce`), the
+    predictor's logits of those tiles with gradients, the seer KL and its
+    backward, scaled so the sum over groups is the head-weighted mean times
+    `grad_scale`. No graph outlives the call; diagnostics stay on the device
+    in `stats`.
+    """
+
+    def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
+                 predictor: veda_predictor.TileScorePredictor,
+                 generator: torch.Generator, grad_scale: float,
+                 dense_backend: str = 'auto', topk_weight: float = 0.0):
+        config = clip.config
+        if config.transport_weight or config.gauge_kl_weight or topk_weight:
+            raise NotImplementedError(
+                'the transport, gauge-fixed KL and oracle top-k BCE '
+                'objectives are ablation losses this package does not '
+                'provide; the seer KL is')
+        if config.heat_reduce not in ('max', 'sum'):
+            raise ValueError(f"heat_reduce must be 'max' or 'sum': "
+                             f'{config.heat_reduce!r}')
+        reason = kernels.unavailable_reason(clip.device)
+        if reason is not None:
+            raise RuntimeError(f'TeacherCollector needs the B200 kernels '
+                               f'({reason}); refusing to fall back silently')
+        self.clip = clip
+        self.plan = plan
+        self.predictor = predictor
+        self.generator = generator
+        self.grad_scale = grad_scale
+        self.dense_backend = dense_backend
+        self.topk_weight = topk_weight
+        self.stats = LayerStats()
+        self._num_heads = sum(
+            g.heads.numel() for g in plan.head_groups(0, clip.device))
+
+    def _sample_rows(self, tile_layout: tiling.TileLayout) -> torch.Tensor:
+        """Sorted supervised video query tiles, drawn from the generator
+        exactly as attention.py:385-389 draws them."""
+        count = self.clip.num_supervised(tile_layout)
+        rows = torch.randperm(tile_layout.n_video_tiles,
+                              generator=self.generator)[:count]
+        return rows.sort().values.to(self.clip.device)
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 layer_index: int) -> torch.Tensor:
+        config = self.clip.config
+        out, lse = dense_attention(q, k, v, self.clip.layout.used,
+                                   return_lse=True,
+                                   backend=self.dense_backend)
+        layer_kl = None
+        for group in self.plan.head_groups(layer_index, self.clip.device):
+            tile_layout = self.clip.get(group.shape)
+            rows = self._sample_rows(tile_layout)
+            for heads in group.heads.split(
+                    _chunk_heads(tile_layout, config.collect_bytes)):
+                with torch.no_grad():
+                    q_tiles, feats_q = tiling.gather_and_pool(
+                        q.detach(), tile_layout, heads)
+                    k_tiles, feats_k = tiling.gather_and_pool(
+                        k.detach(), tile_layout, heads)
+                    heat = heatmap.teacher_heat(
+                        q_tiles, k_tiles,
+                        tiling.gather_lse(lse, tile_layout, heads),
+                        tile_layout, rows, config.heat_reduce)
+                del q_tiles, k_tiles
+                weight = heads.numel() / self._num_heads
+                with torch.enable_grad():
+                    logits = self.predictor.layers[layer_index](
+                        feats_q[:, rows], feats_k, heads)
+                    kl = heatmap.seer_kl(logits, heat, tile_layout,
+                                         config.kl_direction)
+                    loss = config.kl_weight * kl
+                    (loss * (weight * self.grad_scale)).backward()
+                term = kl.detach() * weight
+                layer_kl = term if layer_kl is None else layer_kl + term
+                self.stats.logit_std.append(
+                    logits.detach()[:, :, :tile_layout.n_video_tiles]
+                    .std(dim=-1).mean())
+                if layer_index % config.recall_every == 0:
+                    values = heatmap.mask_diagnostics(
+                        logits.detach(), heat, tile_layout,
+                        self.clip.blocks(tile_layout), rows)
+                    for name, value in values.items():
+                        getattr(self.stats, name).append(value)
+        self.stats.kl.append(layer_kl)
+        return out
 
 
 class SparseStudent:

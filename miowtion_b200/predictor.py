@@ -13,6 +13,8 @@ not implemented on the device and raise NotImplementedError.
 
 from __future__ import annotations
 
+import math
+
 import torch
 from torch import nn
 
@@ -48,34 +50,87 @@ def pool_tiles(x: torch.Tensor, layout: tiling.TileLayout,
     return out
 
 
-def predict_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
-                   proj_q: torch.Tensor, proj_k: torch.Tensor,
-                   heads: torch.Tensor) -> torch.Tensor:
-    """[H', n_q, n_k] fp32 logits of pooled features (predictor.py:251-338)."""
-    if feats_q.dim() != 3 or feats_q.shape[-1] != 3 * 128:
-        raise ValueError('features must be [H\', n, 384]')
-    if not feats_q.is_cuda:
-        raise RuntimeError('the predictor kernels run on CUDA only')
-    heads = heads.to(device=feats_q.device, dtype=torch.int64).contiguous()
-    feats_q = feats_q.float().contiguous()
-    feats_k = feats_k.float().contiguous()
-    proj_q = proj_q.detach().float().contiguous()
-    proj_k = proj_k.detach().float().contiguous()
+def _logits_and_embeddings(feats_q: torch.Tensor, feats_k: torch.Tensor,
+                           proj_q: torch.Tensor, proj_k: torch.Tensor,
+                           heads: torch.Tensor):
+    """The kernel call: logits [H', n_q, n_k] and the tile embeddings q_hat
+    [H', n_q, D], k_hat [H', n_k, D] it leaves in its workspace."""
     n_heads, n_q = feats_q.shape[0], feats_q.shape[1]
     n_k = feats_k.shape[1]
-    if heads.numel() != n_heads or feats_k.shape[0] != n_heads:
-        raise ValueError('heads and features disagree on the head count')
     lib = _lib.load()
     ws_bytes = lib.veda_predict_workspace(n_heads, n_q, n_k)
-    workspace = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32,
+    workspace = torch.empty(n_heads * (n_q + n_k) * 128, dtype=torch.float32,
                             device=feats_q.device)
+    if workspace.numel() * 4 < ws_bytes:
+        raise RuntimeError('predictor workspace layout changed')
     logits = torch.empty(n_heads, n_q, n_k, dtype=torch.float32,
                          device=feats_q.device)
     _lib.call('veda_predict_logits', feats_q.data_ptr(), feats_k.data_ptr(),
               proj_q.data_ptr(), proj_k.data_ptr(), heads.data_ptr(),
               n_heads, n_q, n_k, logits.data_ptr(), workspace.data_ptr(),
-              ws_bytes, _lib.stream_ptr(feats_q.device))
-    return logits
+              workspace.numel() * 4, _lib.stream_ptr(feats_q.device))
+    q_hat = workspace[:n_heads * n_q * 128].view(n_heads, n_q, 128)
+    k_hat = workspace[n_heads * n_q * 128:].view(n_heads, n_k, 128)
+    return logits, q_hat, k_hat
+
+
+class _PredictLogits(torch.autograd.Function):
+    """Logits with gradients for the projections (the stage-1 teacher
+    trains them, veda/attention.py:446-450). Forward: the fp32 kernel.
+    Backward, with G = dL/dlogits / sqrt(D) and the features constant:
+        dq_hat = G k_hat,  dk_hat = G^T q_hat,
+        dP_q[heads[h]] += feats_q[h]^T dq_hat[h]  (and likewise for k)
+    as fp32 batched GEMMs (the `mean` residual carries no parameter)."""
+
+    @staticmethod
+    def forward(ctx, feats_q, feats_k, proj_q, proj_k, heads):
+        logits, q_hat, k_hat = _logits_and_embeddings(
+            feats_q, feats_k, proj_q.detach(), proj_k.detach(), heads)
+        ctx.save_for_backward(feats_q, feats_k, q_hat, k_hat, heads)
+        ctx.proj_shapes = (proj_q.shape, proj_k.shape)
+        return logits
+
+    @staticmethod
+    def backward(ctx, grad):
+        feats_q, feats_k, q_hat, k_hat, heads = ctx.saved_tensors
+        g = grad.float() / math.sqrt(q_hat.shape[-1])
+        d_qhat = torch.bmm(g, k_hat)
+        d_khat = torch.bmm(g.transpose(1, 2), q_hat)
+        grads = []
+        for feats, d_hat, shape in ((feats_q, d_qhat, ctx.proj_shapes[0]),
+                                    (feats_k, d_khat, ctx.proj_shapes[1])):
+            per_head = torch.bmm(feats.transpose(1, 2), d_hat)
+            grads.append(torch.zeros(shape, dtype=torch.float32,
+                                     device=feats.device).index_add_(
+                                         0, heads, per_head))
+        return None, None, grads[0], grads[1], None
+
+
+def predict_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
+                   proj_q: torch.Tensor, proj_k: torch.Tensor,
+                   heads: torch.Tensor) -> torch.Tensor:
+    """[H', n_q, n_k] fp32 logits of pooled features (predictor.py:251-338);
+    differentiable in proj_q / proj_k when they require gradients."""
+    if feats_q.dim() != 3 or feats_q.shape[-1] != 3 * 128:
+        raise ValueError('features must be [H\', n, 384]')
+    if not feats_q.is_cuda:
+        raise RuntimeError('the predictor kernels run on CUDA only')
+    heads = heads.to(device=feats_q.device, dtype=torch.int64).contiguous()
+    feats_q = feats_q.detach().float().contiguous()
+    feats_k = feats_k.detach().float().contiguous()
+    n_heads = feats_q.shape[0]
+    if heads.numel() != n_heads or feats_k.shape[0] != n_heads:
+        raise ValueError('heads and features disagree on the head count')
+    if torch.is_grad_enabled() and (proj_q.requires_grad
+                                    or proj_k.requires_grad):
+        if proj_q.dtype != torch.float32 or proj_k.dtype != torch.float32:
+            raise NotImplementedError('trainable projections must be fp32')
+        return _PredictLogits.apply(feats_q, feats_k, proj_q.contiguous(),
+                                    proj_k.contiguous(), heads)
+    return _logits_and_embeddings(feats_q, feats_k,
+                                  proj_q.detach().float().contiguous(),
+                                  proj_k.detach().float().contiguous(),
+                                  heads)[0]
 
 
 class LayerPredictor(nn.Module):

@@ -601,6 +601,40 @@ def zero_order_compensation(o_kept, lse_kept, q_tiles, k_tiles, v_tiles,
 
 
 # ---------------------------------------------------------------------------
+# stage-1 supervision: the seer KL (miowtion/veda/heatmap.py:113-180)
+# ---------------------------------------------------------------------------
+
+def seer_kl(logits, heat, kv_ok, direction='forward'):
+    """heatmap.py:125-180 in float64: the student is softmax(logits) over
+    the key tiles with kv_ok; the teacher is the heat clipped at 0 and
+    normalised per row. forward: sum of t * (log t - log s) over t > 0;
+    reverse: sum of s * (log s - log max(t, 1e-6)). Rows without heat are
+    left out; the mean is over rows per head, then over heads."""
+    if direction not in ('forward', 'reverse'):
+        raise ValueError(direction)
+    logits = np.asarray(logits, np.float64)
+    cols = np.asarray(kv_ok, bool)[None, None, :]
+    z = np.where(cols, logits, -np.inf)
+    zmax = z.max(-1, keepdims=True)
+    log_s = z - zmax - np.log(np.exp(z - zmax).sum(-1, keepdims=True))
+    t = np.where(cols, np.maximum(np.asarray(heat, np.float64), 0.0), 0.0)
+    total = t.sum(-1, keepdims=True)
+    live = total[..., 0] > 0
+    t = t / np.where(total > 0, total, 1.0)
+    with np.errstate(divide='ignore', invalid='ignore'):
+        if direction == 'forward':
+            pos = cols & (t > 0)
+            terms = np.where(pos, t * (np.log(np.where(pos, t, 1.0))
+                                       - np.where(pos, log_s, 0.0)), 0.0)
+        else:
+            log_t = np.log(np.maximum(t, 1e-6))
+            terms = np.where(cols, np.exp(log_s) * (log_s - log_t), 0.0)
+    rows = terms.sum(-1)
+    per_head = (rows * live).sum(-1) / np.maximum(live.sum(-1), 1)
+    return float(per_head.mean())
+
+
+# ---------------------------------------------------------------------------
 # (f) tile search: oracle relative error (miowtion/veda/search.py:53-175)
 # ---------------------------------------------------------------------------
 

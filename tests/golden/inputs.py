@@ -126,3 +126,14 @@ def projection(dim, seed):
     """[dim] fp32 weights for per-row checksums out[r, h] . w."""
     gen = torch.Generator().manual_seed(seed)
     return torch.randn(dim, generator=gen)
+
+
+# TeacherCollector (stage 1): text rows, a padded target grid cut by two tile
+# shapes over the heads, two layers; each case a heat reduction, a KL
+# direction and a share of supervised query tiles.
+TEACHER = dict(text=130, grid=(4, 12, 20), seq_len=1100, heads=4, dim=128,
+               seed=81, pred_seed=82, pred_std=0.02, layers=2,
+               shapes=[(2, 8, 8), (1, 8, 16)], head_shape=[0, 1, 0, 1],
+               ratio=0.4, gen_seed=7, grad_scale=0.5,
+               cases={'max_fwd': ('max', 'forward', 0.5),
+                      'sum_rev': ('sum', 'reverse', 1.0)})

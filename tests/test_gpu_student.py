@@ -87,7 +87,8 @@ def test_two_shapes_text_rows_and_padding_match_oracle():
         qt, fq = tiling.gather_and_pool(q.to(DEV), tl, g.heads)
         kt, fk = tiling.gather_and_pool(k.to(DEV), tl, g.heads)
         logits = student.predictor.layers[0](fq, fk, g.heads)
-        np.testing.assert_allclose(logits.cpu().numpy(), grp['logits'],
+        np.testing.assert_allclose(logits.detach().cpu().numpy(),
+                                   grp['logits'],
                                    rtol=1e-4, atol=1e-5)
         lists = veda_mask.select_block_lists(
             logits[:, :tl.n_video_tiles], tl, clip.blocks(tl),
