@@ -45,7 +45,12 @@ struct GatherParams {
   int64_t n_tiles;
 };
 
-__global__ void __launch_bounds__(kPoolThreads)
+// kMode: 0 gather only, 1 also mean/max/min, 2 also the second moments.
+// Separate instantiations keep the gather and the first-moment pooling at
+// the registers they need (the second moments hold every row's values for a
+// second pass), so more CTAs per SM keep loads in flight.
+template <int kMode>
+__global__ void __launch_bounds__(kPoolThreads, kMode == 2 ? 1 : 4)
     gather_pool_kernel(GatherParams p, int64_t n_tiles) {
   // Tiles vary fastest across the grid: the CTAs in flight write one head's
   // tiles contiguously (measured faster than all heads of a tile at once).
@@ -93,7 +98,9 @@ __global__ void __launch_bounds__(kPoolThreads)
                                 h * p.out_stride_h + 8 * c8) = vals[i];
     }
   }
-  if (p.feats == nullptr && p.sq == nullptr && p.var == nullptr) return;
+  if constexpr (kMode == 0) {
+    return;
+  } else {
 
   __shared__ float red[3][kPoolThreads / 32][kHeadDim];
   __shared__ float mean_s[kHeadDim];
@@ -157,7 +164,7 @@ __global__ void __launch_bounds__(kPoolThreads)
       f[2 * kHeadDim + tid] = empty ? 0.f : b;
     }
   }
-  if (p.sq == nullptr && p.var == nullptr) return;
+  if constexpr (kMode == 2) {
   __syncthreads();
   // Second moments from the rows still held in registers; the centred one
   // is two-pass (predictor.py:133-168 explains why not E[x^2] - E[x]^2).
@@ -208,6 +215,8 @@ __global__ void __launch_bounds__(kPoolThreads)
     if (p.sq != nullptr) p.sq[base] = empty ? 0.f : a / denom;
     if (p.var != nullptr) p.var[base] = empty ? 0.f : b / denom;
   }
+  }  // kMode == 2
+  }  // kMode > 0
 }
 
 struct ScatterParams {
@@ -255,6 +264,22 @@ __global__ void gather_lse_kernel(const float* lse, int64_t ls, int64_t lh,
   const int h = static_cast<int>(i % n_heads);
   const int64_t src = perm[slot];
   out[i] = src >= 0 ? lse[src * ls + heads[h] * lh] : 0.f;
+}
+
+int launch_gather(const GatherParams& p, int64_t n_tiles, int32_t n_heads,
+                  void* stream) {
+  VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
+  const unsigned grid = static_cast<unsigned>(n_tiles * n_heads);
+  if (p.sq != nullptr || p.var != nullptr)
+    gather_pool_kernel<2><<<grid, kPoolThreads, 0, as_stream(stream)>>>(
+        p, n_tiles);
+  else if (p.feats != nullptr)
+    gather_pool_kernel<1><<<grid, kPoolThreads, 0, as_stream(stream)>>>(
+        p, n_tiles);
+  else
+    gather_pool_kernel<0><<<grid, kPoolThreads, 0, as_stream(stream)>>>(
+        p, n_tiles);
+  return check_launch("gather_pool_kernel");
 }
 
 int check_rows(const void* p, int64_t stride_row, int64_t stride_head,
@@ -311,9 +336,7 @@ extern "C" int veda_gather_pool(const void* x, int64_t x_stride_s,
   p.var = var;
   p.n_tiles = n_tiles;
   VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
-  gather_pool_kernel<<<static_cast<unsigned>(n_tiles * n_heads), kPoolThreads,
-                       0, as_stream(stream)>>>(p, n_tiles);
-  return check_launch("gather_pool_kernel");
+  return launch_gather(p, n_tiles, n_heads, stream);
 }
 
 extern "C" int veda_gather_pool_images(const void* x, int64_t x_stride_s,
@@ -344,9 +367,7 @@ extern "C" int veda_gather_pool_images(const void* x, int64_t x_stride_s,
   p.feats = feats;
   p.n_tiles = n_tiles;
   VEDA_REQUIRE(n_tiles * n_heads < (int64_t(1) << 31), "too many tiles");
-  gather_pool_kernel<<<static_cast<unsigned>(n_tiles * n_heads), kPoolThreads,
-                       0, as_stream(stream)>>>(p, n_tiles);
-  return check_launch("gather_pool_kernel");
+  return launch_gather(p, n_tiles, n_heads, stream);
 }
 
 extern "C" int veda_scatter(const void* tiled, int64_t t_stride_n,

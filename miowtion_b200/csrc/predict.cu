@@ -18,7 +18,7 @@ namespace {
 
 constexpr int kFeat = 3 * kHeadDim;  // 384
 constexpr int kEmbRows = 64;
-constexpr int kEmbK = 32;
+constexpr int kEmbK = 16;
 
 // out[h, i, :] = feats[h, i, :] @ proj[heads[h]] + feats[h, i, :D]
 // grid (ceil(n/64), H', 2): z selects the q or the k side.
@@ -44,42 +44,69 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
   float* out = (k_side ? p.out[1] : p.out[0]) +
                static_cast<int64_t>(h) * n * kHeadDim;
 
-  __shared__ float a_s[kEmbK][kEmbRows + 4];  // transposed feats chunk
-  __shared__ float b_s[kEmbK][kHeadDim];
+  // Two buffers: chunk c + 1 is loaded into registers while chunk c is
+  // multiplied from shared memory.
+  __shared__ float a_s[2][kEmbK][kEmbRows + 4];  // transposed feats chunk
+  __shared__ float b_s[2][kEmbK][kHeadDim];
   const int tid = threadIdx.x;
   const int tr = tid / 32;  // rows tr*8 .. +8
   const int tc = tid % 32;  // cols tc*4 .. +4
+  constexpr int kA = kEmbRows * kEmbK / 256;  // feats values per thread
+  constexpr int kB = kEmbK * kHeadDim / 256;  // proj values per thread
+  float ra[kA], rb[kB];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < kA; ++i) {
+      const int e = tid + 256 * i;
+      const int64_t row = row0 + e / kEmbK;
+      ra[i] = row < n ? feats[row * kFeat + k0 + e % kEmbK] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int e = tid + 256 * i;
+      rb[i] = proj[static_cast<int64_t>(k0 + e / kHeadDim) * kHeadDim +
+                   e % kHeadDim];
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < kA; ++i) {
+      const int e = tid + 256 * i;
+      a_s[buf][e % kEmbK][e / kEmbK] = ra[i];
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int e = tid + 256 * i;
+      b_s[buf][e / kHeadDim][e % kHeadDim] = rb[i];
+    }
+  };
   float acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
-  for (int k0 = 0; k0 < kFeat; k0 += kEmbK) {
-    // feats chunk [64 rows x 32 k] -> a_s[k][row]
-    for (int e = tid; e < kEmbRows * kEmbK; e += 256) {
-      const int r = e / kEmbK, k = e % kEmbK;
-      const int64_t row = row0 + r;
-      a_s[k][r] = row < n ? feats[row * kFeat + k0 + k] : 0.f;
-    }
-    for (int e = tid; e < kEmbK * kHeadDim; e += 256) {
-      const int k = e / kHeadDim, c = e % kHeadDim;
-      b_s[k][c] = proj[static_cast<int64_t>(k0 + k) * kHeadDim + c];
-    }
+  fetch(0);
+  constexpr int kChunks = kFeat / kEmbK;
+  for (int c = 0; c < kChunks; ++c) {
+    const int buf = c & 1;
+    stash(buf);
     __syncthreads();
+    if (c + 1 < kChunks) fetch((c + 1) * kEmbK);
 #pragma unroll 8
     for (int k = 0; k < kEmbK; ++k) {
       float a[8], b[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] = a_s[k][tr * 8 + i];
+      for (int i = 0; i < 8; ++i) a[i] = a_s[buf][k][tr * 8 + i];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = b_s[k][tc * 4 + j];
+      for (int j = 0; j < 4; ++j) b[j] = b_s[buf][k][tc * 4 + j];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
-    __syncthreads();
+    // The next stash writes the other buffer; the one after writes this
+    // buffer again, behind the next iteration's barrier.
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -103,8 +130,10 @@ __global__ void __launch_bounds__(256)
   const int64_t j0 = static_cast<int64_t>(blockIdx.x) * 64;
   const float* qh = q_hat + static_cast<int64_t>(h) * n_q * kHeadDim;
   const float* kh = k_hat + static_cast<int64_t>(h) * n_k * kHeadDim;
-  __shared__ float q_s[32][64 + 4];
-  __shared__ float k_s[32][64 + 4];
+  // Two buffers: chunk c + 1 is loaded into registers while chunk c is
+  // multiplied from shared memory.
+  __shared__ float q_s[2][32][64 + 4];
+  __shared__ float k_s[2][32][64 + 4];
   const int tid = threadIdx.x;
   const int ti = tid / 16, tj = tid % 16;
   float acc[4][4];
@@ -112,27 +141,40 @@ __global__ void __launch_bounds__(256)
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
-    for (int e = tid; e < 64 * 32; e += 256) {
+  float rq[8], rk[8];
+  auto fetch = [&](int d0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + 256 * i;
       const int r = e / 32, d = e % 32;
-      q_s[d][r] = (i0 + r < n_q) ? qh[(i0 + r) * kHeadDim + d0 + d] : 0.f;
-      k_s[d][r] = (j0 + r < n_k) ? kh[(j0 + r) * kHeadDim + d0 + d] : 0.f;
+      rq[i] = (i0 + r < n_q) ? qh[(i0 + r) * kHeadDim + d0 + d] : 0.f;
+      rk[i] = (j0 + r < n_k) ? kh[(j0 + r) * kHeadDim + d0 + d] : 0.f;
+    }
+  };
+  fetch(0);
+  for (int c = 0; c < kHeadDim / 32; ++c) {
+    const int buf = c & 1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + 256 * i;
+      q_s[buf][e % 32][e / 32] = rq[i];
+      k_s[buf][e % 32][e / 32] = rk[i];
     }
     __syncthreads();
+    if (c + 1 < kHeadDim / 32) fetch((c + 1) * 32);
 #pragma unroll 8
     for (int d = 0; d < 32; ++d) {
       float a[4], b[4];
 #pragma unroll
       for (int x = 0; x < 4; ++x) {
-        a[x] = q_s[d][ti * 4 + x];
-        b[x] = k_s[d][tj * 4 + x];
+        a[x] = q_s[buf][d][ti * 4 + x];
+        b[x] = k_s[buf][d][tj * 4 + x];
       }
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(a[x], b[y], acc[x][y]);
     }
-    __syncthreads();
   }
   float* out = logits + static_cast<int64_t>(h) * n_q * n_k;
 #pragma unroll
