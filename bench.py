@@ -314,6 +314,11 @@ def main():
     ap.add_argument('--query-tiles', type=int, default=40,
                     help='sampled query tiles for --only search (the '
                          "reference's SearchConfig default)")
+    ap.add_argument('--pieces', type=int, default=1,
+                    help='ulysses: head pieces whose exchanges overlap')
+    ap.add_argument('--reserve-sms', type=int, default=16,
+                    help='ulysses: SMs the attention leaves to NCCL while '
+                    'pieces overlap')
     ap.add_argument('--parallel', choices=['clips', 'ulysses'], default=None,
                     help='multi-GPU mode (default: clips for cfg2, ulysses '
                          'for cfg3/cfg4)')
@@ -356,7 +361,8 @@ def main():
     if heads_split:
         shard = seq_len // world
         q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
-        fn = ulysses.UlyssesSparseStudent(student)
+        fn = ulysses.UlyssesSparseStudent(student, pieces=args.pieces,
+                                          reserve_sms=args.reserve_sms)
     else:
         # The whole layer on this rank's own clip (clip 0 on one GPU).
         q, k, v = synthetic_qkv(cfg, seq_len, 0, device, clip=rank)
@@ -399,7 +405,9 @@ def main():
             kt, fk = tiling.gather_and_pool(ulysses.seq_to_heads(k)
                                             if heads_split else k, tl,
                                             group.heads)
-            logits = student.predictor.layers[0](fq, fk, group.heads)
+            logits = student.predictor.layers[0](
+                fq, fk, group.heads + (rank * local_heads if heads_split
+                                       else 0))
             lists = veda_mask.select_block_lists(
                 logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
             blocks += int(lists.part_cnt.sum() + lists.full_cnt.sum())

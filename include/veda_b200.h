@@ -65,6 +65,14 @@ int veda_last_error(char* buf, size_t size);
  * set when a bounded wait times out. Synchronizes the current device. */
 int veda_device_status(int32_t* status, int32_t reset);
 
+/* No counterpart in the reference (it overlaps no communication). Leaves n
+ * SMs free of the persistent attention forward (veda_bsa_fwd,
+ * veda_bsa_fwd_packed, veda_dense_fwd, veda_bsa_fwd_heat launch at most
+ * SMs - n CTAs), so that kernels running beside it, such as NCCL
+ * collectives on another stream, find an SM. Process-wide; 0 by default;
+ * n in [0, 128]. */
+int veda_set_sm_reserve(int32_t n);
+
 /* 1 when the current device is sm_100 (B200) and the library can run. */
 int veda_supported_device(void);
 

@@ -375,7 +375,12 @@ class SparseStudent:
     events = _NO_EVENTS  # set a StageEvents to time the stages
 
     def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
-                 predictor: veda_predictor.TileScorePredictor):
+                 predictor: veda_predictor.TileScorePredictor,
+                 head_offset: int = 0):
+        """`head_offset` (not in the reference, which runs every head of a
+        layer on one GPU): the predictor's index of the first head of q,
+        for a caller that hands this student a contiguous slice of the
+        heads (head-parallel ranks, head chunks)."""
         reason = kernels.unavailable_reason(clip.device)
         if reason is not None:
             raise RuntimeError(
@@ -393,6 +398,7 @@ class SparseStudent:
         self.clip = clip
         self.plan = plan
         self.predictor = predictor
+        self.head_offset = head_offset
         self.calls = {'sparse': 0, 'dense': 0}
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -438,8 +444,8 @@ class SparseStudent:
         ev.stop(t)
         with torch.no_grad():
             t = ev.start('score')
-            logits = self.predictor.layers[layer_index](feats_q, feats_k,
-                                                        heads)
+            logits = self.predictor.layers[layer_index](
+                feats_q, feats_k, heads + self.head_offset)
             ev.stop(t)
             t = ev.start('topk')
             lists = veda_mask.select_block_lists(
@@ -480,8 +486,8 @@ class SparseStudent:
         ev.stop(t)
         with torch.no_grad():
             t = ev.start('score')
-            logits = self.predictor.layers[layer_index](feats_q, feats_k,
-                                                        heads)
+            logits = self.predictor.layers[layer_index](
+                feats_q, feats_k, heads + self.head_offset)
             ev.stop(t)
             t = ev.start('topk')
             lists = veda_mask.select_block_lists(
@@ -512,8 +518,8 @@ class SparseStudent:
                                                           tile_layout, heads)
                 k_tiles, feats_k = tiling.gather_and_pool(k.detach(),
                                                           tile_layout, heads)
-                logits = self.predictor.layers[layer_index](feats_q, feats_k,
-                                                            heads)
+                logits = self.predictor.layers[layer_index](
+                    feats_q, feats_k, heads + self.head_offset)
                 lists = veda_mask.select_block_lists(
                     logits[:, :tile_layout.n_video_tiles], tile_layout,
                     self.clip.blocks(tile_layout), want_mask=True)

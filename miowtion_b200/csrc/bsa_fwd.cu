@@ -1017,7 +1017,9 @@ int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
     configured = true;
   }
   if (p.n_items == 0) return VEDA_OK;
-  const int grid = p.n_items < sms ? p.n_items : sms;
+  // SMs left free for kernels that overlap this one (collectives).
+  const int cap = sms - sm_reserve() > 0 ? sms - sm_reserve() : 1;
+  const int grid = p.n_items < cap ? p.n_items : cap;
   bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(maps, p);
   return check_launch("bsa_fwd_kernel");
 }

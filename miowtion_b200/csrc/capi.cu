@@ -3,6 +3,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -52,6 +53,12 @@ unsigned int* device_status_ptr() {
   }
   return cache[dev];
 }
+
+namespace {
+std::atomic<int> g_sm_reserve{0};
+}  // namespace
+
+int sm_reserve() { return g_sm_reserve.load(std::memory_order_relaxed); }
 
 int require_sm100(const char* op) {
   int dev = 0;
@@ -316,6 +323,12 @@ extern "C" int veda_device_status(int32_t* status, int32_t reset) {
   VEDA_CUDA(cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost));
   if (status != nullptr) *status = static_cast<int32_t>(v);
   if (reset) VEDA_CUDA(cudaMemset(p, 0, sizeof(unsigned int)));
+  return VEDA_OK;
+}
+
+extern "C" int veda_set_sm_reserve(int32_t n) {
+  VEDA_REQUIRE(n >= 0 && n <= 128, "the SM reserve must lie in [0, 128]");
+  g_sm_reserve.store(n, std::memory_order_relaxed);
   return VEDA_OK;
 }
 

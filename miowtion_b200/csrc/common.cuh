@@ -41,6 +41,9 @@ int require_sm100(const char* op);
 // Device status word written by kernels whose bounded waits expire.
 unsigned int* device_status_ptr();
 
+// SMs the persistent attention forward leaves free (veda_set_sm_reserve).
+int sm_reserve();
+
 // 3D bf16 tensor map over a [rows, heads, 128] tensor with a (64, 1, 128)
 // box and 128-byte swizzle: coordinates are (d0 in {0, 64}, head, row0).
 int make_tile_map(CUtensorMap* map, const void* base, int64_t rows,

@@ -4,13 +4,22 @@ The reference runs one clip per GPU and has no sequence parallelism
 (miowtion/train/parallel.py:3-5): a tile permutation needs every row of a
 sequence on one device. Heads, however, are independent through the whole
 Veda path (veda/attention.py:735-738), so a sequence-sharded [S/P, H, D]
-activation is exchanged with one NCCL all-to-all into [S, H/P, D], the local
-heads run the complete sparse layer, and a second all-to-all returns
-[S/P, H, D]. The predictor stays replicated (predictor.py:344-348).
+activation is exchanged with NCCL all-to-alls into [S, H/P, D], the local
+heads run the complete sparse layer, and all-to-alls return [S/P, H, D].
+The predictor stays replicated (predictor.py:344-348); each rank scores its
+own heads with their global indices.
 
-Exchange layout: the send buffer is [P, S/P, H/P, D] (chunk p = this
-rank's rows of rank p's heads); the receive buffer [P, S/P, H/P, D] is then
-exactly [S, H/P, D] in sequence order, so no unpack copy is needed.
+The local heads can be processed in `pieces` contiguous chunks so that
+the exchanges overlap the attention: the inputs of piece j + 1 and the
+output of piece j - 1 cross NVLink (asynchronous collectives on NCCL's
+stream) while piece j computes. Measured at config 3 on 2 B200 this does
+not pay: the persistent attention kernel holds every SM, so NCCL's kernels
+either delay some of its CTAs (pieces 2: 20.1 ms/layer) or get SMs it gives
+up (pieces 2, 16 SMs reserved: 20.5 ms), against 19.5 ms with one piece.
+The default is therefore one piece. Every rank issues the same collectives
+in the same order. Exchange layout of a piece of c heads: the send buffer is
+[P, S/P, c, D] (chunk p = this rank's rows of rank p's piece heads); the
+receive buffer [P, S/P, c, D] is then [S, c, D] in sequence order.
 """
 
 from __future__ import annotations
@@ -18,6 +27,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from miowtion_b200 import _lib
 from miowtion_b200 import attention as veda_attention
 from miowtion_b200 import plan as veda_plan
 
@@ -34,14 +44,31 @@ def local_plan(plan: veda_plan.TilePlan, rank: int,
                               dict(plan.provenance, rank=rank, world=world))
 
 
+def piece_bounds(local_heads: int, pieces: int) -> list[tuple[int, int]]:
+    """[start, stop) of each piece of the local heads (at most `pieces`,
+    none empty)."""
+    pieces = max(1, min(pieces, local_heads))
+    size = -(-local_heads // pieces)
+    return [(a, min(a + size, local_heads))
+            for a in range(0, local_heads, size)]
+
+
+def _pack(x: torch.Tensor, world: int, start: int, stop: int) -> torch.Tensor:
+    """[S/P, H, D] -> [P, S/P, c, D]: chunk p holds heads
+    p * H/P + [start, stop)."""
+    rows, heads, dim = x.shape
+    per = heads // world
+    return x.view(rows, world, per, dim)[:, :, start:stop].transpose(
+        0, 1).contiguous()
+
+
 def seq_to_heads(x: torch.Tensor, group=None) -> torch.Tensor:
     """[S/P, H, D] on every rank -> [S, H/P, D] (rank r gets heads block r)."""
     world = dist.get_world_size(group)
     rows, heads, dim = x.shape
     if heads % world:
         raise ValueError('heads must divide by the world size')
-    send = x.view(rows, world, heads // world, dim).transpose(0, 1)
-    send = send.contiguous()
+    send = _pack(x, world, 0, heads // world)
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)
     return recv.view(world * rows, heads // world, dim)
@@ -61,16 +88,110 @@ def heads_to_seq(y: torch.Tensor, group=None) -> torch.Tensor:
 
 
 class UlyssesSparseStudent:
-    """`AttentionFn` over sequence-sharded q, k, v [S/P, H, D] per rank."""
+    """`AttentionFn` over sequence-sharded q, k, v [S/P, H, D] per rank.
 
-    def __init__(self, student: veda_attention.SparseStudent, group=None):
+    `student` is the rank's SparseStudent over its local plan (heads
+    [rank * H/P, (rank + 1) * H/P)); its clip and predictor are shared by
+    the per-piece students built here. `piece_factory(layer, start, stop,
+    first_head)` may replace that construction: it returns the attention
+    function of local heads [start, stop), whose first global head is
+    `first_head` (the CPU tests pass stand-ins this way).
+    """
+
+    def __init__(self, student: veda_attention.SparseStudent | None,
+                 group=None, pieces: int = 1, piece_factory=None,
+                 reserve_sms: int = 16):
         self.student = student
         self.group = group
+        self.pieces = pieces
+        self.piece_factory = piece_factory
+        # While pieces overlap exchanges, the attention leaves this many
+        # SMs to NCCL's kernels (its persistent CTAs would otherwise hold
+        # every SM until it ends).
+        self.reserve_sms = reserve_sms
+        self._students: dict = {}
+
+    def _piece_student(self, layer_index: int, start: int, stop: int,
+                       head0: int) -> veda_attention.SparseStudent:
+        key = (layer_index, start, stop)
+        if key not in self._students and self.piece_factory is not None:
+            self._students[key] = self.piece_factory(layer_index, start, stop,
+                                                     head0 + start)
+        if key not in self._students:
+            base = self.student
+            plan = base.plan
+            sub = veda_plan.TilePlan(
+                plan.geometry, plan.grid, plan.shapes,
+                [list(r)[start:stop] for r in plan.head_shape],
+                dict(plan.provenance, piece=[start, stop]))
+            self._students[key] = veda_attention.SparseStudent(
+                base.clip, sub, base.predictor, head_offset=head0 + start)
+        return self._students[key]
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  layer_index: int) -> torch.Tensor:
-        qh = seq_to_heads(q, self.group)
-        kh = seq_to_heads(k, self.group)
-        vh = seq_to_heads(v, self.group)
-        out = self.student(qh, kh, vh, layer_index)
-        return heads_to_seq(out, self.group)
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        rows, heads, dim = q.shape
+        if heads % world:
+            raise ValueError('heads must divide by the world size')
+        per = heads // world
+        if self.piece_factory is None and len(
+                self.student.plan.head_shape[layer_index]) != per:
+            raise ValueError('the student plan does not hold this rank\'s '
+                             f'{per} heads')
+        bounds = piece_bounds(per, self.pieces)
+        reserve = self.reserve_sms if (world > 1 and len(bounds) > 1
+                                       and self.piece_factory is None) else 0
+        if reserve:
+            _lib.call('veda_set_sm_reserve', reserve)
+        try:
+            return self._run(q, k, v, layer_index, world, rank, per, bounds)
+        finally:
+            if reserve:
+                _lib.call('veda_set_sm_reserve', 0)
+
+    def _run(self, q, k, v, layer_index, world, rank, per, bounds):
+        rows, _, dim = q.shape
+        inputs: dict = {}
+
+        def post_inputs(j: int) -> None:
+            start, stop = bounds[j]
+            bufs, works = [], []
+            for x in (q, k, v):
+                send = _pack(x, world, start, stop)
+                recv = torch.empty_like(send)
+                works.append(dist.all_to_all_single(recv, send,
+                                                    group=self.group,
+                                                    async_op=True))
+                bufs.append((send, recv))
+            inputs[j] = (bufs, works)
+
+        out = torch.empty_like(q)
+        outputs = []
+        post_inputs(0)
+        for j, (start, stop) in enumerate(bounds):
+            if j + 1 < len(bounds):
+                post_inputs(j + 1)
+            bufs, works = inputs.pop(j)
+            for w in works:
+                w.wait()
+            c = stop - start
+            qj, kj, vj = (recv.view(world * rows, c, dim)
+                          for _, recv in bufs)
+            student = self._piece_student(layer_index, start, stop,
+                                          rank * per)
+            if self.student is not None:
+                # Stage timers set on the rank's student cover its pieces.
+                student.events = self.student.events
+            result = student(qj, kj, vj, layer_index)
+            back = torch.empty_like(result).view(world, rows, c, dim)
+            work = dist.all_to_all_single(
+                back, result.view(world, rows, c, dim), group=self.group,
+                async_op=True)
+            outputs.append((start, stop, back, result, work))
+        for start, stop, back, _result, work in outputs:
+            work.wait()
+            out.view(rows, world, per, dim)[:, :, start:stop] = back.transpose(
+                0, 1)
+        return out

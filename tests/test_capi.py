@@ -50,3 +50,11 @@ def test_host_side_validation_needs_no_gpu(lib):
 def test_column_block_struct_layout():
     assert ctypes.sizeof(_lib.ColumnBlockC) == 32
     assert ctypes.sizeof(_lib.Span) == 32
+
+
+def test_sm_reserve_is_validated_on_the_host(lib):
+    with pytest.raises(ValueError, match='reserve'):
+        _lib.call('veda_set_sm_reserve', -1)
+    with pytest.raises(ValueError, match='reserve'):
+        _lib.call('veda_set_sm_reserve', 1000)
+    _lib.call('veda_set_sm_reserve', 0)

@@ -202,3 +202,28 @@ def test_packed_forward_full_size_rows_cfg3():
     real = rows >= 0
     got = np32(out)[rows[real], 1]
     np.testing.assert_allclose(got, want[real][:, 0], rtol=2e-2, atol=2e-2)
+
+
+def test_sm_reserve_changes_the_grid_not_the_result():
+    spec = LAYOUT_SPECS['padded']
+    lay = tiling.build_tile_layout(spans_of(spec), spec['used'],
+                                   spec['seq_len'], DEV)
+    q, k, v = (t.to(DEV) for t in inputs.qkv(spec['seq_len'], 3, 128, 63,
+                                             torch.bfloat16))
+    hd = torch.tensor([0, 1, 2], device=DEV)
+    n = lay.n_tiles
+    gen = torch.Generator().manual_seed(15)
+    mask = torch.rand(3, n, n, generator=gen) < 0.3
+    mask[:, torch.arange(n), torch.arange(n)] = True
+    lists = _lists(mask, lay)
+    ki, vi = (tiling.gather_images(t, lay, hd) for t in (k, v))
+    outs = []
+    for reserve in (0, 120, 0):
+        _lib.call('veda_set_sm_reserve', reserve)
+        out = torch.zeros_like(q)
+        kernels.block_sparse_attention_packed(q, ki, vi, lists, lay, hd, out,
+                                              kv_tiles='images')
+        outs.append(out)
+    _lib.call('veda_set_sm_reserve', 0)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])

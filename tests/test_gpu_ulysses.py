@@ -1,0 +1,64 @@
+"""The head-parallel wrapper on one GPU (a one-rank NCCL group): every
+piece student scores its heads with their global predictor indices, so the
+pieced, exchanged layer equals the plain SparseStudent bit for bit (heads
+are independent through every kernel). The multi-rank exchange itself is
+tested over gloo on the CPU (tests/test_ulysses.py) and measured by
+bench.py --gpus N --config cfg3."""
+
+import os
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+
+import inputs
+from miowtion_b200 import attention as veda_attention
+from miowtion_b200 import mask as veda_mask
+from miowtion_b200 import plan as veda_plan
+from miowtion_b200 import predictor as veda_predictor
+from miowtion_b200 import tiling
+from miowtion_b200 import ulysses
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device('cuda', 0)
+
+
+@pytest.fixture(scope='module')
+def one_rank_group():
+    torch.cuda.set_device(DEV)
+    with tempfile.TemporaryDirectory() as tmp:
+        store = dist.FileStore(os.path.join(tmp, 'store'), 1)
+        dist.init_process_group('nccl', store=store, rank=0, world_size=1,
+                                device_id=DEV)
+        yield
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize('pieces', [1, 3])
+def test_pieced_layer_equals_plain_student(one_rank_group, pieces):
+    text, grid, heads = 130, (4, 12, 20), 5
+    used = text + grid[0] * grid[1] * grid[2]
+    seq_len = used + 14
+    layout = veda_attention.PackedLayout(
+        seq_len, used, (veda_attention.VideoSpan(text, grid),))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=0.3))
+    clip = veda_attention.ClipTiling(layout, config, DEV)
+    plan = veda_plan.TilePlan('u', grid, [tiling.TileShape(2, 8, 8),
+                                          tiling.TileShape(1, 8, 16)],
+                              [[0, 1, 1, 0, 1]])
+    pred = veda_predictor.TileScorePredictor(1, heads, 128)
+    pq, pk = inputs.predictor_weights(heads, 128, 44, 0.02)
+    with torch.no_grad():
+        pred.layers[0].proj_q.copy_(pq)
+        pred.layers[0].proj_k.copy_(pk)
+    student = veda_attention.SparseStudent(clip, plan, pred.to(DEV))
+    q, k, v = (t.to(DEV) for t in inputs.qkv(seq_len, heads, 128, 45,
+                                             torch.bfloat16))
+    with torch.no_grad():
+        want = student(q, k, v, 0)
+        got = ulysses.UlyssesSparseStudent(student, pieces=pieces)(q, k, v, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(got[:used], want[:used])

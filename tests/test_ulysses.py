@@ -36,9 +36,9 @@ class _PerHeadScale:
     """Stand-in attention function: scales local head j by its global head
     id + 1 and checks the shapes it is given."""
 
-    def __init__(self, rank: int, world: int):
-        self.first = rank * HEADS // world
-        self.local = HEADS // world
+    def __init__(self, first: int, local: int):
+        self.first = first
+        self.local = local
 
     def __call__(self, q, k, v, layer_index):
         assert q.shape == (SEQ, self.local, DIM)
@@ -63,13 +63,18 @@ def _worker(rank: int, world: int, port: int, errors) -> None:
         # heads_to_seq inverts it.
         back = ulysses.heads_to_seq(got)
         assert torch.equal(back, q[rows]), 'heads_to_seq'
-        # The wrapper: every rank ends with its rows of every head.
-        fn = ulysses.UlyssesSparseStudent(_PerHeadScale(rank, world))
-        out = fn(q[rows].contiguous(), k[rows].contiguous(),
-                 v[rows].contiguous(), 3)
+        # The wrapper: every rank ends with its rows of every head, for any
+        # number of overlapped pieces of its heads.
         ids = torch.arange(HEADS, dtype=q.dtype) + 1
         want = (q + k + v)[rows] * ids[None, :, None] + 3
-        assert torch.equal(out, want), 'UlyssesSparseStudent'
+        for pieces in (1, 2, 3):
+            fn = ulysses.UlyssesSparseStudent(
+                None, pieces=pieces,
+                piece_factory=lambda layer, a, b, first: _PerHeadScale(
+                    first, b - a))
+            out = fn(q[rows].contiguous(), k[rows].contiguous(),
+                     v[rows].contiguous(), 3)
+            assert torch.equal(out, want), f'UlyssesSparseStudent {pieces}'
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # surfaced by the parent
@@ -111,3 +116,10 @@ def test_local_plan_splits_heads_in_contiguous_blocks():
         assert all(len(p.head_shape[0]) == 48 // world for p in parts)
     with pytest.raises(ValueError):
         ulysses.local_plan(plan, 0, 5)
+
+
+def test_piece_bounds_cover_the_local_heads():
+    assert ulysses.piece_bounds(6, 2) == [(0, 3), (3, 6)]
+    assert ulysses.piece_bounds(5, 2) == [(0, 3), (3, 5)]
+    assert ulysses.piece_bounds(2, 3) == [(0, 1), (1, 2)]
+    assert ulysses.piece_bounds(24, 1) == [(0, 24)]
