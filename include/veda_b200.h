@@ -134,6 +134,18 @@ int veda_scatter(const void* tiled, int64_t t_stride_n, int64_t t_stride_h,
                  int32_t n_heads, void* out, int64_t out_stride_s,
                  int64_t out_stride_h, void* stream);
 
+/* No counterpart in the reference (it has no head parallelism). The send /
+ * receive layout of the head-parallel all-to-all. The strided side holds,
+ * per row, `blocks` segments of seg_bytes at row * row_bytes + b *
+ * block_bytes + offset_bytes (one per rank's heads, or a piece of them);
+ * the packed side holds them as [block][row][seg_bytes]. pack != 0 copies
+ * strided (src) -> packed (dst), pack == 0 packed (src) -> strided (dst).
+ * All sizes and offsets multiples of 16 bytes, buffers 16-byte aligned. */
+int veda_head_blocks(const void* src, void* dst, int64_t rows,
+                     int32_t blocks, int64_t seg_bytes, int64_t row_bytes,
+                     int64_t block_bytes, int64_t offset_bytes, int32_t pack,
+                     void* stream);
+
 /* Replaces miowtion/veda/attention.py:299-305 (_gather_lse):
  *   out[slot, h] = lse[perm[slot], heads[h]] (0 where perm < 0). */
 int veda_gather_lse(const float* lse, int64_t l_stride_s, int64_t l_stride_h,

@@ -59,6 +59,8 @@ SIGNATURES = {
     'veda_gather_pool_images': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_ptr,
                                         c_i64, c_ptr, c_i32, c_ptr, c_ptr,
                                         c_ptr]),
+    'veda_head_blocks': (c_i32, [c_ptr, c_ptr, c_i64, c_i32, c_i64, c_i64,
+                                 c_i64, c_i64, c_i32, c_ptr]),
     'veda_scatter': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_i32,
                              c_ptr, c_i64, c_i64, c_ptr]),
     'veda_gather_lse': (c_i32, [c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr,

@@ -282,6 +282,30 @@ int launch_gather(const GatherParams& p, int64_t n_tiles, int32_t n_heads,
   return check_launch("gather_pool_kernel");
 }
 
+// Head-block exchange layout for the head-parallel all-to-all. The
+// strided side holds, per row, `blocks` segments of w bytes at
+// row * row_bytes + b * block_bytes + offset; the packed side holds them as
+// [block][row][w]. pack copies strided -> packed, unpack the reverse.
+// 16-byte vectors (all sizes are multiples of 16), grid-stride.
+__global__ void head_blocks_kernel(const uint4* __restrict__ src,
+                                   uint4* __restrict__ dst, int64_t rows,
+                                   int blocks, int64_t w16, int64_t row16,
+                                   int64_t block16, int64_t off16, int pack) {
+  const int64_t total = rows * blocks * w16;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x +
+                   threadIdx.x;
+       i < total; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t j = i % w16;
+    const int64_t r = (i / w16) % rows;
+    const int64_t b = i / (w16 * rows);
+    const int64_t strided = r * row16 + b * block16 + off16 + j;
+    if (pack)
+      dst[i] = src[strided];
+    else
+      dst[strided] = src[i];
+  }
+}
+
 int check_rows(const void* p, int64_t stride_row, int64_t stride_head,
                const char* name) {
   if (reinterpret_cast<uintptr_t>(p) % 16 != 0 || stride_row % 8 != 0 ||
@@ -413,4 +437,38 @@ extern "C" int veda_gather_lse(const float* lse, int64_t l_stride_s,
                       threads, 0, as_stream(stream)>>>(
       lse, l_stride_s, l_stride_h, perm, n_tiles * kTile, heads, n_heads, out);
   return check_launch("gather_lse_kernel");
+}
+
+extern "C" int veda_head_blocks(const void* src, void* dst, int64_t rows,
+                                int32_t blocks, int64_t seg_bytes,
+                                int64_t row_bytes, int64_t block_bytes,
+                                int64_t offset_bytes, int32_t pack,
+                                void* stream) {
+  VEDA_REQUIRE(src != nullptr && dst != nullptr && src != dst,
+               "src and dst must be distinct buffers");
+  VEDA_REQUIRE(rows >= 0 && blocks >= 1 && seg_bytes >= 16,
+               "bad shape");
+  VEDA_REQUIRE(seg_bytes % 16 == 0 && row_bytes % 16 == 0 &&
+                   block_bytes % 16 == 0 && offset_bytes % 16 == 0,
+               "sizes and offsets must be multiples of 16 bytes");
+  VEDA_REQUIRE(offset_bytes >= 0 && offset_bytes + seg_bytes <= block_bytes &&
+                   static_cast<int64_t>(blocks) * block_bytes <= row_bytes,
+               "segments must lie inside their blocks and rows");
+  VEDA_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dst) % 16 == 0,
+               "src and dst must be 16-byte aligned");
+  const int64_t total = rows * blocks * (seg_bytes / 16);
+  if (total == 0) return VEDA_OK;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;
+  head_blocks_kernel<<<static_cast<unsigned>(want < cap ? want : cap),
+                       threads, 0, as_stream(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), rows, blocks,
+      seg_bytes / 16, row_bytes / 16, block_bytes / 16, offset_bytes / 16,
+      pack);
+  return check_launch("head_blocks_kernel");
 }

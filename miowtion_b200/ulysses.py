@@ -53,13 +53,36 @@ def piece_bounds(local_heads: int, pieces: int) -> list[tuple[int, int]]:
             for a in range(0, local_heads, size)]
 
 
+def _head_blocks(src: torch.Tensor, dst: torch.Tensor, world: int,
+                 start: int, stop: int, pack: bool) -> None:
+    """veda_head_blocks between a [S/P, H, D] tensor (strided side) and a
+    [P, S/P, c, D] one (packed side), for heads p * H/P + [start, stop)."""
+    strided = src if pack else dst
+    rows, heads, dim = strided.shape
+    per = heads // world
+    size = strided.element_size()
+    if not (strided.is_cuda and strided.is_contiguous()
+            and (dst if pack else src).is_contiguous()):
+        raise ValueError('the exchange buffers must be contiguous CUDA '
+                         'tensors')
+    _lib.call('veda_head_blocks', src.data_ptr(), dst.data_ptr(), rows,
+              world, (stop - start) * dim * size, heads * dim * size,
+              per * dim * size, start * dim * size, 1 if pack else 0,
+              _lib.stream_ptr(strided.device))
+
+
 def _pack(x: torch.Tensor, world: int, start: int, stop: int) -> torch.Tensor:
     """[S/P, H, D] -> [P, S/P, c, D]: chunk p holds heads
     p * H/P + [start, stop)."""
     rows, heads, dim = x.shape
-    per = heads // world
-    return x.view(rows, world, per, dim)[:, :, start:stop].transpose(
-        0, 1).contiguous()
+    if not x.is_cuda:
+        per = heads // world
+        return x.view(rows, world, per, dim)[:, :, start:stop].transpose(
+            0, 1).contiguous()
+    out = torch.empty(world, rows, stop - start, dim, dtype=x.dtype,
+                      device=x.device)
+    _head_blocks(x.contiguous(), out, world, start, stop, pack=True)
+    return out
 
 
 def seq_to_heads(x: torch.Tensor, group=None) -> torch.Tensor:
@@ -83,8 +106,13 @@ def heads_to_seq(y: torch.Tensor, group=None) -> torch.Tensor:
     send = y.view(world, seq // world, local_heads, dim)
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send.contiguous(), group=group)
-    return recv.transpose(0, 1).reshape(seq // world, world * local_heads,
-                                        dim)
+    if not recv.is_cuda:
+        return recv.transpose(0, 1).reshape(seq // world,
+                                            world * local_heads, dim)
+    out = torch.empty(seq // world, world * local_heads, dim, dtype=y.dtype,
+                      device=y.device)
+    _head_blocks(recv, out, world, 0, local_heads, pack=False)
+    return out
 
 
 class UlyssesSparseStudent:
@@ -192,6 +220,9 @@ class UlyssesSparseStudent:
             outputs.append((start, stop, back, result, work))
         for start, stop, back, _result, work in outputs:
             work.wait()
-            out.view(rows, world, per, dim)[:, :, start:stop] = back.transpose(
-                0, 1)
+            if out.is_cuda:
+                _head_blocks(back, out, world, start, stop, pack=False)
+            else:
+                out.view(rows, world, per, dim)[:, :, start:stop] = (
+                    back.transpose(0, 1))
         return out

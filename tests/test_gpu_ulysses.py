@@ -62,3 +62,22 @@ def test_pieced_layer_equals_plain_student(one_rank_group, pieces):
         got = ulysses.UlyssesSparseStudent(student, pieces=pieces)(q, k, v, 0)
     torch.cuda.synchronize()
     assert torch.equal(got[:used], want[:used])
+
+
+@pytest.mark.parametrize('world,start,stop', [(2, 0, 24), (8, 0, 6),
+                                              (4, 3, 9)])
+def test_head_blocks_pack_and_unpack_are_exact(world, start, stop):
+    rows, heads = 1000, 48
+    per = heads // world
+    gen = torch.Generator().manual_seed(world)
+    x = torch.randn(rows, heads, 128, generator=gen).to(DEV, torch.bfloat16)
+    packed = ulysses._pack(x, world, start, stop)  # pylint: disable=protected-access
+    want = x.view(rows, world, per, 128)[:, :, start:stop].transpose(0, 1)
+    assert torch.equal(packed, want)
+    back = torch.zeros_like(x)
+    ulysses._head_blocks(packed, back, world, start, stop, pack=False)  # pylint: disable=protected-access
+    mask = torch.zeros(heads, dtype=torch.bool)
+    for p in range(world):
+        mask[p * per + start:p * per + stop] = True
+    assert torch.equal(back[:, mask.to(DEV)], x[:, mask.to(DEV)])
+    assert (back[:, ~mask.to(DEV)] == 0).all()
