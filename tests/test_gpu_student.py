@@ -205,3 +205,36 @@ def test_dense_attention_fn_matches_oracle():
     with pytest.raises(ValueError):
         veda_attention.dense_attention(q.to(DEV), k.to(DEV), v.to(DEV),
                                        spec['used'], backend='nope')
+
+
+def test_head_chunks_are_exact():
+    """A group processed one head at a time (collect_bytes below one head's
+    copy, attention.py:204-206) gives the same bits as one launch per group
+    (heads are independent in every kernel); the reference's head-chunking
+    test is tests/unit/test_veda_heatmap_attention.py:175-235."""
+    text, grid = 300, (8, 12, 20)
+    used = text + grid[0] * grid[1] * grid[2]
+    seq_len = used + 40
+    heads = 4
+    q, k, v = (t.to(DEV) for t in inputs.qkv(seq_len, heads, 128, 27,
+                                             torch.bfloat16))
+    w = inputs.predictor_weights(heads, 128, 127, 0.02)
+    outs = []
+    for collect in (veda_attention.DEFAULT_COLLECT_BYTES, 1):
+        layout = veda_attention.PackedLayout(
+            seq_len, used, (veda_attention.VideoSpan(text, grid),))
+        config = veda_attention.VedaConfig(
+            target_budget=veda_mask.Budget(ratio=0.3), collect_bytes=collect)
+        clip = veda_attention.ClipTiling(layout, config, torch.device(DEV))
+        plan = veda_plan.TilePlan('chunks', grid,
+                                  [tiling.TileShape(2, 8, 8),
+                                   tiling.TileShape(1, 8, 16)], [[0, 1, 1, 0]])
+        pred = veda_predictor.TileScorePredictor(1, heads, 128)
+        with torch.no_grad():
+            pred.layers[0].proj_q.copy_(w[0])
+            pred.layers[0].proj_k.copy_(w[1])
+        student = veda_attention.SparseStudent(clip, plan, pred.to(DEV))
+        with torch.no_grad():
+            outs.append(student(q, k, v, 0))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])

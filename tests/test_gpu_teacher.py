@@ -109,3 +109,36 @@ def test_teacher_collector_refuses_ablation_losses():
     with pytest.raises(NotImplementedError, match='ablation'):
         veda_attention.TeacherCollector(clip, plan, predictor,
                                         torch.Generator(), 1.0)
+
+
+def test_teacher_output_is_the_dense_attention_and_trains_only_the_predictor():
+    """The collector's output is the dense teacher's, bit for bit, and its
+    backward reaches only the predictor (the reference's
+    tests/unit/test_veda_heatmap_attention.py:108-137)."""
+    spec = inputs.TEACHER
+    text, grid, seq_len = spec['text'], spec['grid'], spec['seq_len']
+    used = text + grid[0] * grid[1] * grid[2]
+    q, k, v = (t.to(DEV).requires_grad_(True)
+               for t in inputs.qkv(seq_len, spec['heads'], spec['dim'],
+                                   spec['seed'], torch.bfloat16))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=spec['ratio']))
+    layout = veda_attention.PackedLayout(
+        seq_len, used, (veda_attention.VideoSpan(text, grid),))
+    clip = veda_attention.ClipTiling(layout, config, DEV)
+    plan = veda_plan.TilePlan(
+        'teacher', grid, [tiling.TileShape(*s) for s in spec['shapes']],
+        [spec['head_shape']])
+    predictor = veda_predictor.TileScorePredictor(1, spec['heads'],
+                                                  spec['dim']).to(DEV)
+    teacher = veda_attention.TeacherCollector(
+        clip, plan, predictor, torch.Generator().manual_seed(3), 1.0)
+    out = teacher(q, k, v, 0)
+    want = veda_attention.dense_attention(q.detach(), k.detach(), v.detach(),
+                                          used)[0]
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert q.grad is None and k.grad is None and v.grad is None
+    for layer in predictor.layers:
+        assert layer.proj_q.grad is not None and layer.proj_k.grad is not None
+        assert layer.proj_q.grad.abs().sum() > 0
