@@ -46,8 +46,8 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
 
   // Two buffers: chunk c + 1 is loaded into registers while chunk c is
   // multiplied from shared memory.
-  __shared__ float a_s[2][kEmbK][kEmbRows + 4];  // transposed feats chunk
-  __shared__ float b_s[2][kEmbK][kHeadDim];
+  __shared__ __align__(16) float a_s[2][kEmbK][kEmbRows + 4];  // transposed feats chunk
+  __shared__ __align__(16) float b_s[2][kEmbK][kHeadDim];
   const int tid = threadIdx.x;
   const int tr = tid / 32;  // rows tr*8 .. +8
   const int tc = tid % 32;  // cols tc*4 .. +4
@@ -80,11 +80,13 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
       b_s[buf][e / kHeadDim][e % kHeadDim] = rb[i];
     }
   };
-  float acc[8][4];
+  // Column pairs accumulate with packed fp32x2 FMAs (two independent fp32
+  // FMAs per instruction, rounded as fmaf rounds).
+  float2 acc[8][2];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 2; ++j) acc[i][j] = make_float2(0.f, 0.f);
 
   fetch(0);
   constexpr int kChunks = kFeat / kEmbK;
@@ -95,15 +97,17 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
     if (c + 1 < kChunks) fetch((c + 1) * kEmbK);
 #pragma unroll 8
     for (int k = 0; k < kEmbK; ++k) {
-      float a[8], b[4];
+      float a[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] = a_s[buf][k][tr * 8 + i];
+      const float4 b4 = *reinterpret_cast<const float4*>(&b_s[buf][k][tc * 4]);
+      const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = b_s[buf][k][tc * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+      for (int i = 0; i < 8; ++i) {
+        const float2 ai = make_float2(a[i], a[i]);
+        acc[i][0] = __ffma2_rn(ai, b01, acc[i][0]);
+        acc[i][1] = __ffma2_rn(ai, b23, acc[i][1]);
+      }
     }
     // The next stash writes the other buffer; the one after writes this
     // buffer again, behind the next iteration's barrier.
@@ -115,7 +119,8 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int c = tc * 4 + j;
-      out[row * kHeadDim + c] = acc[i][j] + feats[row * kFeat + c];
+      const float v = (j & 1) ? acc[i][j >> 1].y : acc[i][j >> 1].x;
+      out[row * kHeadDim + c] = v + feats[row * kFeat + c];
     }
   }
 }
@@ -132,15 +137,15 @@ __global__ void __launch_bounds__(256)
   const float* kh = k_hat + static_cast<int64_t>(h) * n_k * kHeadDim;
   // Two buffers: chunk c + 1 is loaded into registers while chunk c is
   // multiplied from shared memory.
-  __shared__ float q_s[2][32][64 + 4];
-  __shared__ float k_s[2][32][64 + 4];
+  __shared__ __align__(16) float q_s[2][32][64 + 4];
+  __shared__ __align__(16) float k_s[2][32][64 + 4];
   const int tid = threadIdx.x;
   const int ti = tid / 16, tj = tid % 16;
-  float acc[4][4];
+  float2 acc[4][2];  // column pairs, packed fp32x2 FMAs
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
   float rq[8], rk[8];
   auto fetch = [&](int d0) {
 #pragma unroll
@@ -164,16 +169,16 @@ __global__ void __launch_bounds__(256)
     if (c + 1 < kHeadDim / 32) fetch((c + 1) * 32);
 #pragma unroll 8
     for (int d = 0; d < 32; ++d) {
-      float a[4], b[4];
+      const float4 a4 = *reinterpret_cast<const float4*>(&q_s[buf][d][ti * 4]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&k_s[buf][d][tj * 4]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
 #pragma unroll
       for (int x = 0; x < 4; ++x) {
-        a[x] = q_s[buf][d][ti * 4 + x];
-        b[x] = k_s[buf][d][tj * 4 + x];
+        const float2 ax = make_float2(a[x], a[x]);
+        acc[x][0] = __ffma2_rn(ax, b01, acc[x][0]);
+        acc[x][1] = __ffma2_rn(ax, b23, acc[x][1]);
       }
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-#pragma unroll
-        for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(a[x], b[y], acc[x][y]);
     }
   }
   float* out = logits + static_cast<int64_t>(h) * n_q * n_k;
@@ -185,7 +190,8 @@ __global__ void __launch_bounds__(256)
     for (int y = 0; y < 4; ++y) {
       const int64_t j = j0 + tj * 4 + y;
       // Divided, not multiplied by the reciprocal, as the reference does.
-      if (j < n_k) out[i * n_k + j] = __fdiv_rn(acc[x][y], sqrt_d);
+      const float v = (y & 1) ? acc[x][y >> 1].y : acc[x][y >> 1].x;
+      if (j < n_k) out[i * n_k + j] = __fdiv_rn(v, sqrt_d);
     }
   }
 }
