@@ -83,6 +83,22 @@ __device__ uint32_t kth_largest(const uint32_t* keys, int n, int k,
   return t;
 }
 
+// The same with this lane's keys (columns lane + 32 j, j < kPerLane) held
+// in registers: the 32 passes read no shared memory. Absent columns hold 0,
+// below every real key (order_key(-inf) > 0), so they never count.
+template <int kPerLane>
+__device__ uint32_t kth_largest_reg(const uint32_t (&kr)[kPerLane], int k) {
+  uint32_t t = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = t | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) c += kr[j] >= cand;
+    if (__reduce_add_sync(0xffffffffu, c) >= k) t = cand;
+  }
+  return t;
+}
+
 // Marks in `member` (one byte per column of the block) the `take` largest
 // keys, ties to the lowest column. keys > thr are all members, then the
 // first (take - #greater) columns with key == thr.
@@ -154,6 +170,9 @@ __device__ void write_lists(const uint8_t* member, const int32_t* valid_count,
   }
 }
 
+// kRegKeys: keys per lane kept in registers for the radix select (blocks of
+// up to 32 * kRegKeys columns; wider blocks select from shared memory).
+template <int kRegKeys>
 __global__ void __launch_bounds__(kSelectWarps * 32)
     select_kernel(SelectParams p) {
   extern __shared__ uint8_t sel_smem[];
@@ -194,6 +213,10 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
         sel_off += w;
         continue;
       }
+      // The keys also stay in registers when the block is narrow enough.
+      uint32_t kr[kRegKeys];
+#pragma unroll
+      for (int j = 0; j < kRegKeys; ++j) kr[j] = 0u;
       for (int c = lane; c < w; c += 32) {
         const int col = blk.start + c;
         float v = srow[col];
@@ -201,10 +224,17 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
         if (col == t) v = INFINITY;  // own tile, only inside its block
         keys[c] = order_key(v);
       }
+      if (w <= 32 * kRegKeys) {
+#pragma unroll
+        for (int j = 0; j < kRegKeys; ++j)
+          if (lane + 32 * j < w) kr[j] = keys[lane + 32 * j];
+      }
       __syncwarp();
       int allowed = blk.k_lo + (extra_row(t, blk.frac) ? 1 : 0);
       allowed = min(allowed, blk.k_hi);
-      const uint32_t thr = kth_largest(keys, w, allowed, lane);
+      const uint32_t thr = w <= 32 * kRegKeys
+                               ? kth_largest_reg<kRegKeys>(kr, allowed)
+                               : kth_largest(keys, w, allowed, lane);
       // -inf columns are never kept (mask.py:281-282).
       mark_top(keys, w, thr, allowed, thr == kNegInfKey, member + blk.start,
                lane);
@@ -395,13 +425,18 @@ extern "C" int veda_block_select(
   if (items == 0) return VEDA_OK;
   const int stride = static_cast<int>(n_tiles * 4 + ((n_tiles + 15) & ~15));
   const int smem = kSelectWarps * stride;
-  if (smem > 48 * 1024)
-    VEDA_CUDA(cudaFuncSetAttribute(
-        select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  select_kernel<<<static_cast<unsigned>((items + kSelectWarps - 1) /
-                                        kSelectWarps),
-                  kSelectWarps * 32, smem, as_stream(stream)>>>(p);
-  return check_launch("select_kernel");
+  const unsigned grid =
+      static_cast<unsigned>((items + kSelectWarps - 1) / kSelectWarps);
+  auto launch = [&](auto kernel) -> int {
+    if (smem > 48 * 1024)
+      VEDA_CUDA(cudaFuncSetAttribute(
+          kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<grid, kSelectWarps * 32, smem, as_stream(stream)>>>(p);
+    return check_launch("select_kernel");
+  };
+  if (n_video <= 256) return launch(select_kernel<8>);
+  if (n_video <= 512) return launch(select_kernel<16>);
+  return launch(select_kernel<32>);
 }
 
 extern "C" int veda_index_lists(const uint8_t* mask, int32_t n_heads,
