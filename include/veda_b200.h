@@ -272,6 +272,11 @@ int veda_bsa_fwd(const void* q, int64_t q_stride_n, int64_t q_stride_h,
  *   are those of the tile order);
  *   out [S, H, D] (strides out_stride_s, out_stride_h): the rows
  *   box_perm >= 0 of heads[] are written, nothing else.
+ * item_order (device int32, NULL for the default order): a work order of
+ * order_slots = rounds x order_ctas slots, each h * n_tiles + qt or -1;
+ * the kernel then runs order_ctas CTAs, CTA c taking slots c,
+ * c + order_ctas, ... (every item exactly once; the order only balances
+ * the CTAs' work, the results do not depend on it).
  * Rows of a partial video tile sit in box order rather than as a prefix;
  * the masked softmax is the same, so only the fp32 summation order differs
  * from veda_bsa_fwd. */
@@ -289,7 +294,9 @@ int veda_bsa_fwd_packed(const void* q, const void* k, const void* v,
                         const int32_t* part_idx, const int32_t* full_cnt,
                         const int32_t* full_idx, int64_t ld_idx, void* out,
                         int64_t out_stride_s, int64_t out_stride_h,
-                        float softmax_scale, void* stream);
+                        float softmax_scale, const int32_t* item_order,
+                        int32_t order_ctas, int64_t order_slots,
+                        void* stream);
 
 /* Replaces miowtion/kernels/fa4.py:185-205 (dense_attention) and the
  * row-subset contract of miowtion/h3/attention.py:28-102: full attention of

@@ -88,7 +88,7 @@ SIGNATURES = {
                                     c_i32, c_i64, c_i64, c_ptr, c_i32, c_ptr,
                                     c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                                     c_i64, c_ptr, c_i64, c_i64, c_f32,
-                                    c_ptr]),
+                                    c_ptr, c_i32, c_i64, c_ptr]),
     'veda_dense_fwd': (c_i32, [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64,
                                c_i64, c_i32, c_ptr, c_i64, c_i64, c_ptr,
                                c_i64, c_i64, c_f32, c_ptr]),

@@ -495,9 +495,12 @@ class SparseStudent:
                 self.clip.blocks(tile_layout))
             ev.stop(t)
         t = ev.start('attention')
-        kernels.block_sparse_attention_packed(q, k_img, v_img, lists,
-                                              tile_layout, heads, out,
-                                              kv_tiles='images')
+        kernels.block_sparse_attention_packed(
+            q, k_img, v_img, lists, tile_layout, heads, out,
+            kv_tiles='images',
+            order=kernels.work_order(tile_layout, heads.numel(),
+                                     self.clip.blocks(tile_layout),
+                                     q.device))
         ev.stop(t)
         self.last_lists = lists
 

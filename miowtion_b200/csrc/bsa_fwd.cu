@@ -107,6 +107,14 @@ struct FwdParams {
   int n_q_tiles;
   int n_kv_tiles;
   int n_items;
+  // Optional work order: CTA c walks slots c, c + G, c + 2G, ... of
+  // item_order ([n_slots / G][G], G = the grid), each slot an item
+  // h * n_q_tiles + qt or -1 for none. Without it a CTA walks items c,
+  // c + G, ... with each head's query tiles in reverse (the dense global
+  // rows first).
+  const int32_t* item_order;
+  int n_slots;
+  int order_ctas;    // G, the grid a work order is laid out for
   const int32_t* valid_count;
   const int32_t* part_cnt;
   const int32_t* part_idx;
@@ -233,32 +241,50 @@ struct Stream {
   // latency overlaps the current item.
   int npc, nfc;
 
-  __device__ void fetch(const FwdParams& p, int item) {
+  bool pad;  // the slot holds no item (work order padding)
+
+  // Row (h * n_q_tiles + qt) of slot `slot`, or -1.
+  __device__ int64_t row_of(const FwdParams& p, int slot) const {
+    if (p.item_order != nullptr) return p.item_order[slot];
+    // Heaviest query tiles (the dense global rows, last in tile order)
+    // first.
+    return static_cast<int64_t>(slot / p.n_q_tiles) * p.n_q_tiles +
+           (p.n_q_tiles - 1 - slot % p.n_q_tiles);
+  }
+
+  __device__ void fetch(const FwdParams& p, int slot) {
     npc = 0;
     nfc = 0;
-    if (item >= p.n_items) return;
+    if (slot >= p.n_slots) return;
+    const int64_t row = row_of(p, slot);
+    if (row < 0) return;
     if (p.dense) {
       nfc = p.n_kv_tiles;
       return;
     }
-    const int64_t row = static_cast<int64_t>(item / p.n_q_tiles) *
-                            p.n_q_tiles +
-                        (p.n_q_tiles - 1 - item % p.n_q_tiles);
     npc = p.part_cnt[row];
     nfc = p.full_cnt[row];
   }
 
   __device__ void load_item(const FwdParams& p) {
-    h = it / p.n_q_tiles;
-    // Heaviest query tiles (the dense global rows, last in tile order) first.
-    qt = p.n_q_tiles - 1 - it % p.n_q_tiles;
-    off = p.dense ? 0
-                  : (static_cast<int64_t>(h) * p.n_q_tiles + qt) * p.ld_idx;
+    const int64_t row = row_of(p, it);
+    pad = row < 0;
+    h = pad ? 0 : static_cast<int>(row / p.n_q_tiles);
+    qt = pad ? 0 : static_cast<int>(row % p.n_q_tiles);
+    off = p.dense ? 0 : (pad ? 0 : row * p.ld_idx);
     pc = npc;
     fc = nfc;
     len = pc + fc;
     j = 0;
     fetch(p, it + stride);
+  }
+
+  // Moves past padding slots (never items, not even empty ones).
+  __device__ void skip_pads(const FwdParams& p) {
+    while (it < p.n_slots && pad) {
+      it += stride;
+      if (it < p.n_slots) load_item(p);
+    }
   }
 
   // Positions on the first item (on the first non-empty one unless
@@ -269,34 +295,38 @@ struct Stream {
     stride = step;
     blk = 0;
     ka = -1;
-    if (it < p.n_items) {
+    pad = false;
+    if (it < p.n_slots) {
       fetch(p, it);
       load_item(p);
-      if (len > 0) ka = 0;
+      skip_pads(p);
+      if (it < p.n_slots && len > 0) ka = 0;
       if (!keep_empty) skip_empty(p);
     }
   }
 
   __device__ void skip_empty(const FwdParams& p) {
-    while (it < p.n_items && len == 0) {
+    while (it < p.n_slots && len == 0) {
       it += stride;
-      if (it < p.n_items) {
+      if (it < p.n_slots) {
         load_item(p);
-        if (len > 0) ++ka;
+        skip_pads(p);
+        if (it < p.n_slots && len > 0) ++ka;
       }
     }
   }
 
   __device__ void next_item(const FwdParams& p, bool keep_empty) {
     it += stride;
-    if (it < p.n_items) {
+    if (it < p.n_slots) {
       load_item(p);
-      if (len > 0) ++ka;
+      skip_pads(p);
+      if (it < p.n_slots && len > 0) ++ka;
       if (!keep_empty) skip_empty(p);
     }
   }
 
-  __device__ bool valid(const FwdParams& p) const { return it < p.n_items; }
+  __device__ bool valid(const FwdParams& p) const { return it < p.n_slots; }
 
   // The current block without its key tile (no memory access).
   __device__ Block flags() const {
@@ -1019,7 +1049,14 @@ int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
   if (p.n_items == 0) return VEDA_OK;
   // SMs left free for kernels that overlap this one (collectives).
   const int cap = sms - sm_reserve() > 0 ? sms - sm_reserve() : 1;
-  const int grid = p.n_items < cap ? p.n_items : cap;
+  int grid = p.n_items < cap ? p.n_items : cap;
+  if (p.item_order != nullptr) {
+    // A work order is laid out for its own number of CTAs.
+    grid = p.order_ctas;
+    if (grid > sms)
+      return set_error(VEDA_ERR_INVALID, "the work order has more CTAs than "
+                                         "the device has SMs");
+  }
   bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(maps, p);
   return check_launch("bsa_fwd_kernel");
 }
@@ -1071,6 +1108,7 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
   p.n_q_tiles = static_cast<int>(n_q_tiles);
   p.n_kv_tiles = static_cast<int>(n_kv_tiles);
   p.n_items = static_cast<int>(n_q_tiles * n_heads);
+  p.n_slots = p.n_items;
   p.valid_count = valid_count;
   p.part_cnt = part_cnt;
   p.part_idx = part_idx;
@@ -1136,6 +1174,7 @@ extern "C" int veda_bsa_fwd_heat(
   p.n_q_tiles = static_cast<int>(n_tiles);
   p.n_kv_tiles = static_cast<int>(n_tiles);
   p.n_items = static_cast<int>(n_tiles * n_heads);
+  p.n_slots = p.n_items;
   p.valid_count = valid_count;
   p.part_cnt = part_cnt;
   p.part_idx = part_idx;
@@ -1199,6 +1238,7 @@ extern "C" int veda_dense_fwd(const void* q, const void* k, const void* v,
   p.n_q_tiles = static_cast<int>(tiles);
   p.n_kv_tiles = static_cast<int>(tiles);
   p.n_items = static_cast<int>(tiles * n_heads);
+  p.n_slots = p.n_items;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_n = out_stride_s;
   p.out_stride_h = out_stride_h;
@@ -1223,7 +1263,8 @@ extern "C" int veda_bsa_fwd_packed(
     const int32_t* valid_count, const int32_t* part_cnt,
     const int32_t* part_idx, const int32_t* full_cnt,
     const int32_t* full_idx, int64_t ld_idx, void* out, int64_t out_stride_s,
-    int64_t out_stride_h, float softmax_scale, void* stream) {
+    int64_t out_stride_h, float softmax_scale, const int32_t* item_order,
+    int32_t order_ctas, int64_t order_slots, void* stream) {
   int rc = require_sm100("veda_bsa_fwd_packed");
   if (rc != VEDA_OK) return rc;
   VEDA_REQUIRE(q && k && v && out && heads && box_perm && part_cnt &&
@@ -1312,6 +1353,7 @@ extern "C" int veda_bsa_fwd_packed(
   p.n_q_tiles = static_cast<int>(n_tiles);
   p.n_kv_tiles = static_cast<int>(n_tiles);
   p.n_items = static_cast<int>(n_tiles * n_heads);
+  p.n_slots = p.n_items;
   p.valid_count = kv_tile_order ? valid_count : nullptr;
   p.part_cnt = part_cnt;
   p.part_idx = part_idx;
@@ -1325,6 +1367,15 @@ extern "C" int veda_bsa_fwd_packed(
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.dense = 0;
   p.used = 0;
+  if (item_order != nullptr) {
+    VEDA_REQUIRE(order_ctas >= 1 && order_slots >= order_ctas &&
+                     order_slots % order_ctas == 0 &&
+                     order_slots < (int64_t(1) << 31),
+                 "the work order must be [rounds, order_ctas] slots");
+    p.item_order = item_order;
+    p.order_ctas = order_ctas;
+    p.n_slots = static_cast<int>(order_slots);
+  }
   p.packed = 1;
   p.box_kv = kv_tile_order ? 0 : 1;
   p.total_heads = total_heads;

@@ -171,19 +171,76 @@ def packed_supported(layout: tiling.TileLayout) -> bool:
     return 1 <= len(layout.spans) <= PACKED_MAX_SPANS
 
 
+def work_order(layout: tiling.TileLayout, n_heads: int,
+               blocks: list[veda_mask.ColumnBlock],
+               device: torch.device) -> torch.Tensor | None:
+    """A balanced work order for the forward over the selection lists of
+    `blocks` (cached on the layout), or None where the default order is
+    balanced already (no global query rows, or fewer items than SMs).
+
+    A global (text) query row keeps every non-empty key tile, about ten
+    times a video row's budget, so striding items over the CTAs in order
+    leaves some CTAs with two of them: 5 % above the mean at config 3 on
+    one GPU, 18 % with six heads per GPU. Here the global rows are dealt
+    first, then the video rows head by head, each to the CTA with the
+    least work so far (heads stay together in time, so their key tiles
+    stay in L2). Layout [rounds, G] int32, slot h * n_tiles + qt or -1.
+    """
+    n_global = layout.n_global_tiles
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    n_items = n_heads * layout.n_tiles
+    if n_global == 0 or n_items <= sms:
+        return None
+    key = (n_heads, sms, tuple((b.start, b.stop, b.budget, b.real_tokens)
+                               for b in blocks))
+    cache = layout.work_orders
+    if key in cache:
+        return cache[key]
+    import heapq  # pylint: disable=import-outside-toplevel
+    valid = layout.valid_count.cpu().tolist()
+    n_video = layout.n_video_tiles
+    live_global_cols = sum(1 for c in range(n_video, layout.n_tiles)
+                           if valid[c] > 0)
+    per_row = 0.0
+    for arr in veda_mask.resolve_blocks(blocks):
+        per_row += (arr.k_lo + arr.frac) if not arr.keeps_all else arr.k_lo
+    video_weight = per_row + live_global_cols
+    global_weight = float(sum(1 for v in valid if v > 0))
+    heavy = [(h, qt) for h in range(n_heads)
+             for qt in range(layout.n_tiles - 1, n_video - 1, -1)]
+    light = [(h, qt) for h in range(n_heads)
+             for qt in range(n_video - 1, -1, -1)]
+    loads = [(0.0, c) for c in range(sms)]
+    lists = [[] for _ in range(sms)]
+    for items, weight in ((heavy, global_weight), (light, video_weight)):
+        for h, qt in items:
+            load, c = heapq.heappop(loads)
+            lists[c].append(h * layout.n_tiles + qt)
+            heapq.heappush(loads, (load + weight, c))
+    rounds = max(len(x) for x in lists)
+    order = torch.full((rounds, sms), -1, dtype=torch.int32)
+    for c, items in enumerate(lists):
+        order[:len(items), c] = torch.tensor(items, dtype=torch.int32)
+    order = order.to(device)
+    cache[key] = order
+    return order
+
+
 def block_sparse_attention_packed(q: torch.Tensor, k: torch.Tensor,
                                   v: torch.Tensor,
                                   lists: veda_mask.BlockLists,
                                   layout: tiling.TileLayout,
                                   heads: torch.Tensor,
                                   out: torch.Tensor,
-                                  kv_tiles: bool = False) -> None:
+                                  kv_tiles: bool = False,
+                                  order: torch.Tensor | None = None) -> None:
     """Forward of the heads `heads` of one tile layout, with the queries
     read from and the output written to the packed tensors in place:
     q [S, H, D] -> rows [0, used) of out [S, H, D] for those heads. Equals
     `gather_tiles`, then `block_sparse_attention_lists` over all query
     tiles, then `scatter_rows_` (veda/attention.py:724-743), in one kernel
-    without the tile-ordered q or output. k and v are the group's
+    without the tile-ordered q or output. `order` (see `work_order`) only
+    balances the CTAs' work. k and v are the group's
     tile-ordered copies [N, H', D] with `kv_tiles` (as `gather_and_pool`
     writes them), else packed [S, H, D] like q and read in place too."""
     _require(q, 'block_sparse_attention')
@@ -240,6 +297,8 @@ def block_sparse_attention_packed(q: torch.Tensor, k: torch.Tensor,
               lists.full_cnt.data_ptr(), lists.full_idx.data_ptr(),
               lists.part_idx.shape[-1], out.data_ptr(), out.stride(0),
               out.stride(1), 1.0 / math.sqrt(q.shape[-1]),
+              _lib.ptr(order), order.shape[1] if order is not None else 0,
+              order.numel() if order is not None else 0,
               _lib.stream_ptr(q.device))
 
 

@@ -131,6 +131,8 @@ class TileLayout:
     spans: tuple = ()
     box_perm: torch.Tensor | None = None
     key_mask: torch.Tensor | None = None
+    # Balanced forward work orders, built once per (heads, SMs, budgets).
+    work_orders: dict = dataclasses.field(default_factory=dict)
 
     @property
     def n_tiles(self) -> int:

@@ -227,3 +227,43 @@ def test_sm_reserve_changes_the_grid_not_the_result():
     _lib.call('veda_set_sm_reserve', 0)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+def test_work_order_covers_every_item_and_keeps_the_bits():
+    """The balanced work order (global query rows dealt first, then video
+    rows to the least-loaded CTA) holds every (head, query tile) once, and
+    the forward's output does not depend on it."""
+    from miowtion_b200 import mask as veda_mask
+    spec = inputs.BENCH_LAYOUTS['cfg3_a']
+    lay = tiling.build_tile_layout(spans_of(spec), spec['used'],
+                                   spec['seq_len'], DEV)
+    heads = 2
+    blocks = veda_mask.column_blocks(lay, veda_mask.Budget(ratio=0.1))
+    order = kernels.work_order(lay, heads, blocks, torch.device(DEV))
+    assert order is not None and order.dtype == torch.int32
+    items = order[order >= 0].cpu().numpy()
+    assert sorted(items.tolist()) == list(range(heads * lay.n_tiles))
+    # Every CTA starts with at most one global query row's worth of work
+    # more than the others: the global rows go to different CTAs first.
+    first = order[0].cpu().numpy()
+    assert ((first % lay.n_tiles) >= lay.n_video_tiles).sum() == min(
+        order.shape[1], heads * lay.n_global_tiles)
+    assert kernels.work_order(lay, heads, blocks, torch.device(DEV)) is order
+    q, k, v = (t.to(DEV) for t in inputs.qkv(spec['seq_len'], heads, 128,
+                                             64, torch.bfloat16))
+    hd = torch.arange(heads, device=DEV)
+    n = lay.n_tiles
+    gen = torch.Generator().manual_seed(16)
+    mask = torch.rand(heads, n, n, generator=gen) < 0.08
+    mask[:, torch.arange(n), torch.arange(n)] = True
+    mask[:, lay.n_video_tiles:, :] = True
+    lists = _lists(mask, lay)
+    ki, vi = (tiling.gather_images(t, lay, hd) for t in (k, v))
+    outs = []
+    for o in (None, order):
+        out = torch.zeros_like(q)
+        kernels.block_sparse_attention_packed(q, ki, vi, lists, lay, hd, out,
+                                              kv_tiles='images', order=o)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
