@@ -13,6 +13,7 @@ built library every entry point raises.
 
 from __future__ import annotations
 
+import heapq
 import math
 import threading
 
@@ -196,7 +197,6 @@ def work_order(layout: tiling.TileLayout, n_heads: int,
     cache = layout.work_orders
     if key in cache:
         return cache[key]
-    import heapq  # pylint: disable=import-outside-toplevel
     valid = layout.valid_count.cpu().tolist()
     n_video = layout.n_video_tiles
     live_global_cols = sum(1 for c in range(n_video, layout.n_tiles)
