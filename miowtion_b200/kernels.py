@@ -172,6 +172,17 @@ def packed_supported(layout: tiling.TileLayout) -> bool:
     return 1 <= len(layout.spans) <= PACKED_MAX_SPANS
 
 
+_SM_RESERVE = 0
+
+
+def set_sm_reserve(n: int) -> None:
+    """veda_set_sm_reserve: leave `n` SMs free of the attention forward
+    (for kernels that overlap it, such as NCCL collectives)."""
+    global _SM_RESERVE
+    _lib.call('veda_set_sm_reserve', n)
+    _SM_RESERVE = n
+
+
 def work_order(layout: tiling.TileLayout, n_heads: int,
                blocks: list[veda_mask.ColumnBlock],
                device: torch.device) -> torch.Tensor | None:
@@ -188,7 +199,8 @@ def work_order(layout: tiling.TileLayout, n_heads: int,
     stay in L2). Layout [rounds, G] int32, slot h * n_tiles + qt or -1.
     """
     n_global = layout.n_global_tiles
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    sms = max(1, torch.cuda.get_device_properties(device).multi_processor_count
+              - _SM_RESERVE)
     n_items = n_heads * layout.n_tiles
     if n_global == 0 or n_items <= sms:
         return None

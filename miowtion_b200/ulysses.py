@@ -29,6 +29,7 @@ import torch.distributed as dist
 
 from miowtion_b200 import _lib
 from miowtion_b200 import attention as veda_attention
+from miowtion_b200 import kernels
 from miowtion_b200 import plan as veda_plan
 
 
@@ -172,12 +173,12 @@ class UlyssesSparseStudent:
         reserve = self.reserve_sms if (world > 1 and len(bounds) > 1
                                        and self.piece_factory is None) else 0
         if reserve:
-            _lib.call('veda_set_sm_reserve', reserve)
+            kernels.set_sm_reserve(reserve)
         try:
             return self._run(q, k, v, layer_index, world, rank, per, bounds)
         finally:
             if reserve:
-                _lib.call('veda_set_sm_reserve', 0)
+                kernels.set_sm_reserve(0)
 
     def _run(self, q, k, v, layer_index, world, rank, per, bounds):
         rows, _, dim = q.shape
