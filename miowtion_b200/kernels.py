@@ -218,23 +218,36 @@ def work_order(layout: tiling.TileLayout, n_heads: int,
         per_row += (arr.k_lo + arr.frac) if not arr.keeps_all else arr.k_lo
     video_weight = per_row + live_global_cols
     global_weight = float(sum(1 for v in valid if v > 0))
+    order = balanced_order(n_heads, layout.n_tiles, n_video, global_weight,
+                           video_weight, sms).to(device)
+    cache[key] = order
+    return order
+
+
+def balanced_order(n_heads: int, n_tiles: int, n_video: int,
+                   global_weight: float, video_weight: float,
+                   ctas: int) -> torch.Tensor:
+    """The work order of `work_order` on the host: the global query rows
+    (tiles >= n_video) of every head first, then the video rows head by
+    head (each head's tiles in reverse), every item to the CTA with the
+    least work so far (ties to the lower CTA). [rounds, ctas] int32 with
+    slots h * n_tiles + qt, -1 where a CTA has no more items."""
     heavy = [(h, qt) for h in range(n_heads)
-             for qt in range(layout.n_tiles - 1, n_video - 1, -1)]
+             for qt in range(n_tiles - 1, n_video - 1, -1)]
     light = [(h, qt) for h in range(n_heads)
              for qt in range(n_video - 1, -1, -1)]
-    loads = [(0.0, c) for c in range(sms)]
-    lists = [[] for _ in range(sms)]
+    loads = [(0.0, c) for c in range(ctas)]
+    lists = [[] for _ in range(ctas)]
     for items, weight in ((heavy, global_weight), (light, video_weight)):
         for h, qt in items:
             load, c = heapq.heappop(loads)
-            lists[c].append(h * layout.n_tiles + qt)
+            lists[c].append(h * n_tiles + qt)
             heapq.heappush(loads, (load + weight, c))
     rounds = max(len(x) for x in lists)
-    order = torch.full((rounds, sms), -1, dtype=torch.int32)
+    order = torch.full((rounds, ctas), -1, dtype=torch.int32)
     for c, items in enumerate(lists):
-        order[:len(items), c] = torch.tensor(items, dtype=torch.int32)
-    order = order.to(device)
-    cache[key] = order
+        if items:
+            order[:len(items), c] = torch.tensor(items, dtype=torch.int32)
     return order
 
 

@@ -6,6 +6,7 @@ import json
 
 import numpy as np
 import pytest
+import torch
 
 import inputs
 from miowtion_b200 import mask as veda_mask
@@ -131,3 +132,29 @@ def test_fma_exp2_polynomial_error_bound():
     got = fit_exp2_poly.exp2_emulated(x, coef).astype(np.float64)
     rel = np.abs(got / np.exp2(x.astype(np.float64)) - 1.0)
     assert rel.max() < 1e-4
+
+
+def test_balanced_order_deals_every_item_once_and_evens_the_load():
+    """kernels.balanced_order (the forward's work order) on the host: every
+    (head, query tile) once, the dense global rows on distinct CTAs first,
+    and no CTA more than one item's weight above the mean (the greedy
+    least-loaded bound)."""
+    from miowtion_b200 import kernels
+    heads, n_tiles, n_video, ctas = 6, 788, 780, 148
+    gw, vw = 788.0, 76.7
+    order = kernels.balanced_order(heads, n_tiles, n_video, gw, vw, ctas)
+    assert order.shape[1] == ctas and order.dtype == torch.int32
+    items = order[order >= 0]
+    assert sorted(items.tolist()) == list(range(heads * n_tiles))
+    first = order[0]
+    assert int(((first % n_tiles) >= n_video).sum()) == min(
+        ctas, heads * (n_tiles - n_video))
+    weight = torch.where((order % n_tiles) >= n_video, gw, vw)
+    load = torch.where(order >= 0, weight, 0.0).sum(0)
+    assert float(load.max()) <= float(load.mean()) + gw
+    # Against striding the default order over the CTAs, the spread shrinks.
+    stride = torch.zeros(ctas)
+    for i in range(heads * n_tiles):
+        qt = n_tiles - 1 - i % n_tiles
+        stride[i % ctas] += gw if qt >= n_video else vw
+    assert float(load.max()) < float(stride.max())
