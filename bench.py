@@ -38,6 +38,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from miowtion_b200 import attention as veda_attention  # noqa: E402
+from miowtion_b200 import kernels  # noqa: E402
 from miowtion_b200 import mask as veda_mask  # noqa: E402
 from miowtion_b200 import plan as veda_plan  # noqa: E402
 from miowtion_b200 import predictor as veda_predictor  # noqa: E402
@@ -489,7 +490,8 @@ def main():
             'e2e': {'value': e2e_ms, 'unit': 'ms/layer', 'steps': e2e_steps,
                     'h2d_bytes_per_step': world * 3 * q.numel() * 2,
                     'd2h_bytes_per_step': world * q.numel() * 2},
-            'gpu_launches': args.steps * launches_per_step(plan, world),
+            'gpu_launches': args.steps * launches_per_step(
+                clip, plan, heads_split, args.pieces if heads_split else 1),
             'clocks': clk,
         }
         if dense is not None:
@@ -889,10 +891,24 @@ def run_train_step(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-def launches_per_step(plan, world):
-    """Our kernels per layer: per head group gather+pool q, k, gather v,
-    embed, logits, select, attention, scatter."""
-    return 8 * len(plan.head_groups(0, 'cpu'))
+def launches_per_step(clip, plan, heads_split, pieces=1):
+    """Our kernels per layer. Per head group on the packed path: pool q,
+    k and v to tile images (k pooled too), embed, logits, select, attention
+    (7), plus the gather of the global query tiles when there are any; on
+    the tile path gather+pool q, k, gather v, embed, logits, select,
+    attention, scatter (8). Head-parallel: per piece three packs and an
+    unpack of the exchange buffers."""
+    n = 0
+    for group in plan.head_groups(0, 'cpu'):
+        tl = clip.get(group.shape)
+        if kernels.packed_supported(tl) and not clip.config.compensated:
+            n += 7 + (1 if tl.n_global_tiles else 0)
+        else:
+            n += 8
+    if heads_split:
+        n *= pieces
+        n += 4 * pieces
+    return n
 
 
 if __name__ == '__main__':
