@@ -1,4 +1,4 @@
-"""Benchmark of the Veda sparse-attention layer on B200 (see DESIGN.md).
+"""Benchmark of the Veda sparse-attention layer on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
     python bench.py --impl reference ...   # the reference algorithm on CPU
