@@ -43,9 +43,9 @@ class VedaConfig:
     `teacher_q_tiles` (supervised video query tiles per layer and head
     group: a fraction of the video tiles when <= 1, else a count) and
     `recall_every` (diagnostics on every n-th layer). `transport_weight`
-    and `gauge_kl_weight` select the reference's ablation objectives, which
-    this package does not provide (TeacherCollector raises when they are
-    non-zero)."""
+    and `gauge_kl_weight` add the retained-transport-mass loss and the
+    gauge-fixed KL (`heatmap.transport_loss`, `heatmap.gauge_fixed_kl`)
+    to the seer KL (attention.py:52-63)."""
 
     heat_reduce: str = 'max'
     transport_weight: float = 0.0
@@ -281,10 +281,13 @@ class TeacherCollector:
     dense kernel); per head group of the plan, a seeded sample of video
     query tiles, the group's q and k gathered and pooled, the heat of the
     sampled tiles (`veda_teacher_heat`, reduce `config.heat_reduce`), the
-    predictor's logits of those tiles with gradients, the seer KL and its
-    backward, scaled so the sum over groups is the head-weighted mean times
-    `grad_scale`. No graph outlives the call; diagnostics stay on the device
-    in `stats`.
+    predictor's logits of those tiles with gradients, the seer KL (plus,
+    when their weights are non-zero, the transport loss, the gauge-fixed KL
+    and `topk_weight` times the oracle BCE) and its backward, scaled so the
+    sum over groups is the head-weighted mean times `grad_scale`. The heat's
+    own top-k is selected once per group for the terms and diagnostics that
+    compare against it. No graph outlives the call; diagnostics stay on the
+    device in `stats`.
     """
 
     def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
@@ -292,11 +295,6 @@ class TeacherCollector:
                  generator: torch.Generator, grad_scale: float,
                  dense_backend: str = 'auto', topk_weight: float = 0.0):
         config = clip.config
-        if config.transport_weight or config.gauge_kl_weight or topk_weight:
-            raise NotImplementedError(
-                'the transport, gauge-fixed KL and oracle top-k BCE '
-                'objectives are ablation losses this package does not '
-                'provide; the seer KL is')
         if config.heat_reduce not in ('max', 'sum'):
             raise ValueError(f"heat_reduce must be 'max' or 'sum': "
                              f'{config.heat_reduce!r}')
@@ -346,22 +344,45 @@ class TeacherCollector:
                         tile_layout, rows, config.heat_reduce)
                 del q_tiles, k_tiles
                 weight = heads.numel() / self._num_heads
+                blocks = self.clip.blocks(tile_layout)
+                diagnose = layer_index % config.recall_every == 0
+                # The heat's own top-k, selected once for every term that
+                # compares against it.
+                oracle = (heatmap.oracle_set(heat, tile_layout, blocks, rows)
+                          if (config.transport_weight or self.topk_weight
+                              or diagnose) else None)
                 with torch.enable_grad():
                     logits = self.predictor.layers[layer_index](
                         feats_q[:, rows], feats_k, heads)
                     kl = heatmap.seer_kl(logits, heat, tile_layout,
                                          config.kl_direction)
                     loss = config.kl_weight * kl
+                    if config.transport_weight:
+                        transport = heatmap.transport_loss(
+                            logits, heat, tile_layout, blocks, rows,
+                            oracle=oracle)
+                        loss = loss + config.transport_weight * transport
+                        self.stats.transport.append(transport.detach())
+                    if config.gauge_kl_weight:
+                        gauge = heatmap.gauge_fixed_kl(logits, heat,
+                                                       tile_layout, rows)
+                        loss = loss + config.gauge_kl_weight * gauge
+                        self.stats.gauge_kl.append(gauge.detach())
+                    if self.topk_weight:
+                        bce = heatmap.oracle_bce(logits, heat, tile_layout,
+                                                 blocks, rows, oracle=oracle)
+                        loss = loss + self.topk_weight * bce
+                        self.stats.topk_bce.append(bce.detach())
                     (loss * (weight * self.grad_scale)).backward()
                 term = kl.detach() * weight
                 layer_kl = term if layer_kl is None else layer_kl + term
                 self.stats.logit_std.append(
                     logits.detach()[:, :, :tile_layout.n_video_tiles]
                     .std(dim=-1).mean())
-                if layer_index % config.recall_every == 0:
+                if diagnose:
                     values = heatmap.mask_diagnostics(
-                        logits.detach(), heat, tile_layout,
-                        self.clip.blocks(tile_layout), rows)
+                        logits.detach(), heat, tile_layout, blocks, rows,
+                        oracle=oracle)
                     for name, value in values.items():
                         getattr(self.stats, name).append(value)
         self.stats.kl.append(layer_kl)

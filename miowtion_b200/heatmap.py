@@ -1,11 +1,13 @@
 """Teacher block heat: drop-in for the reference's `miowtion/veda/heatmap.py`
 heat entry points (`teacher_heat`, `teacher_heat_reference`), backed by the
-tcgen05 kernel `veda_teacher_heat`, plus the two pieces of the stage-1
-supervision the teacher collector runs by default: the seer KL and the
-mask diagnostics. Both are small fp32 torch on the [H', R, n] tile grid
-(about 1e-6 of the heat's cost); the reference's other losses
-(transport_loss, gauge_fixed_kl, oracle_bce) are ablation objectives and
-are not provided.
+tcgen05 kernel `veda_teacher_heat`, plus the stage-1 supervision the
+teacher collector trains the predictor with: the seer KL, the three
+ablation objectives (`transport_loss`, `gauge_fixed_kl`, `oracle_bce`) and
+the mask diagnostics. All of them are small fp32 torch on the [H', R, n]
+tile grid (about 1e-6 of the heat's cost). The heat's own top-k, which
+three of them compare against, is one launch of the selection kernel
+(`oracle_set`); a caller that needs it more than once per head group
+computes it once and passes it as `oracle=`.
 """
 
 from __future__ import annotations
@@ -182,15 +184,245 @@ def seer_kl(logits: torch.Tensor, heat: torch.Tensor,
         terms = torch.where(cols, log_student.exp()
                             * (log_student - log_teacher), 0.0)
     row_kl = terms.sum(-1)
-    head_kl = (row_kl * live).sum(-1) / live.sum(-1).clamp(min=1)
-    return head_kl.mean()
+    return _mean_rows_then_heads(row_kl, live)
+
+
+def _mean_rows_then_heads(per_row: torch.Tensor,
+                          live: torch.Tensor) -> torch.Tensor:
+    """Mean over the live rows of each head, then over heads; a head
+    without live rows counts as 0."""
+    per_row = torch.where(live, per_row, 0.0)
+    return (per_row.sum(-1) / live.sum(-1).clamp(min=1)).mean()
+
+
+def _decision_columns(layout: tiling.TileLayout,
+                      q_tiles: torch.Tensor) -> torch.Tensor:
+    """[1, R, n_video] bool: the video key tiles a predictor decides on for
+    each supervised row, i.e. the non-empty ones minus the row's own tile
+    (the forced diagonal is a kernel rule, heatmap.py:283-289)."""
+    n_video = layout.n_video_tiles
+    own = F.one_hot(q_tiles, n_video).bool()[None]
+    return layout.kv_ok[:n_video].view(1, 1, -1) & ~own
+
+
+def _standardise(scores: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Per-row zero mean, unit variance over the columns where `weight` is
+    1 (0 elsewhere): the projection that removes the per-row offset and
+    scale a top-k read-out cannot see (heatmap.py:309-317)."""
+    count = weight.sum(-1, keepdim=True).clamp(min=1.0)
+    centred = (scores - (scores * weight).sum(-1, keepdim=True) / count) * weight
+    var = (centred.square() * weight).sum(-1, keepdim=True) / count
+    return centred / var.clamp(min=1e-12).sqrt()
+
+
+def _video_mass(heat: torch.Tensor, columns: torch.Tensor) -> torch.Tensor:
+    """The teacher's non-negative block heat on the decision columns."""
+    mass = heat[:, :, :columns.shape[-1]].float()
+    return torch.where(columns, mass, 0.0).clamp(min=0.0)
+
+
+@torch.no_grad()
+def oracle_set(heat: torch.Tensor, layout: tiling.TileLayout,
+               blocks: list[veda_mask.ColumnBlock],
+               q_tiles: torch.Tensor) -> torch.Tensor:
+    """The heat's own top-k selection over the video key tiles at the
+    clip's budgets, as a [H', R, n_video] bool mask: the oracle set that
+    `transport_loss`, `oracle_bce` and `mask_diagnostics` compare against
+    (heatmap.py:285-291, :462-466). One launch of the selection kernel."""
+    n_video = layout.n_video_tiles
+    q_tiles = q_tiles.to(device=heat.device, dtype=torch.int64)
+    sel = veda_mask.select_video_blocks(heat.float().contiguous(), layout,
+                                        blocks, q_tiles)
+    chosen = torch.zeros(*sel.index.shape[:2], n_video, dtype=torch.bool,
+                         device=heat.device)
+    return chosen.scatter_(2, sel.index, sel.keep)
+
+
+# Width of the soft top-k boundary in row-standardised score units
+# (heatmap.py:183-190).
+TRANSPORT_TAU = 0.15
+
+# Masked columns sort below every standardised score at this value
+# (heatmap.py:118-121). Where a row's budget reaches its last valid column
+# the cut falls halfway down to it, and the sigmoid is then 1 at every
+# valid column for any value this large.
+_BELOW_EVERY_SCORE = 1e4
+
+
+def transport_loss(logits: torch.Tensor, heat: torch.Tensor,
+                   layout: tiling.TileLayout,
+                   blocks: list[veda_mask.ColumnBlock],
+                   q_tiles: torch.Tensor,
+                   temperature: float = TRANSPORT_TAU,
+                   oracle: torch.Tensor | None = None) -> torch.Tensor:
+    """Minus the retained transport mass relative to the oracle's
+    (heatmap.py:192-333).
+
+    Per row: the student's scores over the decision columns are
+    standardised, the row's cut is placed halfway between its k-th and
+    (k+1)-th largest standardised score (k = the oracle's off-diagonal
+    budget of the row; the cut carries no gradient), and the soft policy
+    sigmoid((z - cut) / temperature) is rescaled to spend exactly k. The
+    row's value is the policy's share of the teacher mass the oracle keeps;
+    rows where the oracle keeps nothing or no mass do not count. -1 is the
+    oracle's own choice; as temperature -> 0 the loss is minus the
+    `retained` diagnostic of the student's hard top-k. Invariant to a
+    per-row positive affine map of the logits.
+
+    Args:
+        logits: [H', R, n_tiles] fp32 student logits (with grad).
+        heat: [H', R, n_tiles] teacher heat (the mass reduction).
+        layout: Tile layout.
+        blocks: Column blocks with their budgets.
+        q_tiles: [R] int64 supervised video query tiles.
+        temperature: Width of the soft boundary; > 0.
+        oracle: The heat's own selection, `oracle_set(heat, ...)`, if the
+            caller has it already.
+
+    Returns:
+        Scalar loss (rows averaged, then heads).
+
+    Raises:
+        ValueError: If temperature is not positive.
+    """
+    if temperature <= 0:
+        raise ValueError(f'temperature must be > 0: {temperature}')
+    n_video = layout.n_video_tiles
+    q_tiles = q_tiles.to(device=logits.device, dtype=torch.int64)
+    with torch.no_grad():
+        if oracle is None:
+            oracle = oracle_set(heat, layout, blocks, q_tiles)
+        columns = _decision_columns(layout, q_tiles)
+        kept = oracle & columns
+        mass = _video_mass(heat, columns)
+        ceiling = (mass * kept).sum(-1)
+        budget = kept.sum(-1)
+        live = (ceiling > 0) & (budget > 0)
+    weight = columns.float()
+    z = _standardise(logits[:, :, :n_video].float(), weight)
+    with torch.no_grad():
+        ranked = z.masked_fill(~columns, -_BELOW_EVERY_SCORE).sort(
+            -1, descending=True).values
+        last = n_video - 1
+        kth = (budget - 1).clamp(min=0, max=last).unsqueeze(-1)
+        cut = 0.5 * (ranked.gather(-1, kth)
+                     + ranked.gather(-1, (kth + 1).clamp(max=last)))
+    policy = torch.sigmoid((z - cut) / temperature) * weight
+    spend = budget.unsqueeze(-1).float() / policy.sum(-1, keepdim=True).clamp(
+        min=1e-6)
+    retained = (policy * spend * mass).sum(-1) / ceiling.clamp(
+        min=torch.finfo(torch.float32).tiny)
+    return -_mean_rows_then_heads(retained, live)
+
+
+# Floor of the teacher's block probability relative to the row's largest,
+# for the logarithm that sets the row's scale (heatmap.py:336-340).
+GAUGE_FLOOR = 1e-6
+
+
+def gauge_fixed_kl(logits: torch.Tensor, heat: torch.Tensor,
+                   layout: tiling.TileLayout,
+                   q_tiles: torch.Tensor) -> torch.Tensor:
+    """Forward KL(teacher || student) over the decision columns after
+    moving the student's standardised scores onto the teacher's own
+    log-probability scale (heatmap.py:341-430).
+
+    Per row: t = the teacher's mass normalised over the decision columns,
+    floored at GAUGE_FLOOR times its row maximum; the student's scores are
+    standardised and mapped to mean(log t) + std(log t) * z; the row's term
+    is sum t * (log t - log softmax). 0 when the student reproduces the
+    teacher up to a per-row positive affine map; rows without teacher mass
+    do not count.
+
+    Args:
+        logits: [H', R, n_tiles] fp32 student logits (with grad).
+        heat: [H', R, n_tiles] teacher heat (the mass reduction).
+        layout: Tile layout.
+        q_tiles: [R] int64 supervised video query tiles.
+
+    Returns:
+        Scalar divergence (rows averaged, then heads).
+    """
+    n_video = layout.n_video_tiles
+    q_tiles = q_tiles.to(device=logits.device, dtype=torch.int64)
+    columns = _decision_columns(layout, q_tiles)
+    weight = columns.float()
+    count = weight.sum(-1, keepdim=True).clamp(min=1.0)
+    tiny = torch.finfo(torch.float32).tiny
+    with torch.no_grad():
+        mass = _video_mass(heat, columns)
+        total = mass.sum(-1, keepdim=True)
+        live = total.squeeze(-1) > 0
+        teacher = mass / total.clamp(min=tiny)
+        floor = GAUGE_FLOOR * teacher.amax(-1, keepdim=True).clamp(min=tiny)
+        log_teacher = torch.maximum(teacher, floor).log()
+        level = (log_teacher * weight).sum(-1, keepdim=True) / count
+        spread = (((log_teacher - level) * weight).square() * weight).sum(
+            -1, keepdim=True) / count
+    z = _standardise(logits[:, :, :n_video].float(), weight)
+    moved = z * spread.sqrt() + level
+    log_student = F.log_softmax(moved.masked_fill(~columns, float('-inf')),
+                                dim=-1)
+    # Excluded columns carry teacher weight 0; their log is -inf, so zero
+    # it before the product (0 * -inf would be NaN).
+    log_student = log_student.masked_fill(~columns, 0.0)
+    per_row = (teacher * (log_teacher - log_student) * weight).sum(-1)
+    return _mean_rows_then_heads(per_row, live)
+
+
+def oracle_bce(logits: torch.Tensor, heat: torch.Tensor,
+               layout: tiling.TileLayout,
+               blocks: list[veda_mask.ColumnBlock],
+               q_tiles: torch.Tensor,
+               oracle: torch.Tensor | None = None) -> torch.Tensor:
+    """Class-balanced BCE of the row-centred student logits against the
+    oracle's top-k set over the decision columns (heatmap.py:433-496).
+
+    Each row's logits are centred on their mean over the decision columns;
+    the BCE terms of the oracle's members and of the other decision columns
+    are averaged separately (over all heads and rows) and the two means
+    halved. An indifferent predictor scores ln 2; 0 when no decision
+    column exists.
+
+    Args:
+        logits: [H', R, n_tiles] fp32 student logits (with grad).
+        heat: [H', R, n_tiles] teacher heat.
+        layout: Tile layout.
+        blocks: Column blocks with their budgets.
+        q_tiles: [R] int64 supervised video query tiles.
+        oracle: The heat's own selection, `oracle_set(heat, ...)`, if the
+            caller has it already.
+
+    Returns:
+        Scalar loss.
+    """
+    n_video = layout.n_video_tiles
+    q_tiles = q_tiles.to(device=logits.device, dtype=torch.int64)
+    with torch.no_grad():
+        if oracle is None:
+            oracle = oracle_set(heat, layout, blocks, q_tiles)
+        columns = _decision_columns(layout, q_tiles)
+        members = oracle & columns
+        others = ~oracle & columns
+    weight = columns.float()
+    scores = logits[:, :, :n_video].float()
+    count = weight.sum(-1, keepdim=True).clamp(min=1.0)
+    centred = scores - (scores * weight).sum(-1, keepdim=True) / count
+    terms = F.binary_cross_entropy_with_logits(centred, oracle.float(),
+                                               reduction='none')
+    loss = 0.5 * ((terms * members).sum() / members.sum().clamp(min=1)
+                  + (terms * others).sum() / others.sum().clamp(min=1))
+    # Decided on the device, so the host never waits for the counts.
+    return torch.where(columns.any(), loss, torch.zeros_like(loss))
 
 
 @torch.no_grad()
 def mask_diagnostics(logits: torch.Tensor, heat: torch.Tensor,
                      layout: tiling.TileLayout,
                      blocks: list[veda_mask.ColumnBlock],
-                     q_tiles: torch.Tensor) -> dict[str, torch.Tensor]:
+                     q_tiles: torch.Tensor,
+                     oracle: torch.Tensor | None = None
+                     ) -> dict[str, torch.Tensor]:
     """Predictor against oracle on the video quadrant, as device scalars
     (heatmap.py:499-574): `recall` (off-diagonal overlap of the predicted
     and the heat's own top-k sets; NaN when the budget holds nothing but the
@@ -206,18 +438,14 @@ def mask_diagnostics(logits: torch.Tensor, heat: torch.Tensor,
         layout: Tile layout.
         blocks: Column blocks with their budgets.
         q_tiles: [R] int64 video query tiles.
+        oracle: The heat's own selection, `oracle_set(heat, ...)`, if the
+            caller has it already.
     """
     n_video = layout.n_video_tiles
     q_tiles = q_tiles.to(device=logits.device, dtype=torch.int64)
-
-    def chosen(scores: torch.Tensor) -> torch.Tensor:
-        sel = veda_mask.select_video_blocks(scores.contiguous(), layout,
-                                            blocks, q_tiles)
-        out = torch.zeros(*sel.index.shape[:2], n_video, dtype=torch.bool,
-                          device=logits.device)
-        return out.scatter_(2, sel.index, sel.keep)
-
-    predicted, oracle = chosen(logits.float()), chosen(heat.float())
+    predicted = oracle_set(logits, layout, blocks, q_tiles)
+    if oracle is None:
+        oracle = oracle_set(heat, layout, blocks, q_tiles)
     mass = heat[:, :, :n_video].float().clamp(min=0.0)
     total = mass.sum(-1)
     tiny = torch.finfo(torch.float32).tiny

@@ -130,10 +130,21 @@ def projection(dim, seed):
 
 # TeacherCollector (stage 1): text rows, a padded target grid cut by two tile
 # shapes over the heads, two layers; each case a heat reduction, a KL
-# direction and a share of supervised query tiles.
+# direction, a share of supervised query tiles and optionally the weights
+# of the ablation losses added to the seer KL.
 TEACHER = dict(text=130, grid=(4, 12, 20), seq_len=1100, heads=4, dim=128,
                seed=81, pred_seed=82, pred_std=0.02, layers=2,
                shapes=[(2, 8, 8), (1, 8, 16)], head_shape=[0, 1, 0, 1],
                ratio=0.4, gen_seed=7, grad_scale=0.5,
                cases={'max_fwd': ('max', 'forward', 0.5),
-                      'sum_rev': ('sum', 'reverse', 1.0)})
+                      'sum_rev': ('sum', 'reverse', 1.0),
+                      'sum_ablate': ('sum', 'forward', 0.5,
+                                     dict(transport_weight=0.5,
+                                          gauge_kl_weight=0.25,
+                                          topk_weight=0.3))})
+
+# The ablation losses (transport, gauge-fixed KL, oracle BCE) on seeded
+# logits and heat over the padded layout: supervised rows, a budget that
+# reaches well past the diagonal, temperatures of the transport loss.
+LOSSES = dict(heads=3, rows=[0, 3, 7, 12, 19], ratio=0.5, seed=93,
+              temperatures=[0.15, 0.5, 1e-4])

@@ -1,7 +1,8 @@
 """TeacherCollector (stage 1) on the B200 kernels against the reference's
 own collector run on the CPU (tests/golden/make_teacher.py): the dense
-output, the per-layer seer KL, the diagnostics and the predictor's
-gradients, for a heat reduction / KL direction / supervision share each."""
+output, the per-layer seer KL, the diagnostics, the ablation losses and
+the predictor's gradients, for a heat reduction / KL direction /
+supervision share / loss weighting each."""
 
 import os
 
@@ -12,6 +13,7 @@ import torch
 import inputs
 from miowtion_b200 import _lib
 from miowtion_b200 import attention as veda_attention
+from miowtion_b200 import heatmap
 from miowtion_b200 import mask as veda_mask
 from miowtion_b200 import plan as veda_plan
 from miowtion_b200 import predictor as veda_predictor
@@ -30,7 +32,9 @@ def _status_clean():
     assert _lib.device_status(reset=True) == 0, 'a kernel wait timed out'
 
 
-def run_case(spec, heat_reduce, direction, q_tiles):
+def run_case(spec, heat_reduce, direction, q_tiles, weights=None):
+    weights = dict(weights or {})
+    topk_weight = weights.pop('topk_weight', 0.0)
     text, grid, seq_len = spec['text'], spec['grid'], spec['seq_len']
     used = text + grid[0] * grid[1] * grid[2]
     q, k, v = (t.to(DEV) for t in inputs.qkv(seq_len, spec['heads'],
@@ -39,7 +43,7 @@ def run_case(spec, heat_reduce, direction, q_tiles):
     config = veda_attention.VedaConfig(
         target_budget=veda_mask.Budget(ratio=spec['ratio']),
         heat_reduce=heat_reduce, kl_direction=direction,
-        teacher_q_tiles=q_tiles)
+        teacher_q_tiles=q_tiles, **weights)
     layout = veda_attention.PackedLayout(
         seq_len, used, (veda_attention.VideoSpan(text, grid),))
     clip = veda_attention.ClipTiling(layout, config, DEV)
@@ -58,7 +62,8 @@ def run_case(spec, heat_reduce, direction, q_tiles):
     predictor = predictor.to(DEV)
     gen = torch.Generator().manual_seed(spec['gen_seed'])
     teacher = veda_attention.TeacherCollector(clip, plan, predictor, gen,
-                                              spec['grad_scale'])
+                                              spec['grad_scale'],
+                                              topk_weight=topk_weight)
     outs = [teacher(q, k, v, layer) for layer in range(spec['layers'])]
     torch.cuda.synchronize()
     return outs, teacher.stats.resolve(), predictor
@@ -85,6 +90,14 @@ def test_teacher_collector_matches_reference(case):
     for name in ('recall', 'heat_kept', 'heat_ceiling', 'retained'):
         np.testing.assert_allclose(stats[name], want[name], rtol=0,
                                    atol=0.05, equal_nan=True, err_msg=name)
+    # The ablation losses, where the case weights them: one value per
+    # layer and head group, from the heat within its tolerance.
+    for name in ('transport', 'gauge_kl', 'topk_bce'):
+        if name in want:
+            np.testing.assert_allclose(stats[name], want[name], rtol=0,
+                                       atol=0.05, err_msg=name)
+        else:
+            assert stats[name] == [], name
     # Gradients of the projections (feature rows [::12]).
     for i, layer in enumerate(predictor.layers):
         for side, param in (('q', layer.proj_q), ('k', layer.proj_k)):
@@ -95,20 +108,38 @@ def test_teacher_collector_matches_reference(case):
                                        err_msg=f'grad_{side}{i}')
 
 
-def test_teacher_collector_refuses_ablation_losses():
-    spec = inputs.TEACHER
-    text, grid, seq_len = spec['text'], spec['grid'], spec['seq_len']
-    used = text + grid[0] * grid[1] * grid[2]
-    config = veda_attention.VedaConfig(transport_weight=1.0)
-    layout = veda_attention.PackedLayout(
-        seq_len, used, (veda_attention.VideoSpan(text, grid),))
-    clip = veda_attention.ClipTiling(layout, config, DEV)
-    plan = veda_plan.TilePlan('t', grid, [tiling.TileShape(2, 8, 8)],
-                              [[0] * spec['heads']])
-    predictor = veda_predictor.TileScorePredictor(1, spec['heads'], 128)
-    with pytest.raises(NotImplementedError, match='ablation'):
-        veda_attention.TeacherCollector(clip, plan, predictor,
-                                        torch.Generator(), 1.0)
+def test_ablation_losses_select_the_oracle_set_on_the_gpu():
+    """`oracle_set` on the selection kernel reproduces the reference's own
+    top-k set of the heat, and the losses that select it themselves match
+    the reference's values and gradients (tests/golden/make_teacher.py)."""
+    golden = np.load(GOLDEN)
+    pad, spec = inputs.PADDED, inputs.LOSSES
+    layout = tiling.build_tile_layout(
+        [tiling.TiledSpan(s, g, tiling.TileShape(*sh))
+         for s, g, sh in pad['spans']], pad['used'], pad['seq_len'], DEV)
+    blocks = veda_mask.column_blocks(layout,
+                                     veda_mask.Budget(ratio=spec['ratio']))
+    rows = torch.tensor(spec['rows'], device=DEV)
+    heat = torch.from_numpy(golden['loss_heat']).to(DEV)
+    oracle = heatmap.oracle_set(heat, layout, blocks, rows)
+    assert np.array_equal(oracle.cpu().numpy(), golden['loss_oracle'])
+    cases = {f'transport_{t:g}': lambda x, t=t: heatmap.transport_loss(
+        x, heat, layout, blocks, rows, temperature=t)
+        for t in spec['temperatures']}
+    cases['gauge'] = lambda x: heatmap.gauge_fixed_kl(x, heat, layout, rows)
+    cases['bce'] = lambda x: heatmap.oracle_bce(x, heat, layout, blocks,
+                                                rows)
+    for name, fn in cases.items():
+        logits = torch.from_numpy(golden['loss_logits']).to(
+            DEV).requires_grad_(True)
+        value = fn(logits)
+        value.backward()
+        np.testing.assert_allclose(value.item(), golden[f'loss_{name}'],
+                                   rtol=1e-4, atol=1e-6, err_msg=name)
+        want = golden[f'loss_{name}_grad']
+        np.testing.assert_allclose(logits.grad.cpu().numpy(), want, rtol=0,
+                                   atol=1e-4 * max(1.0, np.abs(want).max()),
+                                   err_msg=name)
 
 
 def test_teacher_output_is_the_dense_attention_and_trains_only_the_predictor():
