@@ -235,6 +235,35 @@ class _SparseGroup(torch.autograd.Function):
         return (*outs, None, None, None, None, None, None)
 
 
+def _extra_features(predictor: veda_predictor.TileScorePredictor,
+                    tile_layout: tiling.TileLayout,
+                    sq_q: torch.Tensor | None, var_k: torch.Tensor | None,
+                    rows: torch.Tensor | None = None) -> dict:
+    """Keyword inputs of the predictor's optional score terms
+    (attention.py:251-288): log B_j from the layout for the count term, the
+    pooled E[q^2] (query rows `rows` of it, if given) and Var(k) for the
+    second-order head; {} for a plain predictor."""
+    extra: dict = {}
+    if predictor.count_term:
+        extra['log_count'] = veda_predictor.log_tile_counts(tile_layout)
+    if predictor.second_order_rank:
+        if sq_q is None or var_k is None:
+            raise ValueError('the second-order head needs the pooled '
+                             'second moments; gather with second=True')
+        extra['sq_q'] = sq_q if rows is None else sq_q[:, rows]
+        extra['var_k'] = var_k
+    return extra
+
+
+def _gather_pool_moments(x: torch.Tensor, tile_layout: tiling.TileLayout,
+                         heads: torch.Tensor, second: bool):
+    """(tiles, features, E[x^2], Var(x)) of one gather/pool pass; the
+    moments are None unless `second`."""
+    if second:
+        return tiling.gather_and_pool(x, tile_layout, heads, second=True)
+    return (*tiling.gather_and_pool(x, tile_layout, heads), None, None)
+
+
 # Diagnostic fields of LayerStats in the order resolve() transfers them
 # (attention.py:308-310).
 STAT_FIELDS = ('kl', 'topk_bce', 'transport', 'logit_std', 'recall',
@@ -333,11 +362,12 @@ class TeacherCollector:
             rows = self._sample_rows(tile_layout)
             for heads in group.heads.split(
                     _chunk_heads(tile_layout, config.collect_bytes)):
+                second = bool(self.predictor.second_order_rank)
                 with torch.no_grad():
-                    q_tiles, feats_q = tiling.gather_and_pool(
-                        q.detach(), tile_layout, heads)
-                    k_tiles, feats_k = tiling.gather_and_pool(
-                        k.detach(), tile_layout, heads)
+                    q_tiles, feats_q, sq_q, _ = _gather_pool_moments(
+                        q.detach(), tile_layout, heads, second)
+                    k_tiles, feats_k, _, var_k = _gather_pool_moments(
+                        k.detach(), tile_layout, heads, second)
                     heat = heatmap.teacher_heat(
                         q_tiles, k_tiles,
                         tiling.gather_lse(lse, tile_layout, heads),
@@ -351,9 +381,11 @@ class TeacherCollector:
                 oracle = (heatmap.oracle_set(heat, tile_layout, blocks, rows)
                           if (config.transport_weight or self.topk_weight
                               or diagnose) else None)
+                extra = _extra_features(self.predictor, tile_layout, sq_q,
+                                        var_k, rows)
                 with torch.enable_grad():
                     logits = self.predictor.layers[layer_index](
-                        feats_q[:, rows], feats_k, heads)
+                        feats_q[:, rows], feats_k, heads, **extra)
                     kl = heatmap.seer_kl(logits, heat, tile_layout,
                                          config.kl_direction)
                     loss = config.kl_weight * kl
@@ -453,20 +485,24 @@ class SparseStudent:
                 tile_layout: tiling.TileLayout, heads: torch.Tensor,
                 out: torch.Tensor) -> None:
         """Sparse attention of some heads of one group, scattered to out."""
-        if (not self.clip.config.compensated
+        second = bool(self.predictor.second_order_rank)
+        if (not self.clip.config.compensated and not second
                 and kernels.packed_supported(tile_layout)):
             self._attend_packed(q, k, v, layer_index, tile_layout, heads, out)
             return
         ev = self.events
         t = ev.start('permute_pool')
-        q_tiles, feats_q = tiling.gather_and_pool(q, tile_layout, heads)
-        k_tiles, feats_k = tiling.gather_and_pool(k, tile_layout, heads)
+        q_tiles, feats_q, sq_q, _ = _gather_pool_moments(q, tile_layout,
+                                                         heads, second)
+        k_tiles, feats_k, _, var_k = _gather_pool_moments(k, tile_layout,
+                                                          heads, second)
         v_tiles = tiling.gather_tiles(v, tile_layout, heads)
         ev.stop(t)
         with torch.no_grad():
             t = ev.start('score')
             logits = self.predictor.layers[layer_index](
-                feats_q, feats_k, heads + self.head_offset)
+                feats_q, feats_k, heads + self.head_offset,
+                **_extra_features(self.predictor, tile_layout, sq_q, var_k))
             ev.stop(t)
             t = ev.start('topk')
             lists = veda_mask.select_block_lists(
@@ -508,7 +544,8 @@ class SparseStudent:
         with torch.no_grad():
             t = ev.start('score')
             logits = self.predictor.layers[layer_index](
-                feats_q, feats_k, heads + self.head_offset)
+                feats_q, feats_k, heads + self.head_offset,
+                **_extra_features(self.predictor, tile_layout, None, None))
             ev.stop(t)
             t = ev.start('topk')
             lists = veda_mask.select_block_lists(
@@ -537,13 +574,16 @@ class SparseStudent:
         for group in self.plan.head_groups(layer_index, self.clip.device):
             tile_layout = self.clip.get(group.shape)
             heads = group.heads
+            second = bool(self.predictor.second_order_rank)
             with torch.no_grad():
-                q_tiles, feats_q = tiling.gather_and_pool(q.detach(),
-                                                          tile_layout, heads)
-                k_tiles, feats_k = tiling.gather_and_pool(k.detach(),
-                                                          tile_layout, heads)
+                q_tiles, feats_q, sq_q, _ = _gather_pool_moments(
+                    q.detach(), tile_layout, heads, second)
+                k_tiles, feats_k, _, var_k = _gather_pool_moments(
+                    k.detach(), tile_layout, heads, second)
                 logits = self.predictor.layers[layer_index](
-                    feats_q, feats_k, heads + self.head_offset)
+                    feats_q, feats_k, heads + self.head_offset,
+                    **_extra_features(self.predictor, tile_layout, sq_q,
+                                      var_k))
                 lists = veda_mask.select_block_lists(
                     logits[:, :tile_layout.n_video_tiles], tile_layout,
                     self.clip.blocks(tile_layout), want_mask=True)

@@ -7,8 +7,13 @@ and head a residual projection maps them to D dims,
 and block logits are q_hat . k_hat / sqrt(D) in fp32. Pooling and logits run
 in CUDA kernels (csrc/permute.cu, csrc/predict.cu).
 
-The reference's optional terms (`count_term`, `second_order_rank > 0`) are
-not implemented on the device and raise NotImplementedError.
+The reference's optional score terms are supported on top of that kernel:
+`count_term` adds a learned per-head gain times log B_j (B_j = the real
+rows of key tile j), and `second_order_rank = r > 0` a low-rank
+second-cumulant head (sq_q @ So_q) . (var_k @ So_k) over the pooled E[q^2]
+and Var(k), which the gather/pool kernel produces in the same pass. Both
+are small fp32 batched products next to the logits (r / D of the logit
+GEMM's work), with autograd for their parameters.
 """
 
 from __future__ import annotations
@@ -133,37 +138,163 @@ def predict_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
                                   heads)[0]
 
 
+def _psd_roots(matrix: torch.Tensor,
+               floor: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric square root of a PSD matrix and the pseudo-inverse of that
+    root, dropping eigenvalues at or below `floor` times the largest
+    (predictor.py:171-194)."""
+    values, vectors = torch.linalg.eigh(matrix)
+    values = values.clamp(min=0.0)
+    cut = float(values.max()) * floor
+    kept = values > cut
+    root = torch.where(kept, values.sqrt(), 0.0)
+    inverse = torch.where(kept, values.clamp(min=cut).rsqrt(), 0.0)
+    basis_t = vectors.transpose(0, 1)
+    return (vectors * root) @ basis_t, (vectors * inverse) @ basis_t
+
+
 class LayerPredictor(nn.Module):
     """Projections of one layer: proj_q, proj_k [num_heads, 3D, D]
-    (predictor.py:197-230)."""
+    (predictor.py:197-230); with `second_order_rank = r` also so_q, so_k
+    [num_heads, D, r], with `count_term` a gain [num_heads] on log B_j
+    (initialised to 1, the exact coefficient)."""
 
     def __init__(self, num_heads: int, head_dim: int,
                  second_order_rank: int = 0, count_term: bool = False):
         super().__init__()
-        if second_order_rank or count_term:
-            raise NotImplementedError(
-                'second-order and count terms have no B200 kernel')
+        if not 0 <= second_order_rank <= head_dim:
+            raise ValueError(f'second_order_rank {second_order_rank} must be '
+                             f'in [0, {head_dim}]')
         self.head_dim = head_dim
-        self.second_order_rank = 0
+        self.second_order_rank = second_order_rank
         self.proj_q = nn.Parameter(torch.empty(num_heads, 3 * head_dim,
                                                head_dim))
         self.proj_k = nn.Parameter(torch.empty(num_heads, 3 * head_dim,
                                                head_dim))
         nn.init.normal_(self.proj_q, std=INIT_STD)
         nn.init.normal_(self.proj_k, std=INIT_STD)
+        if second_order_rank:
+            self.so_q = nn.Parameter(torch.empty(num_heads, head_dim,
+                                                 second_order_rank))
+            self.so_k = nn.Parameter(torch.empty(num_heads, head_dim,
+                                                 second_order_rank))
+            nn.init.normal_(self.so_q, std=INIT_STD)
+            nn.init.normal_(self.so_k, std=INIT_STD)
+        if count_term:
+            self.count_gain = nn.Parameter(torch.ones(num_heads))
 
-    def forward(self, feats_q: torch.Tensor, feats_k: torch.Tensor,
-                heads: torch.Tensor) -> torch.Tensor:
-        """Block logits [H', n_q, n_k] fp32 (predictor.py:299-338).
+    @torch.no_grad()
+    def init_exact_second_order_(self) -> None:
+        """Sets the full-rank head to the diagonal cumulant term
+        E[q^2] . Var(k) / (2 D): both sides sqrt(1 / (2 D)) times the
+        identity (predictor.py:232-249).
 
         Raises:
+            ValueError: If the rank is not head_dim.
+        """
+        if self.second_order_rank != self.head_dim:
+            raise ValueError('the exact term needs second_order_rank == '
+                             f'head_dim, not {self.second_order_rank}')
+        scaled = torch.eye(self.head_dim, dtype=self.so_q.dtype,
+                           device=self.so_q.device) * math.sqrt(
+                               0.5 / self.head_dim)
+        self.so_q.copy_(scaled)
+        self.so_k.copy_(scaled)
+
+    @torch.no_grad()
+    def init_low_rank_second_order_(self, c_u: torch.Tensor,
+                                    c_v: torch.Tensor,
+                                    floor: float = 1e-6) -> None:
+        """The rank-r head closest to (1 / 2D) I under the feature moments
+        C_u = E[sq_q^T sq_q], C_v = E[var_k^T var_k] [num_heads, D, D]
+        (predictor.py:258-297): per head the rank-r truncated SVD
+        L S R^T of (1 / 2D) C_u^(1/2) C_v^(1/2), mapped back to each side,
+        so_q = C_u^(-1/2) L_r S_r^(1/2), so_k = C_v^(-1/2) R_r S_r^(1/2).
+        At r = D it reproduces `init_exact_second_order_`'s product on the
+        moments' support.
+
+        Raises:
+            ValueError: Without a second-order head, or on moments of the
+                wrong shape.
+        """
+        if not self.second_order_rank:
+            raise ValueError('no second-order head to initialize')
+        heads, dim = self.so_q.shape[0], self.head_dim
+        for name, moment in (('c_u', c_u), ('c_v', c_v)):
+            if tuple(moment.shape) != (heads, dim, dim):
+                raise ValueError(f'{name} has shape {tuple(moment.shape)}, '
+                                 f'expected {(heads, dim, dim)}')
+        rank = self.second_order_rank
+        for head in range(heads):
+            root_u, inv_u = _psd_roots(c_u[head].float(), floor)
+            root_v, inv_v = _psd_roots(c_v[head].float(), floor)
+            left, sing, right_t = torch.linalg.svd(
+                (0.5 / dim) * (root_u @ root_v))
+            gain = sing[:rank].clamp(min=0.0).sqrt()
+            self.so_q[head] = (inv_u @ left[:, :rank]) * gain
+            self.so_k[head] = (inv_v @ right_t[:rank].transpose(0, 1)) * gain
+
+    def _check_terms(self, sq_q, var_k, log_count) -> None:
+        if hasattr(self, 'count_gain') != (log_count is not None):
+            raise ValueError('log_count and count_term must be set '
+                             'together')
+        if bool(self.second_order_rank) != (sq_q is not None
+                                            and var_k is not None):
+            raise ValueError('second-order features and second_order_rank '
+                             'must be set together')
+
+    def optional_terms(self, heads: torch.Tensor,
+                       sq_q: torch.Tensor | None = None,
+                       var_k: torch.Tensor | None = None,
+                       log_count: torch.Tensor | None = None
+                       ) -> torch.Tensor | None:
+        """The count and second-order terms [H', n_q, n_k] fp32 that
+        `forward` adds to the bilinear logits (predictor.py:331-338), or
+        None for a plain predictor. Differentiable in count_gain, so_q and
+        so_k."""
+        self._check_terms(sq_q, var_k, log_count)
+        heads = heads.to(dtype=torch.int64)
+        terms = None
+        if log_count is not None:
+            gain = self.count_gain.index_select(0, heads).float()
+            terms = gain[:, None, None] * log_count.float()[None, None, :]
+        if self.second_order_rank:
+            u = torch.bmm(sq_q.float(),
+                          self.so_q.index_select(0, heads).float())
+            w = torch.bmm(var_k.float(),
+                          self.so_k.index_select(0, heads).float())
+            second = torch.bmm(u, w.transpose(1, 2))
+            terms = second if terms is None else terms + second
+        return terms
+
+    def forward(self, feats_q: torch.Tensor, feats_k: torch.Tensor,
+                heads: torch.Tensor, sq_q: torch.Tensor | None = None,
+                var_k: torch.Tensor | None = None,
+                log_count: torch.Tensor | None = None) -> torch.Tensor:
+        """Block logits [H', n_q, n_k] fp32 (predictor.py:299-338).
+
+        Args:
+            feats_q, feats_k: [H', n, 3D] pooled features.
+            heads: [H'] global head indices.
+            sq_q: [H', n_q, D] pooled E[q^2]; iff second_order_rank > 0.
+            var_k: [H', n_k, D] pooled Var(k); likewise.
+            log_count: [n_k] log of each key tile's real rows (clamped to
+                >= 1); iff count_term.
+
+        Raises:
+            ValueError: If an optional feature is missing, or given when
+                its term is off.
             NotImplementedError: For a head_dim other than 128 (the scoring
                 kernel's only size; other sizes load and save, nothing more).
         """
+        self._check_terms(sq_q, var_k, log_count)
         if self.head_dim != 128:
             raise NotImplementedError('the predictor kernels take head_dim 128')
-        return predict_logits(feats_q, feats_k, self.proj_q, self.proj_k,
-                              heads)
+        logits = predict_logits(feats_q, feats_k, self.proj_q, self.proj_k,
+                                heads)
+        terms = self.optional_terms(heads.to(feats_q.device), sq_q, var_k,
+                                    log_count)
+        return logits if terms is None else logits + terms
 
 
 class TileScorePredictor(nn.Module):
@@ -179,9 +310,39 @@ class TileScorePredictor(nn.Module):
             LayerPredictor(num_heads, head_dim, second_order_rank, count_term)
             for _ in range(num_layers))
 
+    def init_exact_second_order_(self) -> None:
+        """`LayerPredictor.init_exact_second_order_` on every layer."""
+        for layer in self.layers:
+            layer.init_exact_second_order_()
+
+    def init_low_rank_second_order_(self, c_u: torch.Tensor,
+                                    c_v: torch.Tensor,
+                                    floor: float = 1e-6) -> None:
+        """Per layer from moments [num_layers, num_heads, D, D]
+        (predictor.py:367-385)."""
+        if c_u.shape[0] != len(self.layers) or c_v.shape[0] != len(
+                self.layers):
+            raise ValueError('one moment per layer is needed')
+        for index, layer in enumerate(self.layers):
+            layer.init_low_rank_second_order_(c_u[index], c_v[index], floor)
+
     def scores(self, layer: int, q_tiles: torch.Tensor, k_tiles: torch.Tensor,
                layout: tiling.TileLayout, heads: torch.Tensor) -> torch.Tensor:
-        """Block logits of one head group [H', n, n] fp32."""
+        """Block logits of one head group [H', n, n] fp32, with the
+        optional terms' inputs pooled from the same tiles
+        (predictor.py:387-410)."""
         feats_q = pool_tiles(q_tiles, layout)
         feats_k = pool_tiles(k_tiles, layout)
-        return self.layers[layer](feats_q, feats_k, heads)
+        extra = {}
+        if self.count_term:
+            extra['log_count'] = log_tile_counts(layout)
+        if self.second_order_rank:
+            extra['sq_q'] = pool_tiles(q_tiles, layout, SECOND_RAW)
+            extra['var_k'] = pool_tiles(k_tiles, layout, SECOND_CENTRAL)
+        return self.layers[layer](feats_q, feats_k, heads, **extra)
+
+
+def log_tile_counts(layout: tiling.TileLayout) -> torch.Tensor:
+    """[n_tiles] fp32 log of each tile's real rows, clamped to >= 1: the
+    count term's input (attention.py:278-280)."""
+    return torch.log(layout.valid_count.clamp(min=1).to(torch.float32))

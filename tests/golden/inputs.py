@@ -148,3 +148,48 @@ TEACHER = dict(text=130, grid=(4, 12, 20), seq_len=1100, heads=4, dim=128,
 # reaches well past the diagonal, temperatures of the transport loss.
 LOSSES = dict(heads=3, rows=[0, 3, 7, 12, 19], ratio=0.5, seed=93,
               temperatures=[0.15, 0.5, 1e-4])
+
+
+# The predictor's optional score terms: a head subset out of order, a
+# rank-8 second-order head and the count term, over seeded pooled features
+# of 37 query and 41 key tiles (some key tiles partly or wholly empty).
+PREDICTOR_TERMS = dict(heads=4, dim=128, rank=8, n_q=37, n_k=41, seed=61,
+                       sub_heads=[2, 0, 3])
+
+
+def predictor_term_inputs(spec):
+    """Seeded parameters and pooled inputs of the optional-terms case."""
+    gen = torch.Generator().manual_seed(spec['seed'])
+    heads, dim, rank = spec['heads'], spec['dim'], spec['rank']
+    sub = torch.tensor(spec['sub_heads'], dtype=torch.int64)
+    n_sub, n_q, n_k = sub.numel(), spec['n_q'], spec['n_k']
+
+    def normal(*shape, std=1.0):
+        return torch.randn(*shape, generator=gen) * std
+
+    counts = torch.randint(0, 129, (n_k,), generator=gen)
+    counts[:3] = torch.tensor([128, 0, 17])
+    return {
+        'heads': sub,
+        'proj_q': normal(heads, 3 * dim, dim, std=0.02),
+        'proj_k': normal(heads, 3 * dim, dim, std=0.02),
+        'so_q': normal(heads, dim, rank, std=0.05),
+        'so_k': normal(heads, dim, rank, std=0.05),
+        'count_gain': 1.0 + normal(heads, std=0.3),
+        'feats_q': normal(n_sub, n_q, 3 * dim),
+        'feats_k': normal(n_sub, n_k, 3 * dim),
+        'sq_q': normal(n_sub, n_q, dim).square(),
+        'var_k': normal(n_sub, n_k, dim).square() * 0.5,
+        'log_count': torch.log(counts.clamp(min=1).float()),
+        'probe': normal(n_sub, n_q, n_k),
+    }
+
+
+def predictor_term_moments(spec):
+    """Seeded PSD moments [2, D, D] (two heads) of non-negative features
+    (the first rank deficient on purpose: 96 samples of 128 features)."""
+    gen = torch.Generator().manual_seed(spec['seed'] + 1)
+    heads, dim = 2, spec['dim']
+    u = torch.randn(heads, 96, dim, generator=gen).square()
+    v = torch.randn(heads, 160, dim, generator=gen).square()
+    return (u.transpose(1, 2) @ u / 96.0, v.transpose(1, 2) @ v / 160.0)
