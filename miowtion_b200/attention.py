@@ -439,9 +439,6 @@ class SparseStudent:
             raise RuntimeError(
                 f'SparseStudent needs the B200 block-sparse kernels '
                 f'({reason}); refusing to fall back silently')
-        if clip.config.budget_rule != 'topk':
-            raise NotImplementedError("only the 'topk' budget rule has a "
-                                      'B200 kernel')
         if clip.config.fused_compensation:
             raise NotImplementedError(
                 'fused_compensation is the INT8 Sol kernel (an external '
@@ -487,6 +484,7 @@ class SparseStudent:
         """Sparse attention of some heads of one group, scattered to out."""
         second = bool(self.predictor.second_order_rank)
         if (not self.clip.config.compensated and not second
+                and self.clip.config.budget_rule == 'topk'
                 and kernels.packed_supported(tile_layout)):
             self._attend_packed(q, k, v, layer_index, tile_layout, heads, out)
             return
@@ -505,9 +503,7 @@ class SparseStudent:
                 **_extra_features(self.predictor, tile_layout, sq_q, var_k))
             ev.stop(t)
             t = ev.start('topk')
-            lists = veda_mask.select_block_lists(
-                logits[:, :tile_layout.n_video_tiles], tile_layout,
-                self.clip.blocks(tile_layout))
+            lists = self._block_lists(logits, tile_layout)
             ev.stop(t)
         t = ev.start('attention')
         if self.clip.config.compensated:
@@ -525,6 +521,25 @@ class SparseStudent:
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
         ev.stop(t)
         self.last_lists = lists
+
+    def _block_lists(self, logits: torch.Tensor,
+                     tile_layout: tiling.TileLayout,
+                     want_mask: bool = False) -> veda_mask.BlockLists:
+        """Lists of the logits under `config.budget_rule`: 'topk' in one
+        selection launch; 'threshold' through its Selection, the block
+        mask and the mask's lists (attention.py:764-770)."""
+        scores = logits[:, :tile_layout.n_video_tiles]
+        blocks = self.clip.blocks(tile_layout)
+        if self.clip.config.budget_rule == 'topk':
+            return veda_mask.select_block_lists(scores, tile_layout, blocks,
+                                               want_mask=want_mask)
+        selection = veda_mask.select_video_blocks(scores, tile_layout,
+                                                  blocks, rule='threshold')
+        block_mask = veda_mask.dense_block_mask(selection, tile_layout)
+        lists = kernels.index_lists_from_mask(block_mask, tile_layout,
+                                              transpose=False)
+        lists.mask = block_mask
+        return lists
 
     def _attend_packed(self, q, k, v, layer_index: int,
                        tile_layout: tiling.TileLayout, heads: torch.Tensor,
@@ -584,9 +599,8 @@ class SparseStudent:
                     feats_q, feats_k, heads + self.head_offset,
                     **_extra_features(self.predictor, tile_layout, sq_q,
                                       var_k))
-                lists = veda_mask.select_block_lists(
-                    logits[:, :tile_layout.n_video_tiles], tile_layout,
-                    self.clip.blocks(tile_layout), want_mask=True)
+                lists = self._block_lists(logits, tile_layout,
+                                          want_mask=True)
                 t_lists = kernels.index_lists_from_mask(lists.mask,
                                                         tile_layout)
             parts.append(_SparseGroup.apply(q, k, v, q_tiles, k_tiles, heads,

@@ -6,8 +6,9 @@ exactly as the reference does; selection runs in one CUDA kernel
 (csrc/select.cu), which can also emit the block mask and the full/partial
 index lists directly, so the sparse path never materialises a Selection.
 
-Only the reference's default rule 'topk' is implemented on the device; the
-'threshold' rule (an ablation arm) raises NotImplementedError.
+The reference's default rule 'topk' runs entirely in that kernel; its
+'threshold' rule (an ablation arm) ranks candidates in it and sets each
+row's count with a per-head threshold in torch.
 """
 
 from __future__ import annotations
@@ -159,16 +160,103 @@ def _rows_arg(rows, layout, device):
     return rows, rows.numel()
 
 
+# [rows whose threshold count reached the widened cap, rows seen] of the
+# 'threshold' rule (mask.py:136-140); reading it synchronises the host.
+SATURATED = [0, 0]
+
+
+def threshold_allowed(sorted_scores: torch.Tensor, valid: torch.Tensor,
+                      mean_k: float, cap: int) -> torch.Tensor:
+    """Kept count per row [H', R] of the 'threshold' rule (mask.py:143-197).
+
+    Each row's candidates (descending, forced columns +inf) are
+    standardised over its valid, non-forced entries (sample variance, at
+    least 2 counted); the head's threshold is its round(mean_k * R)-th
+    largest standardised score over all rows, so the head spends the top-k
+    total unevenly across rows. A row keeps its candidates at or above the
+    threshold, at least 1.
+    """
+    counts = valid.sum(-1, keepdim=True).clamp(min=2).float()
+    x = torch.where(valid, sorted_scores.float(), 0.0)
+    forced = torch.isposinf(x)
+    x = torch.where(forced, 0.0, x)
+    n_stat = (counts - forced.sum(-1, keepdim=True)).clamp(min=2)
+    mean = x.sum(-1, keepdim=True) / n_stat
+    var = torch.where(valid & ~forced, (x - mean).square(), 0.0).sum(
+        -1, keepdim=True) / (n_stat - 1)
+    z = (sorted_scores.float() - mean) / var.sqrt().clamp(min=1e-12)
+    z = torch.where(valid, z, float('-inf'))
+    z = torch.where(forced, float('inf'), z)
+    heads, rows, width = z.shape
+    total = max(1, min(int(round(float(mean_k) * rows)), width * rows))
+    cut = z.reshape(heads, -1).topk(total, dim=-1).values[:, -1:]
+    allowed = (z >= cut[:, :, None]).sum(-1)
+    SATURATED[0] += int((allowed >= cap).sum())
+    SATURATED[1] += heads * rows
+    return allowed.clamp(min=1)
+
+
+def _select_threshold(scores, layout, blocks, rows, cap_mult):
+    """The 'threshold' rule: the selection kernel ranks each block's top
+    ceil(cap_mult * budget) candidates (at least the top-k width) in the
+    reference's order, and `threshold_allowed` sets each row's count."""
+    wide, widths = [], []
+    for b in blocks:
+        n_cols = b.stop - b.start
+        if b.budget.keeps_all:
+            wide.append(b)
+            widths.append(None)
+            continue
+        budget = b.budget.per_row(b.real_tokens, n_cols)
+        k_hi = split_budget(budget, n_cols)[1]
+        k_wide = min(n_cols, max(k_hi, math.ceil(cap_mult * budget)))
+        wide.append(ColumnBlock(b.start, b.stop, Budget(tiles=k_wide),
+                                b.real_tokens))
+        widths.append((k_wide, budget))
+    ranked = select_video_blocks(scores, layout, wide, rows)
+    rows_t = (torch.arange(layout.n_video_tiles, device=scores.device)
+              if rows is None else rows.to(device=scores.device,
+                                           dtype=torch.int64))
+    indices, keeps, off = [], [], 0
+    for b, w, b_wide in zip(blocks, widths, wide):
+        span = _selection_width([b_wide])
+        if w is None:
+            indices.append(ranked.index[..., off:off + span])
+            keeps.append(ranked.keep[..., off:off + span])
+            off += span
+            continue
+        k_wide, budget = w
+        idx = ranked.index[..., off:off + k_wide]
+        off += span
+        s = scores[:, :, b.start:b.stop].float().masked_fill(
+            ~layout.kv_ok[None, None, b.start:b.stop], float('-inf'))
+        own = (rows_t >= b.start) & (rows_t < b.stop)
+        col = (rows_t - b.start).clamp(0, b.stop - b.start - 1)
+        s[:, own, col[own]] = float('inf')
+        vals = s.gather(-1, idx - b.start)
+        live = vals > float('-inf')
+        allowed = threshold_allowed(vals, live, budget, k_wide)
+        keeps.append((torch.arange(k_wide, device=scores.device)
+                      < allowed[:, :, None]) & live)
+        indices.append(idx)
+    return Selection(torch.cat(indices, -1), torch.cat(keeps, -1))
+
+
 @torch.no_grad()
 def select_video_blocks(scores: torch.Tensor, layout: tiling.TileLayout,
                         blocks: list[ColumnBlock],
                         rows: torch.Tensor | None = None,
-                        rule: str = 'topk') -> Selection:
-    """Top-k over the video quadrant of `scores` (mask.py:200-285)."""
+                        rule: str = 'topk',
+                        cap_mult: float = 4.0) -> Selection:
+    """Top-k over the video quadrant of `scores` (mask.py:200-285); with
+    rule 'threshold' each row's count follows `threshold_allowed`, capped
+    at cap_mult times the block's mean budget."""
     if rule not in ('topk', 'threshold'):
         raise ValueError(f"rule must be 'topk' or 'threshold': {rule!r}")
-    if rule != 'topk':
-        raise NotImplementedError("the 'threshold' rule has no B200 kernel")
+    if rule == 'threshold':
+        _check_scores(scores, layout, layout.n_video_tiles if rows is None
+                      else rows.numel())
+        return _select_threshold(scores, layout, blocks, rows, cap_mult)
     rows_t, num_rows = _rows_arg(rows, layout, scores.device)
     scores = _check_scores(scores, layout, num_rows)
     heads = scores.shape[0]
