@@ -1,20 +1,22 @@
 """Benchmark of the Veda sparse-attention layer on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3]
     python bench.py --impl reference ...   # the reference algorithm on CPU
     python bench.py --config cfg5 ...      # the stage-2 training step
     python bench.py --only backward|heat   # one stage on one head group
 
 One step = one Veda attention layer forward over synthetic q, k, v already
 resident in HBM: permute + pool q/k/v, predictor logits, budgeted top-k
-lists, tcgen05 block-sparse attention, inverse permutation. With N > 1:
+lists, tcgen05 block-sparse attention, inverse permutation. The default
+workload is the H3-scale config (cfg3: 48 heads, two tile shapes, 1024
+text rows). With N > 1:
+  --parallel ulysses  (default) one clip, heads split over the ranks by an
+                      all-to-all from the sequence-sharded layout; strong
+                      scaling, the value is the time of one layer;
   --parallel clips    every rank runs the layer on its own clip (the
                       reference's one-clip-per-GPU data parallelism, no
                       collective on the data path; weak scaling, the value
-                      is ms per layer of the whole job); default for cfg2;
-  --parallel ulysses  one clip, heads split over the ranks by an all-to-all
-                      from the sequence-sharded layout (BASELINE configs 3
-                      and 4; strong scaling); default for cfg3 and cfg4.
+                      is ms per layer of the whole job).
 Prints one JSON line on rank 0.
 """
 
@@ -54,7 +56,6 @@ BLOCK_FLOPS = 4 * 128 * 128 * 128  # QK^T + PV of one 128x128 block, fwd
 CONFIGS = {
     'cfg2': dict(desc='1xB200 fwd, 24 heads, grid (20,32,56)=35840 tokens, '
                       'tile 2x8x8, 280x280 tiles, 28 key tiles/row (90%)',
-                 parallel='clips',
                  heads=24, seq_len=35840, used=35840, target=(0, (20, 32, 56)),
                  cond=None, shapes=[(2, 8, 8)], head_shape=[0] * 24,
                  target_ratio=0.1, ref_ratio=None, seed=1),
@@ -227,6 +228,11 @@ def cpu_baseline(cfg, budget_s=12.0, timed_steps=None):
     heads (heads are independent with equal per-head cost)."""
     from oracle import veda_oracle as vo
     import threadpoolctl
+    # Every host core, whatever OMP_NUM_THREADS the launcher set (torchrun
+    # sets 1): numpy's BLAS pool and torch's intra-op pool.
+    cores = os.cpu_count() or 1
+    threadpoolctl.threadpool_limits(cores)
+    torch.set_num_threads(cores)
     seq_len, used = cfg['seq_len'], cfg['used']
     gen = torch.Generator().manual_seed(1000 + cfg['seed'])
     pq = (torch.randn(cfg['heads'], 384, 128, generator=gen) * 0.02).numpy()
@@ -299,9 +305,11 @@ def main():
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=400)
     ap.add_argument('--warmup', type=int, default=5)
-    ap.add_argument('--config', default='cfg2', choices=sorted(CONFIGS))
+    ap.add_argument('--config', default='cfg3', choices=sorted(CONFIGS))
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-comparators', action='store_true',
+                    help='skip the same-box GPU comparators (N=1)')
     ap.add_argument('--only', choices=['backward', 'heat', 'compensation',
                                        'search'], default=None,
                     help='time one stage on head group 0 of the config '
@@ -320,9 +328,10 @@ def main():
     ap.add_argument('--reserve-sms', type=int, default=16,
                     help='ulysses: SMs the attention leaves to NCCL while '
                     'pieces overlap')
-    ap.add_argument('--parallel', choices=['clips', 'ulysses'], default=None,
-                    help='multi-GPU mode (default: clips for cfg2, ulysses '
-                         'for cfg3/cfg4)')
+    ap.add_argument('--parallel', choices=['clips', 'ulysses'],
+                    default='ulysses',
+                    help='multi-GPU mode: heads split over the ranks '
+                         '(ulysses) or one clip per rank (clips)')
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.impl == 'reference':
@@ -350,7 +359,7 @@ def main():
                                 timeout=datetime.timedelta(seconds=120))
 
     seq_len, heads = cfg['seq_len'], cfg['heads']
-    mode = args.parallel or cfg.get('parallel', 'ulysses')
+    mode = args.parallel
     heads_split = world > 1 and mode == 'ulysses'
     if heads_split and (heads % world or seq_len % world):
         raise SystemExit('heads and sequence must divide by the GPU count')
@@ -436,6 +445,8 @@ def main():
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
         dense = dense_comparison(cfg, q, k, v) if world == 1 else None
+        comp = (comparators(cfg, clip, plan, student, q, k, v)
+                if world == 1 and not args.no_comparators else None)
 
     vals = torch.tensor([ms, e2e_ms, stages.get('attention', 0.0),
                          float(blocks)], dtype=torch.float64, device=device)
@@ -469,9 +480,9 @@ def main():
                     'N(0,0.02))',
             'config': {'workload': f'{args.config}: {cfg["desc"]}',
                        'heads': heads, 'seq_len': seq_len, 'head_dim': 128,
-                       'parallelism': (f'ulysses-heads x{world}'
-                                       if heads_split else
-                                       f'clip per GPU x{world}'),
+                       'parallelism': (f'clip per GPU x{world}'
+                                       if mode == 'clips' else
+                                       f'ulysses-heads x{world}'),
                        'l2': 'inputs exceed L2 (q/k/v/tiles >> 126 MB)'},
             'effective_tflops': eff,
             'frac_of_peak': eff / peak,
@@ -503,6 +514,8 @@ def main():
                         'rows (no permutation, predictor or top-k), timed '
                         'with CUDA events; the sparse layer is the whole '
                         'Veda path'}
+        if comp is not None:
+            line['comparators'] = comp
         if world == 1 and not args.no_cpu_baseline:
             cpu_ms, n_heads, threads, _ = cpu_baseline(cfg)
             line['cpu_baseline'] = {
@@ -564,6 +577,176 @@ def dense_comparison(cfg, q, k, v, reps=3):
                 continue
         del qs, ks, vs
     return out
+
+
+REF_DIR = os.path.join(ROOT, 'baseline', '_ref')
+
+
+def reference_package():
+    """The reference's own package, installed unmodified (`pip install
+    --no-deps` of the reference project) under baseline/_ref, or None when
+    that install is absent."""
+    if not os.path.isdir(os.path.join(REF_DIR, 'miowtion')):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    import importlib
+    return importlib.import_module('miowtion')
+
+
+def _timed_ms(fn, reps):
+    fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def _rel_err(got, want):
+    got, want = got.float(), want.float()
+    return float((got - want).abs().max() / want.abs().max().clamp(min=1e-30))
+
+
+def comparators(cfg, clip, plan, student, q, k, v, reps=3):
+    """Same-box GPU comparators for head group 0 of the layer: this
+    library's kernels beside the reference's own GPU kernels, run
+    unmodified from baseline/_ref through their public functions
+    (kernels/tile_gather_triton.py:156-224, kernels/block_heat_triton.py:
+    140-173), torch flex_attention with a BlockMask of the same lists
+    through the reference's benchmark backend (kernels/bench.py:241-262),
+    and FA4 SM100 where it can be imported. ms per call, CUDA events,
+    after one warm-up call; each entry that cannot run says why. Every
+    pair is checked to compute the same thing (max relative difference)."""
+    from miowtion_b200 import heatmap
+    device = q.device
+    res: dict = {}
+    group = plan.head_groups(0, device)[0]
+    tl = clip.get(group.shape)
+    heads = group.heads
+    res['workload'] = (f'head group 0 ({heads.numel()} heads, tile '
+                       f'{group.shape.t}x{group.shape.h}x{group.shape.w}, '
+                       f'{tl.n_tiles} tiles)')
+    with torch.no_grad():
+        qt, fq = tiling.gather_and_pool(q, tl, heads)
+        kt, fk = tiling.gather_and_pool(k, tl, heads)
+        vt = tiling.gather_tiles(v, tl, heads)
+        logits = student.predictor.layers[0](fq, fk, heads)
+        lists = veda_mask.select_block_lists(
+            logits[:, :tl.n_video_tiles], tl, clip.blocks(tl),
+            want_mask=True)
+        ours = {
+            'gather_pool_q_k_gather_v': _timed_ms(lambda: (
+                tiling.gather_and_pool(q, tl, heads),
+                tiling.gather_and_pool(k, tl, heads),
+                tiling.gather_tiles(v, tl, heads)), reps),
+            'packed_pool_q_images_k_v': _timed_ms(lambda: (
+                tiling.pool_features(q, tl, heads),
+                tiling.gather_images(k, tl, heads, pool=True),
+                tiling.gather_images(v, tl, heads)), reps)}
+        buf = torch.zeros(q.shape[0] + 1, q.shape[1], 128,
+                          dtype=q.dtype, device=device)
+        ours['scatter'] = _timed_ms(
+            lambda: tiling.scatter_tiles_(buf, qt, tl, heads), reps)
+        ot = kernels.block_sparse_attention_lists(qt, kt, vt, lists, tl)
+        ours['block_sparse_attention'] = _timed_ms(
+            lambda: kernels.block_sparse_attention_lists(qt, kt, vt, lists,
+                                                         tl), reps)
+        _, lse = kernels.dense_attention(q, k, v, 128 ** -0.5, True,
+                                         used=cfg['used'])
+        lse_t = tiling.gather_lse(lse, tl, heads)
+        del lse
+        rows = torch.arange(tl.n_tiles, device=device)
+        heat = heatmap.teacher_heat(qt, kt, lse_t, tl, rows, 'sum')
+        ours['teacher_heat_sum_all_query_tiles'] = _timed_ms(
+            lambda: heatmap.teacher_heat(qt, kt, lse_t, tl, rows, 'sum'), 1)
+        res['b200_ms'] = ours
+
+        ref = None
+        try:
+            ref = reference_package()
+        except Exception as exc:  # pylint: disable=broad-except
+            res['reference_triton'] = f'unavailable: import failed ({exc})'
+        if ref is None and 'reference_triton' not in res:
+            res['reference_triton'] = ('unavailable: the reference is not '
+                                       'installed under baseline/_ref')
+        if ref is not None:
+            theirs, same = {}, {}
+            try:
+                from miowtion.kernels import block_heat_triton as rbh
+                from miowtion.kernels import tile_gather_triton as rtg
+                from miowtion.veda import tiling as rtiling
+                spans = []
+                if cfg['cond'] is not None:
+                    spans.append(rtiling.TiledSpan(
+                        cfg['cond'][0], tuple(cfg['cond'][1]),
+                        rtiling.TileShape(2, 8, 8)))
+                spans.append(rtiling.TiledSpan(
+                    cfg['target'][0], tuple(cfg['target'][1]),
+                    rtiling.TileShape(group.shape.t, group.shape.h,
+                                      group.shape.w)))
+                rl = rtiling.build_tile_layout(spans, cfg['used'],
+                                               q.shape[0], device)
+                rqt, rfq = rtg.gather_and_pool(q, rl, heads)
+                same['gather_tiles_equal'] = bool(torch.equal(rqt, qt))
+                same['pool_rel_diff'] = _rel_err(rfq, fq)
+                theirs['gather_pool_q_k_gather_v'] = _timed_ms(lambda: (
+                    rtg.gather_and_pool(q, rl, heads),
+                    rtg.gather_and_pool(k, rl, heads),
+                    rtg.gather_tiles(v, rl, heads)), reps)
+                rbuf = torch.zeros_like(buf)
+                rtg.scatter_tiles_(rbuf, qt, rl, heads)
+                tiling.scatter_tiles_(buf, qt, tl, heads)
+                same['scatter_equal'] = bool(torch.equal(rbuf, buf))
+                theirs['scatter'] = _timed_ms(
+                    lambda: rtg.scatter_tiles_(rbuf, qt, rl, heads), reps)
+                rheat = rbh.teacher_heat(qt, kt, lse_t, rl, rows, 'sum')
+                same['teacher_heat_rel_diff'] = _rel_err(heat, rheat)
+                theirs['teacher_heat_sum_all_query_tiles'] = _timed_ms(
+                    lambda: rbh.teacher_heat(qt, kt, lse_t, rl, rows,
+                                             'sum'), 1)
+                del rbuf, rqt, rfq, rheat
+            except Exception as exc:  # pylint: disable=broad-except
+                theirs['error'] = f'{type(exc).__name__}: {exc}'[:300]
+            res['reference_triton_ms'] = theirs
+            res['agreement'] = same
+            try:
+                from miowtion.kernels import bench as rbench
+                flex = rbench._Flex(qt, kt, vt)  # pylint: disable=protected-access
+                meta = flex.prepare(lists.mask.bool())
+                fo = flex.run(meta)
+                res['flex_attention_ms'] = _timed_ms(lambda: flex.run(meta),
+                                                     reps)
+                # flex attends every row of a kept tile (the reference
+                # backend's BlockMask has no partial tiles), so compare the
+                # (query tile, head) pairs that are full and keep only full
+                # key tiles.
+                res['flex_note'] = (
+                    'torch.compile(flex_attention) with the same kept '
+                    'blocks as full blocks (the reference backend, '
+                    'kernels/bench.py:241-262); tile-ordered q, k, v')
+                mask = lists.mask.bool()
+                partial = (mask & ~tl.full_tile[None, None, :]).any(-1)
+                ok = (tl.full_tile[:, None] & ~partial.T).repeat_interleave(
+                    128, 0)[:, :, None]
+                diff = ((fo.float() - ot.float()).abs() * ok).max()
+                res['flex_rel_diff_full_tiles'] = float(
+                    diff / (ot.float().abs() * ok).max().clamp(min=1e-30))
+                del flex, meta, fo
+            except Exception as exc:  # pylint: disable=broad-except
+                res['flex_attention_ms'] = (
+                    f'unavailable: {type(exc).__name__}: {exc}'[:300])
+        import importlib.util
+        if importlib.util.find_spec('flash_attn') is None or \
+                importlib.util.find_spec('flash_attn.cute') is None:
+            res['fa4_sm100'] = ('not installable on this box: flash-attn-4 '
+                                '(flash_attn.cute @ d15f1531) is not in the '
+                                'image and there is no network')
+    return res
 
 
 def run_stage(args, cfg):

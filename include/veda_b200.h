@@ -155,7 +155,8 @@ int veda_gather_lse(const float* lse, int64_t l_stride_s, int64_t l_stride_h,
 
 /* ---- a4: predictor logits ---------------------------------------------- */
 
-/* Bytes of workspace veda_predict_logits needs. */
+/* Bytes of workspace veda_predict_logits needs; -1 for sizes it rejects
+ * (n_heads outside [1, 65535], tile counts negative or above 2^31). */
 int64_t veda_predict_workspace(int32_t n_heads, int64_t n_q, int64_t n_k);
 
 /* Replaces miowtion/veda/predictor.py:251-255 + :299-338 (LayerPredictor
@@ -179,8 +180,11 @@ int veda_predict_logits(const float* feats_q, const float* feats_k,
  * VEDA_PREDICT_NOALLOC_MAX_FLOATS floats (32 MiB), which every GPU that loads
  * the library holds until exit; calls needing more (n_heads * (n_q + n_k) *
  * 128 floats) are rejected with VEDA_ERR_INVALID. The first call on a device
- * looks the array's device address up (cudaGetSymbolAddress); make that
- * first call before any stream capture. Every call shares the one array, so
+ * looks the array's device address up (cudaGetSymbolAddress) and caches it
+ * for the life of the process; make that first call before any stream
+ * capture, and do not use the entry point across a cudaDeviceReset (the
+ * library's module is then loaded again and the cached address is stale).
+ * Every call shares the one array, so
  * calls that overlap on the GPU (e.g. on two streams) race; serialise them.
  * Nothing carries over between calls: every scratch element read is first
  * written by the same call. Calls no cudaMalloc, cudaFree or allocating

@@ -421,6 +421,26 @@ class TeacherCollector:
         return out
 
 
+def _rule_lists(scores: torch.Tensor, tile_layout: tiling.TileLayout,
+                clip: ClipTiling, want_mask: bool = False
+                ) -> veda_mask.BlockLists:
+    """Block lists of the video rows' scores [H', n_video, n] under
+    `clip.config.budget_rule`: 'topk' in one selection launch; 'threshold'
+    through its Selection, the block mask and the mask's lists
+    (attention.py:764-770 and, for the oracle student, :574-580)."""
+    blocks = clip.blocks(tile_layout)
+    if clip.config.budget_rule == 'topk':
+        return veda_mask.select_block_lists(scores, tile_layout, blocks,
+                                           want_mask=want_mask)
+    selection = veda_mask.select_video_blocks(scores, tile_layout, blocks,
+                                              rule='threshold')
+    block_mask = veda_mask.dense_block_mask(selection, tile_layout)
+    lists = kernels.index_lists_from_mask(block_mask, tile_layout,
+                                          transpose=False)
+    lists.mask = block_mask
+    return lists
+
+
 class SparseStudent:
     """Stage-2 / evaluation attention: predictor-masked block sparsity
     (attention.py:692-794)."""
@@ -528,18 +548,8 @@ class SparseStudent:
         """Lists of the logits under `config.budget_rule`: 'topk' in one
         selection launch; 'threshold' through its Selection, the block
         mask and the mask's lists (attention.py:764-770)."""
-        scores = logits[:, :tile_layout.n_video_tiles]
-        blocks = self.clip.blocks(tile_layout)
-        if self.clip.config.budget_rule == 'topk':
-            return veda_mask.select_block_lists(scores, tile_layout, blocks,
-                                               want_mask=want_mask)
-        selection = veda_mask.select_video_blocks(scores, tile_layout,
-                                                  blocks, rule='threshold')
-        block_mask = veda_mask.dense_block_mask(selection, tile_layout)
-        lists = kernels.index_lists_from_mask(block_mask, tile_layout,
-                                              transpose=False)
-        lists.mask = block_mask
-        return lists
+        return _rule_lists(logits[:, :tile_layout.n_video_tiles],
+                           tile_layout, self.clip, want_mask)
 
     def _attend_packed(self, q, k, v, layer_index: int,
                        tile_layout: tiling.TileLayout, heads: torch.Tensor,
@@ -684,9 +694,6 @@ class OracleStudent:
             raise RuntimeError(
                 f'OracleStudent needs the B200 block-sparse kernels '
                 f'({reason}); refusing to fall back silently')
-        if clip.config.budget_rule != 'topk':
-            raise NotImplementedError("only the 'topk' budget rule has a "
-                                      'B200 kernel')
         self.clip = clip
         self.plan = plan
         self.target = target
@@ -723,8 +730,8 @@ class OracleStudent:
         if self.target == 'mean':
             counts = tile_layout.valid_count.clamp(min=1).to(heat.dtype)
             heat = heat / counts[None, None, :]
-        lists = veda_mask.select_block_lists(heat, tile_layout,
-                                             self.clip.blocks(tile_layout))
+        lists = _rule_lists(heat, tile_layout, self.clip, want_mask=True)
         o_tiles = kernels.block_sparse_attention_lists(
             q_tiles, k_tiles, v_tiles, lists, tile_layout)
         tiling.scatter_rows_(out, o_tiles, tile_layout, heads)
+        self.last_lists = lists

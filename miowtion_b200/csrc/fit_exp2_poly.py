@@ -66,9 +66,13 @@ def f32_horner(coef: np.ndarray, f: np.ndarray) -> np.ndarray:
     return acc
 
 
+# Lower clamp of the argument in exp2_poly.cuh (masked keys give ~0).
+CLAMP = -125.0
+
+
 def exp2_emulated(x: np.ndarray, coef: np.ndarray) -> np.ndarray:
     """The kernel's evaluation, in float32: clamp, round, poly, exponent."""
-    x = np.maximum(x.astype(np.float32), np.float32(-127.0))
+    x = np.maximum(x.astype(np.float32), np.float32(CLAMP))
     n = np.rint(x).astype(np.float32)
     f = (x - n).astype(np.float32)
     p = f32_horner(coef, f)

@@ -202,8 +202,18 @@ __global__ void __launch_bounds__(256)
 
 using namespace veda;
 
+// Tile counts above this are rejected before any size arithmetic, so that
+// n_heads (<= 65535) x (n_q + n_k) x 128 x 4 bytes stays far below 2^63.
+constexpr int64_t kMaxPredictTiles = int64_t{1} << 31;
+
+static bool predict_sizes_ok(int32_t n_heads, int64_t n_q, int64_t n_k) {
+  return n_heads >= 1 && n_heads <= 65535 && n_q >= 0 && n_k >= 0 &&
+         n_q <= kMaxPredictTiles && n_k <= kMaxPredictTiles;
+}
+
 extern "C" int64_t veda_predict_workspace(int32_t n_heads, int64_t n_q,
                                           int64_t n_k) {
+  if (!predict_sizes_ok(n_heads, n_q, n_k)) return -1;
   return static_cast<int64_t>(n_heads) * (n_q + n_k) * kHeadDim *
          static_cast<int64_t>(sizeof(float));
 }
@@ -218,6 +228,8 @@ extern "C" int veda_predict_logits(const float* feats_q, const float* feats_k,
                "all tensors are required");
   VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
   VEDA_REQUIRE(n_q >= 0 && n_k >= 0, "bad tile counts");
+  VEDA_REQUIRE(n_q <= kMaxPredictTiles && n_k <= kMaxPredictTiles,
+               "tile counts above 2^31");
   VEDA_REQUIRE(workspace != nullptr &&
                    workspace_bytes >= veda_predict_workspace(n_heads, n_q, n_k),
                "workspace is smaller than veda_predict_workspace()");
@@ -256,7 +268,10 @@ extern "C" int veda_predict_logits(const float* feats_q, const float* feats_k,
 // which every GPU that loads the library holds until the process exits. The
 // array's name in host code is only a host-side stand-in: the device address
 // is obtained once per device with cudaGetSymbolAddress (with that device
-// current) on the first call made on it, and passed to the kernels.
+// current) on the first call made on it, and passed to the kernels. The
+// address is cached for the life of the process, so the entry point must not
+// be used across a cudaDeviceReset (or any other teardown of the device's
+// primary context), after which the module loads again at a new address.
 // ---------------------------------------------------------------------------
 
 namespace veda {
@@ -296,6 +311,9 @@ extern "C" int veda_predict_logits_noalloc(
     int64_t n_k, float* logits, void* stream) {
   VEDA_REQUIRE(n_heads >= 1 && n_heads <= 65535, "bad number of heads");
   VEDA_REQUIRE(n_q >= 0 && n_k >= 0, "bad tile counts");
+  // Bounded first, so the product below cannot wrap.
+  VEDA_REQUIRE(n_q <= kMaxPredictTiles && n_k <= kMaxPredictTiles,
+               "tile counts above 2^31");
   const int64_t need = static_cast<int64_t>(n_heads) * (n_q + n_k) * kHeadDim;
   if (need > kNoAllocScratchFloats) {
     char buf[256];

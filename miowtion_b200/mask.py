@@ -231,8 +231,13 @@ def _select_threshold(scores, layout, blocks, rows, cap_mult):
         s = scores[:, :, b.start:b.stop].float().masked_fill(
             ~layout.kv_ok[None, None, b.start:b.stop], float('-inf'))
         own = (rows_t >= b.start) & (rows_t < b.stop)
+        # Each row's own column to +inf when the row lies in this block,
+        # without a boolean index (which would wait on the host for its
+        # count): gather the diagonal entry, replace it, scatter it back.
         col = (rows_t - b.start).clamp(0, b.stop - b.start - 1)
-        s[:, own, col[own]] = float('inf')
+        col = col[None, :, None].expand(s.shape[0], -1, 1)
+        s.scatter_(-1, col, torch.where(own[None, :, None], float('inf'),
+                                        s.gather(-1, col)))
         vals = s.gather(-1, idx - b.start)
         live = vals > float('-inf')
         allowed = threshold_allowed(vals, live, budget, k_wide)

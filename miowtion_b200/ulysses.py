@@ -196,8 +196,13 @@ class UlyssesSparseStudent:
                 bufs.append((send, recv))
             inputs[j] = (bufs, works)
 
+        # Stage timers (bench): the exchanges, packing included, on the
+        # launching stream. With several pieces they overlap the attention.
+        ev = (self.student.events if self.student is not None
+              else veda_attention._NO_EVENTS)  # pylint: disable=protected-access
         out = torch.empty_like(q)
         outputs = []
+        t = ev.start('exchange')
         post_inputs(0)
         for j, (start, stop) in enumerate(bounds):
             if j + 1 < len(bounds):
@@ -205,6 +210,8 @@ class UlyssesSparseStudent:
             bufs, works = inputs.pop(j)
             for w in works:
                 w.wait()
+            if j == 0:
+                ev.stop(t)
             c = stop - start
             qj, kj, vj = (recv.view(world * rows, c, dim)
                           for _, recv in bufs)
@@ -215,6 +222,8 @@ class UlyssesSparseStudent:
                 student.events = self.student.events
             result = student(qj, kj, vj, layer_index)
             back = torch.empty_like(result).view(world, rows, c, dim)
+            if j + 1 == len(bounds):
+                t = ev.start('exchange')
             work = dist.all_to_all_single(
                 back, result.view(world, rows, c, dim), group=self.group,
                 async_op=True)
@@ -226,4 +235,5 @@ class UlyssesSparseStudent:
             else:
                 out.view(rows, world, per, dim)[:, :, start:stop] = (
                     back.transpose(0, 1))
+        ev.stop(t)
         return out

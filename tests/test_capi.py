@@ -45,6 +45,14 @@ def test_host_side_validation_needs_no_gpu(lib):
     with pytest.raises(ValueError, match='target span'):
         _lib.check(rc, 'veda_build_layout')
     assert lib.veda_predict_workspace(2, 10, 12) == 2 * 22 * 128 * 4
+    # Sizes whose byte count would not fit in 64 bits are refused, not
+    # wrapped into a small (or negative) size.
+    assert lib.veda_predict_workspace(2, 1 << 60, 12) == -1
+    assert lib.veda_predict_workspace(0, 10, 12) == -1
+    rc = lib.veda_predict_logits_noalloc(None, None, None, None, None, 2,
+                                         1 << 60, 1 << 60, None, None)
+    assert rc == _lib.VEDA_ERR_INVALID
+    assert '2^31' in _lib.last_error()
 
 
 def test_column_block_struct_layout():

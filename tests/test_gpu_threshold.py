@@ -91,3 +91,34 @@ def test_student_with_threshold_rule():
     kept = want[:, :lay.n_video_tiles, :lay.n_video_tiles].sum(-1)
     assert kept.float().std() > 0, 'the rule should keep uneven counts'
     assert torch.isfinite(out[:used].float()).all()
+
+
+def test_oracle_student_with_threshold_rule():
+    """OracleStudent passes the clip's budget rule to the selection, as the
+    reference does (attention.py:574-580): under 'threshold' its block mask
+    is the threshold selection of the true block mass of the video rows."""
+    from miowtion_b200 import heatmap
+    heads, seq_len, text, grid = 3, 1100, 130, (4, 12, 20)
+    used = text + grid[0] * grid[1] * grid[2]
+    q, k, v = (x.to(DEV) for x in inputs.qkv(seq_len, heads, 128, 87,
+                                             torch.bfloat16))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=0.4), budget_rule='threshold')
+    clip = veda_attention.ClipTiling(veda_attention.PackedLayout(
+        seq_len, used, (veda_attention.VideoSpan(text, grid),)), config, DEV)
+    plan = veda_plan.TilePlan('thr', grid, [tiling.TileShape(2, 8, 8)],
+                              [[0] * heads])
+    student = veda_attention.OracleStudent(clip, plan, 'mass')
+    out = student(q, k, v, 0)
+    lay = clip.get(tiling.TileShape(2, 8, 8))
+    all_heads = torch.arange(heads, device=DEV)
+    qt, kt, vt = (tiling.gather_tiles(t, lay, all_heads) for t in (q, k, v))
+    _, _, heat = heatmap.fused_dense_heat(qt, kt, vt, lay, 'sum')
+    sel = veda_mask.select_video_blocks(
+        heat[:, :lay.n_video_tiles], lay, clip.blocks(lay), rule='threshold')
+    want = veda_mask.dense_block_mask(sel, lay)
+    torch.cuda.synchronize()
+    assert torch.equal(student.last_lists.mask.bool(), want)
+    kept = want[:, :lay.n_video_tiles, :lay.n_video_tiles].sum(-1)
+    assert kept.float().std() > 0, 'the rule should keep uneven counts'
+    assert torch.isfinite(out[:used].float()).all()
