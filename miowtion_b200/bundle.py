@@ -1,34 +1,37 @@
-"""Predictor bundle: one safetensors file with the live predictor weights and
-every tile plan the predictor was trained against.
+"""Predictor bundle: one safetensors file holding the predictor's weights and
+the tile plans it was trained against.
 
-The on-disk format is the reference's `miowtion-veda-predictor-v1`
-(`miowtion/veda/bundle.py:1-330`), so a bundle exported by the reference
-loads here and one written here loads there:
+File format `miowtion-veda-predictor-v1` (the reference's exporter,
+miowtion/veda/bundle.py), so files move both ways between the two:
 
-- tensors: the predictor's state dict with bare keys (`layers.{i}.proj_q`,
-  `layers.{i}.proj_k`), stored as float32, bfloat16 or float8_e4m3fn;
-- an fp8 tensor `name` carries `name.__scale`, fp32 [H]: per head, amax
-  divided by 448 (the largest finite e4m3 value), at least the smallest
-  normal float32, with weight ~= value * scale;
-- `__metadata__` (str -> str): `format`, `num_layers`, `num_heads`,
-  `head_dim`, `dtype`, `tile_conditions` ('true' / 'false'), `source`,
-  `source_weights`, `step`, `second_order_rank`, `count_term` ('1' / '0'),
-  `plans` (one JSON object, geometry name -> plan JSON, in name order),
-  `target_budget_kind` / `target_budget_value` ('ratio' or 'tiles', the
-  value as Python's repr of a float), optionally `ref_budget_kind` /
-  `ref_budget_value`, and the legacy `keep_ratio` for ratio budgets.
+Tensors. The predictor's state dict under bare keys (`layers.{i}.proj_q`,
+`layers.{i}.proj_k`, ...), all stored in one dtype: float32, bfloat16 or
+float8_e4m3fn. A float8 tensor `name` is stored as e4m3 values of
+`weight / scale` and travels with `name.__scale`, float32 [H]: per leading
+index (head), max |weight| / 448 (448 = largest finite e4m3), never below
+the smallest normal float32.
 
-Loading is strict: every stored tensor must land on a parameter of the
-predictor the metadata describes. fp8 and bf16 bundles come back as bf16
-parameters (the scoring kernel reads them as fp32 whatever they are stored
-in); float32 bundles stay float32.
+String metadata. `format`; `num_layers`, `num_heads`, `head_dim`,
+`second_order_rank` (decimal integers); `count_term` ('1' / '0');
+`tile_conditions` ('true' / 'false'); `dtype` (the storage dtype's name;
+missing in old files, which are float32); `source`, `source_weights`,
+`step`; `plans`, one JSON object mapping each geometry name (sorted) to its
+plan's JSON; the budgets as `<p>_budget_kind` ('ratio' / 'tiles') and
+`<p>_budget_value` (Python repr of a float) for p = 'target' and, with
+tiled conditioning references, p = 'ref'; `keep_ratio` repeats a ratio
+target budget (older readers know only that key).
+
+Loading is strict: the tensors must fill exactly the parameters of the
+predictor the metadata describes. float8 and bfloat16 files load as
+bfloat16 parameters, float32 files as float32 (the scoring kernels read
+fp32 whatever the parameter dtype).
 """
 
 from __future__ import annotations
 
 import dataclasses
 import json
-from collections.abc import Sequence
+from collections.abc import Mapping, Sequence
 
 import torch
 from safetensors import safe_open
@@ -44,35 +47,93 @@ FORMAT = 'miowtion-veda-predictor-v1'
 
 DTYPES = {'float32': torch.float32, 'bfloat16': torch.bfloat16,
           'float8_e4m3fn': torch.float8_e4m3fn}
+_DTYPE_NAMES = {dt: name for name, dt in DTYPES.items()}
 
-_PREFIX = 'predictor.'
-_SCALE_SUFFIX = '.__scale'
-_E4M3_MAX = 448.0
-# A bundle without a `dtype` key predates it and holds float32 tensors.
-_LEGACY_DTYPE = 'float32'
-
-
-def _quantize_fp8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """[H, ...] weights -> (e4m3 values, fp32 per-head scale) with
-    weight ~= values * scale (bundle.py:69-85)."""
-    w = weight.float()
-    reduce_dims = tuple(range(1, w.dim()))
-    scale = (w.abs().amax(dim=reduce_dims) / _E4M3_MAX).clamp(
-        min=torch.finfo(torch.float32).tiny)
-    shaped = scale.view(-1, *([1] * len(reduce_dims)))
-    return (w / shaped).to(torch.float8_e4m3fn).contiguous(), \
-        scale.contiguous()
+_TRAINER_PREFIX = 'predictor.'  # how a training checkpoint names them
+_SCALE = '.__scale'
+_E4M3_LARGEST = 448.0
 
 
-def _dequantize_fp8(values: torch.Tensor, scale: torch.Tensor,
-                    dtype: torch.dtype) -> torch.Tensor:
-    shaped = scale.view(-1, *([1] * (values.dim() - 1)))
-    return (values.float() * shaped).to(dtype)
+# -- tensor codecs -------------------------------------------------------
 
+def _per_head(scale: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """[H] -> broadcastable against [H, ...]."""
+    return scale.reshape((-1,) + (1,) * (like.dim() - 1))
+
+
+def _encode(weights: Mapping[str, torch.Tensor],
+            dtype: torch.dtype) -> dict[str, torch.Tensor]:
+    """Parameters -> the tensors stored for them in `dtype`."""
+    stored = {}
+    for name, weight in weights.items():
+        w = weight.detach()
+        if dtype is not torch.float8_e4m3fn:
+            stored[name] = w.to(dtype).contiguous()
+            continue
+        w = w.float()
+        amax = w.abs().flatten(1).amax(1) if w.dim() > 1 else w.abs()
+        scale = (amax / _E4M3_LARGEST).clamp_min(
+            torch.finfo(torch.float32).tiny)
+        stored[name] = (w / _per_head(scale, w)).to(dtype).contiguous()
+        stored[name + _SCALE] = scale.contiguous()
+    return stored
+
+
+def _decode(stored: Mapping[str, torch.Tensor], dtype: torch.dtype,
+            where: str) -> tuple[dict[str, torch.Tensor], torch.dtype]:
+    """Stored tensors -> (parameters, the dtype they load as)."""
+    if dtype is not torch.float8_e4m3fn:
+        return dict(stored), dtype
+    params = {}
+    missing = []
+    for name, values in stored.items():
+        if name.endswith(_SCALE):
+            continue
+        scale = stored.get(name + _SCALE)
+        if scale is None:
+            missing.append(name)
+            continue
+        params[name] = (values.float() * _per_head(scale, values)).to(
+            torch.bfloat16)
+    if missing:
+        raise ValueError(f'{where}: fp8 tensors without a {_SCALE} scale: '
+                         f'{sorted(missing)}')
+    return params, torch.bfloat16
+
+
+# -- budgets in the metadata ---------------------------------------------
+
+def _budget_fields(which: str, ratio: float | None,
+                   tiles: float | None) -> dict[str, str]:
+    given = [(kind, val) for kind, val in (('ratio', ratio),
+                                           ('tiles', tiles))
+             if val is not None]
+    if len(given) != 1:
+        raise ValueError(f'set exactly one of {which}_ratio / '
+                         f'{which}_tiles')
+    kind, value = given[0]
+    veda_mask.Budget(**{kind: value})  # rejects out-of-range values
+    return {f'{which}_budget_kind': kind,
+            f'{which}_budget_value': repr(float(value))}
+
+
+def _budget_from(meta: Mapping[str, str],
+                 which: str) -> veda_mask.Budget | None:
+    kind = meta.get(f'{which}_budget_kind')
+    if kind is None:
+        return None
+    value = meta.get(f'{which}_budget_value')
+    if kind not in ('ratio', 'tiles') or value is None:
+        raise ValueError(f'invalid {which} budget metadata: kind={kind!r}, '
+                         f'value={value!r}')
+    return veda_mask.Budget(**{kind: float(value)})
+
+
+# -- the bundle ------------------------------------------------------------
 
 @dataclasses.dataclass
 class Bundle:
-    """A loaded bundle (bundle.py:96-120)."""
+    """A loaded bundle."""
 
     predictor: veda_predictor.TileScorePredictor
     plans: veda_plan.PlanTable
@@ -83,28 +144,15 @@ class Bundle:
     metadata: dict[str, str]
 
 
-def _budget_entries(prefix: str, ratio: float | None,
-                    tiles: float | None) -> dict[str, str]:
-    if (ratio is None) == (tiles is None):
-        raise ValueError(f'set exactly one of {prefix}_ratio / {prefix}_tiles')
-    kind, value = ('tiles', tiles) if tiles is not None else ('ratio', ratio)
-    veda_mask.Budget(**{kind: value})  # validates the value
-    return {f'{prefix}_budget_kind': kind,
-            f'{prefix}_budget_value': repr(float(value))}
-
-
-def _parse_budget(metadata: dict[str, str], prefix: str,
-                  legacy_ratio: str | None = None) -> veda_mask.Budget | None:
-    kind = metadata.get(f'{prefix}_budget_kind')
-    value = metadata.get(f'{prefix}_budget_value')
-    if kind is None:
-        if legacy_ratio is not None and legacy_ratio in metadata:
-            return veda_mask.Budget(ratio=float(metadata[legacy_ratio]))
-        return None
-    if kind not in ('ratio', 'tiles') or value is None:
-        raise ValueError(f'invalid {prefix} budget metadata: kind={kind!r}, '
-                         f'value={value!r}')
-    return veda_mask.Budget(**{kind: float(value)})
+def _bare_keys(weights: Mapping[str, torch.Tensor]
+               ) -> dict[str, torch.Tensor]:
+    """Drops the trainer's 'predictor.' prefix (all keys or none)."""
+    flags = {k.startswith(_TRAINER_PREFIX) for k in weights}
+    if len(flags) > 1:
+        raise ValueError('weights mix prefixed and bare keys')
+    if flags == {True}:
+        return {k[len(_TRAINER_PREFIX):]: v for k, v in weights.items()}
+    return dict(weights)
 
 
 def save(path: str, weights: dict[str, torch.Tensor],
@@ -117,155 +165,122 @@ def save(path: str, weights: dict[str, torch.Tensor],
          source_weights: str, step: int,
          dtype: torch.dtype = torch.bfloat16,
          second_order_rank: int = 0, count_term: bool = False) -> None:
-    """Writes a bundle (bundle.py:151-249); same arguments and errors.
+    """Writes a bundle. Exactly one target budget (`keep_ratio` or
+    `keep_tiles`); a reference budget exactly when `tile_conditions`.
 
     Raises:
-        ValueError: No weights, prefixed and bare keys mixed, an unsupported
-            storage dtype, no plans, a budget given twice or not at all, or a
-            reference budget without `tile_conditions` (and the converse).
+        ValueError: No weights, prefixed and bare keys mixed, a storage
+            dtype outside DTYPES, an empty plan table, or budgets that break
+            the rules above.
     """
     if not weights:
         raise ValueError('no predictor weights to save')
-    metadata_budgets = _budget_entries('target', keep_ratio, keep_tiles)
-    has_ref = ref_keep_ratio is not None or ref_keep_tiles is not None
-    if has_ref and not tile_conditions:
-        raise ValueError('a reference budget requires tile_conditions')
-    if tile_conditions and not has_ref:
-        raise ValueError('tile_conditions requires a reference budget')
-    if has_ref:
-        metadata_budgets.update(
-            _budget_entries('ref', ref_keep_ratio, ref_keep_tiles))
-    dtype_name = {v: k for k, v in DTYPES.items()}.get(dtype)
-    if dtype_name is None:
-        raise ValueError(f'unsupported storage dtype {dtype}; '
-                         f'expected one of {sorted(DTYPES)}')
-    n_prefixed = sum(k.startswith(_PREFIX) for k in weights)
-    if n_prefixed and n_prefixed != len(weights):
-        raise ValueError('weights mix prefixed and bare keys')
-    bare = {(k[len(_PREFIX):] if n_prefixed else k): v
-            for k, v in weights.items()}
-    tensors = {}
-    for key, value in bare.items():
-        if dtype is torch.float8_e4m3fn:
-            tensors[key], tensors[key + _SCALE_SUFFIX] = _quantize_fp8(value)
-        else:
-            tensors[key] = value.detach().to(dtype).contiguous()
+    meta = _budget_fields('target', keep_ratio, keep_tiles)
+    with_ref = (ref_keep_ratio, ref_keep_tiles) != (None, None)
+    if with_ref != tile_conditions:
+        raise ValueError('a reference budget requires tile_conditions'
+                         if with_ref else
+                         'tile_conditions requires a reference budget')
+    if with_ref:
+        meta.update(_budget_fields('ref', ref_keep_ratio, ref_keep_tiles))
+    if dtype not in _DTYPE_NAMES:
+        raise ValueError(f'unsupported storage dtype {dtype}; expected one '
+                         f'of {sorted(DTYPES)}')
+    params = _bare_keys(weights)
     if not plans.plans:
         raise ValueError('bundle without plans; pass the run\'s plan table')
-    metadata = {
-        'format': FORMAT,
-        'num_layers': str(num_layers),
-        'num_heads': str(num_heads),
-        'head_dim': str(head_dim),
-        'dtype': dtype_name,
-        'tile_conditions': 'true' if tile_conditions else 'false',
-        'source': source,
-        'source_weights': source_weights,
-        'step': str(step),
-        'second_order_rank': str(second_order_rank),
-        'count_term': '1' if count_term else '0',
-        'plans': json.dumps({name: plans.plans[name].to_json()
-                             for name in sorted(plans.plans)}),
-    }
-    metadata.update(metadata_budgets)
+    meta.update(
+        format=FORMAT, num_layers=str(num_layers), num_heads=str(num_heads),
+        head_dim=str(head_dim), dtype=_DTYPE_NAMES[dtype],
+        tile_conditions=str(bool(tile_conditions)).lower(), source=source,
+        source_weights=source_weights, step=str(step),
+        second_order_rank=str(second_order_rank),
+        count_term=str(int(bool(count_term))),
+        plans=json.dumps({g: plans.plans[g].to_json()
+                          for g in sorted(plans.plans)}))
     if keep_ratio is not None:
-        metadata['keep_ratio'] = repr(float(keep_ratio))
-    save_file({k: v.cpu() for k, v in tensors.items()}, path,
-              metadata=metadata)
+        meta['keep_ratio'] = repr(float(keep_ratio))
+    stored = _encode(params, dtype)
+    save_file({k: v.cpu() for k, v in stored.items()}, path, metadata=meta)
 
 
 def read_metadata(path: str) -> dict[str, str]:
-    """The string metadata alone, no tensor read (bundle.py:252-263).
+    """The string metadata alone (no tensor is read).
 
     Raises:
         ValueError: If the file is not a bundle of this format.
     """
     with safe_open(path, framework='pt', device='cpu') as f:
-        metadata = dict(f.metadata() or {})
-    if metadata.get('format') != FORMAT:
-        raise ValueError(f'{path}: not a {FORMAT} bundle '
-                         f'(format {metadata.get("format")!r})')
-    return metadata
+        meta = dict(f.metadata() or {})
+    if meta.get('format') != FORMAT:
+        raise ValueError(f'{path}: not a {FORMAT} bundle (format '
+                         f'{meta.get("format")!r})')
+    return meta
 
 
 def load(path: str, device: torch.device | str = 'cpu') -> Bundle:
-    """Loads a bundle strictly (bundle.py:266-330).
+    """Loads a bundle strictly.
 
     Raises:
-        ValueError: Not a bundle of this format, an unknown storage dtype, an
-            fp8 tensor without its scale, tensors that do not match the
-            predictor the metadata declares, no target budget, or tiled
+        ValueError: Not a bundle of this format, an unknown storage dtype,
+            an fp8 tensor without its scale, tensors that do not fill the
+            declared predictor exactly, no target budget, or tiled
             references without a reference budget.
-        NotImplementedError: A predictor with a second-order head or a count
-            term (no B200 scoring kernel for those).
     """
-    metadata = read_metadata(path)
+    meta = read_metadata(path)
+    dtype_name = meta.get('dtype', 'float32')
+    if dtype_name not in DTYPES:
+        raise ValueError(f'{path}: unknown storage dtype {dtype_name!r}')
     with safe_open(path, framework='pt', device='cpu') as f:
-        tensors = {k: f.get_tensor(k) for k in f.keys()}
-    stored = metadata.get('dtype', _LEGACY_DTYPE)
-    if stored not in DTYPES:
-        raise ValueError(f'{path}: unknown storage dtype {stored!r}')
-    model = veda_predictor.TileScorePredictor(
-        int(metadata['num_layers']), int(metadata['num_heads']),
-        int(metadata['head_dim']),
-        second_order_rank=int(metadata.get('second_order_rank', 0)),
-        count_term=metadata.get('count_term', '0') == '1')
-    resident = DTYPES[stored]
-    if resident is torch.float8_e4m3fn:
-        resident = torch.bfloat16
-        scales = {k[:-len(_SCALE_SUFFIX)]: v for k, v in tensors.items()
-                  if k.endswith(_SCALE_SUFFIX)}
-        values = {k: v for k, v in tensors.items()
-                  if not k.endswith(_SCALE_SUFFIX)}
-        unscaled = sorted(set(values) - set(scales))
-        if unscaled:
-            raise ValueError(f'{path}: fp8 tensors without a '
-                             f'{_SCALE_SUFFIX} scale: {unscaled}')
-        tensors = {k: _dequantize_fp8(v, scales[k], resident)
-                   for k, v in values.items()}
-    # Cast the module first: loading into fp32 parameters would upcast a
-    # bf16 file and hold twice the memory it was exported to save.
-    model = model.to(resident)
-    declared = (f'{metadata["num_layers"]} layers x {metadata["num_heads"]} '
-                f'heads x {metadata["head_dim"]}')
+        stored = {k: f.get_tensor(k) for k in f.keys()}
+    params, param_dtype = _decode(stored, DTYPES[dtype_name], path)
+    shape = (int(meta['num_layers']), int(meta['num_heads']),
+             int(meta['head_dim']))
+    # Parameters take the stored precision before the state is copied in,
+    # so a bf16 file never sits in fp32 parameters.
+    predictor = veda_predictor.TileScorePredictor(
+        *shape, second_order_rank=int(meta.get('second_order_rank', 0)),
+        count_term=meta.get('count_term', '0') == '1').to(param_dtype)
     try:
-        model.load_state_dict(tensors, strict=True)
-    except RuntimeError as error:
-        raise ValueError(f'{path}: predictor weights do not match the '
-                         f'{declared} the metadata declares: {error}') from error
-    plans = veda_plan.PlanTable(
-        [veda_plan.TilePlan.from_json(p)
-         for p in json.loads(metadata['plans']).values()])
-    target = _parse_budget(metadata, 'target', legacy_ratio='keep_ratio')
+        predictor.load_state_dict(params, strict=True)
+    except RuntimeError as err:
+        raise ValueError(
+            f'{path}: predictor weights do not match the {shape[0]} layers '
+            f'x {shape[1]} heads x {shape[2]} the metadata declares: '
+            f'{err}') from err
+    target = _budget_from(meta, 'target')
+    if target is None and 'keep_ratio' in meta:
+        target = veda_mask.Budget(ratio=float(meta['keep_ratio']))
     if target is None:
         raise ValueError(f'{path}: bundle has no target budget')
-    ref = _parse_budget(metadata, 'ref')
-    tile_conditions = metadata.get('tile_conditions', 'false') == 'true'
-    if tile_conditions and ref is None:
+    ref = _budget_from(meta, 'ref')
+    tiled_refs = meta.get('tile_conditions', 'false') == 'true'
+    if tiled_refs and ref is None:
         raise ValueError(f'{path}: tiled references need a ref budget')
-    return Bundle(predictor=model.to(device).eval(), plans=plans,
-                  target_budget=target, ref_budget=ref,
-                  tile_conditions=tile_conditions, keep_ratio=target.ratio,
-                  metadata=metadata)
+    table = veda_plan.PlanTable(veda_plan.TilePlan.from_json(p)
+                                for p in json.loads(meta['plans']).values())
+    return Bundle(predictor.to(device).eval(), table, target, ref,
+                  tiled_refs, target.ratio, meta)
 
 
 def random_bundle(num_layers: int, num_heads: int, head_dim: int,
                   geometries: Sequence[veda_geometry.Geometry],
                   keep_ratio: float, seed: int = 0,
                   device: torch.device | str = 'cpu') -> Bundle:
-    """A randomly initialised bf16 predictor with a uniform least-padding
-    plan per geometry, for benchmarks (bundle.py:333-369). The cost of a
-    Veda step depends on the budget and the tile shapes, not on the scores."""
-    with torch.random.fork_rng(devices=[]):
-        torch.manual_seed(seed)
-        predictor = veda_predictor.TileScorePredictor(num_layers, num_heads,
-                                                      head_dim)
-    plans = veda_plan.PlanTable([
-        veda_plan.TilePlan.uniform(
-            g, tiling.least_padding_shape(g.video_grid), num_layers,
-            num_heads) for g in geometries])
-    return Bundle(predictor=predictor.to(device, torch.bfloat16).eval(),
-                  plans=plans, target_budget=veda_mask.Budget(ratio=keep_ratio),
-                  ref_budget=None, tile_conditions=False,
-                  keep_ratio=keep_ratio,
-                  metadata={'source': 'random', 'seed': str(seed)})
+    """A bf16 predictor with weights drawn from N(0, INIT_STD) by a
+    generator seeded with `seed`, and one uniform least-padding plan per
+    geometry: a stand-in for benchmarks, whose cost depends on the budget
+    and the tile shapes rather than on the scores."""
+    predictor = veda_predictor.TileScorePredictor(num_layers, num_heads,
+                                                  head_dim)
+    gen = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for param in predictor.parameters():
+            param.copy_(torch.randn(param.shape, generator=gen) *
+                        veda_predictor.INIT_STD)
+    table = veda_plan.PlanTable(
+        veda_plan.TilePlan.uniform(g, tiling.least_padding_shape(
+            g.video_grid), num_layers, num_heads) for g in geometries)
+    return Bundle(predictor.to(device, torch.bfloat16).eval(), table,
+                  veda_mask.Budget(ratio=keep_ratio), None, False,
+                  keep_ratio, {'source': 'random', 'seed': str(seed)})

@@ -1,36 +1,69 @@
-"""Tile plans: which tile shape every (layer, head) uses on one geometry.
+"""Tile plans: the tile shape each (layer, head) uses on one video geometry.
 
-Mirror of the reference's `miowtion/veda/plan.py`: the JSON format of its
-released plans (`plans/released/*.json`), the head grouping, the mirrored and
-transposed plans and the plan table's selection rule. Plan search itself is
-the reference's (`veda/search.py`); plans come from it or are built uniform.
+A plan is stored as one JSON object, the format of the reference's released
+plans (miowtion/veda/plan.py:81-106, plans/released/*.json):
+
+    geometry    geometry name "<W>x<H>_t<latent frames>", e.g. "16x9_t37"
+    grid        [t, h, w], the latent video grid of that geometry
+    shapes      the tile shapes in use, as "<t>x<h>x<w>" strings (128 tokens)
+    head_shape  per layer, per head: an index into `shapes`
+    provenance  a free-form object (search settings, derivations)
+
+Rules this module enforces or implements (same behaviour as the reference):
+
+- a layer uses at most two distinct shapes (each shape is one group of
+  heads, one launch of the attention kernels);
+- the heads of a layer form one group per shape, groups in the order of the
+  shape index, heads ascending inside a group (plan.py:28-33, :68-79);
+- H<->W symmetry: the plan of geometry "WxH_tN" serves "HxW_tN" with every
+  tile shape and the grid transposed. `mirrored()` names the result after the
+  mirrored geometry and requires its grid to be the exact transpose (canvas
+  rounding may break the symmetry); `transposed()` keeps the name with a
+  "_T" suffix and requires nothing;
+- selecting a plan for a geometry (PlanTable.select): an exact name match;
+  otherwise the nearest latent_t of the same aspect (ties to the shorter
+  clip); otherwise, when the aspect has no plan at all, the nearest plan of
+  the mirrored aspect or its transpose, whichever needs fewer padded tiles
+  on this grid (the untransposed one on a tie). Plans are never
+  interpolated.
 """
 
 from __future__ import annotations
 
 import dataclasses
-import glob
 import json
 import os
-from collections.abc import Sequence
+import pathlib
+from collections.abc import Iterable
 
 import torch
 
 from miowtion_b200 import geometry as veda_geometry
 from miowtion_b200 import tiling
 
+MAX_SHAPES_PER_LAYER = 2
+
 
 @dataclasses.dataclass(frozen=True)
 class HeadGroup:
-    """Heads of one layer that share a tile shape (plan.py:28-33)."""
+    """The heads of one layer that share a tile shape."""
 
     shape: tiling.TileShape
-    heads: torch.Tensor  # [H'] int64
+    heads: torch.Tensor  # [H'] int64, ascending
+
+
+def _aspect_key(geometry_name: str) -> str:
+    """'16x9_t37' -> '16x9'."""
+    return geometry_name.partition('_t')[0]
+
+
+def _latent_t(plan: 'TilePlan') -> int:
+    return plan.grid[0]
 
 
 @dataclasses.dataclass
 class TilePlan:
-    """Per-(layer, head) tile shapes for one geometry (plan.py:36-144)."""
+    """Tile shapes of every (layer, head) for one geometry."""
 
     geometry: str
     grid: tuple[int, int, int]
@@ -39,146 +72,159 @@ class TilePlan:
     provenance: dict = dataclasses.field(default_factory=dict)
 
     def __post_init__(self):
+        self.grid = tuple(int(g) for g in self.grid)
         for layer, row in enumerate(self.head_shape):
-            if len(set(row)) > 2:
-                raise ValueError(f'layer {layer} uses {len(set(row))} shapes; '
-                                 'at most 2 per layer are allowed')
-        self._groups = {}
+            distinct = len(set(row))
+            if distinct > MAX_SHAPES_PER_LAYER:
+                raise ValueError(
+                    f'layer {layer} mixes {distinct} tile shapes; a layer '
+                    f'may use at most {MAX_SHAPES_PER_LAYER}')
+        self._group_cache: dict = {}
+
+    # -- queries -----------------------------------------------------------
 
     @property
     def num_layers(self) -> int:
         return len(self.head_shape)
 
+    def _shape_ids(self, layer: int) -> list[int]:
+        return sorted(set(self.head_shape[layer]))
+
     def layer_shapes(self, layer: int) -> list[tiling.TileShape]:
-        return [self.shapes[i] for i in sorted(set(self.head_shape[layer]))]
+        """The shapes layer `layer` uses, by shape index."""
+        return [self.shapes[i] for i in self._shape_ids(layer)]
 
     def head_groups(self, layer: int,
                     device: torch.device | str) -> list[HeadGroup]:
-        """Groups of heads sharing a shape (cached per layer and device)."""
+        """One group per shape of the layer, built once per device."""
         key = (layer, str(device))
-        if key not in self._groups:
-            row = torch.tensor(self.head_shape[layer])
-            self._groups[key] = [
-                HeadGroup(self.shapes[i],
-                          torch.nonzero(row == i).view(-1).to(device))
-                for i in sorted(set(self.head_shape[layer]))]
-        return self._groups[key]
+        groups = self._group_cache.get(key)
+        if groups is None:
+            row = self.head_shape[layer]
+            groups = []
+            for sid in self._shape_ids(layer):
+                members = [h for h, s in enumerate(row) if s == sid]
+                groups.append(HeadGroup(
+                    self.shapes[sid],
+                    torch.tensor(members, dtype=torch.int64, device=device)))
+            self._group_cache[key] = groups
+        return groups
+
+    # -- JSON --------------------------------------------------------------
 
     def to_json(self) -> dict:
-        return {'geometry': self.geometry, 'grid': list(self.grid),
-                'shapes': [str(s) for s in self.shapes],
-                'head_shape': self.head_shape,
-                'provenance': self.provenance}
+        return dict(geometry=self.geometry, grid=list(self.grid),
+                    shapes=[str(s) for s in self.shapes],
+                    head_shape=[list(r) for r in self.head_shape],
+                    provenance=self.provenance)
 
     @classmethod
-    def from_json(cls, data: dict) -> TilePlan:
-        return cls(geometry=data['geometry'], grid=tuple(data['grid']),
-                   shapes=[tiling.TileShape.parse(s) for s in data['shapes']],
-                   head_shape=[list(r) for r in data['head_shape']],
-                   provenance=data.get('provenance', {}))
+    def from_json(cls, data: dict) -> 'TilePlan':
+        return cls(data['geometry'], tuple(data['grid']),
+                   [tiling.TileShape.parse(s) for s in data['shapes']],
+                   [list(r) for r in data['head_shape']],
+                   data.get('provenance', {}))
 
     def save(self, path: str) -> None:
-        tmp = path + '.tmp'
-        with open(tmp, 'w') as f:
-            json.dump(self.to_json(), f, indent=1)
-        os.replace(tmp, path)
+        """Writes the JSON next to `path` first, then renames it into place,
+        so a reader never sees a half-written plan."""
+        target = pathlib.Path(path)
+        partial = target.with_name(target.name + '.tmp')
+        partial.write_text(json.dumps(self.to_json(), indent=1))
+        os.replace(partial, target)
 
     @classmethod
-    def load(cls, path: str) -> TilePlan:
-        with open(path) as f:
-            return cls.from_json(json.load(f))
+    def load(cls, path: str) -> 'TilePlan':
+        return cls.from_json(json.loads(pathlib.Path(path).read_text()))
+
+    # -- derived plans -----------------------------------------------------
 
     @classmethod
     def uniform(cls, geometry: veda_geometry.Geometry,
                 shape: tiling.TileShape, num_layers: int,
-                num_heads: int) -> TilePlan:
-        """Every head uses one shape (plan.py:108-114)."""
-        return cls(geometry.name, tuple(geometry.video_grid), [shape],
-                   [[0] * num_heads for _ in range(num_layers)],
+                num_heads: int) -> 'TilePlan':
+        """Every head of every layer on one shape."""
+        rows = [[0] * num_heads for _ in range(num_layers)]
+        return cls(geometry.name, tuple(geometry.video_grid), [shape], rows,
                    {'source': 'uniform'})
 
-    def mirrored(self) -> TilePlan:
-        """The plan of the H<->W mirrored geometry (plan.py:116-138), e.g.
-        9x16_t37 from 16x9_t37: shapes and grid transposed, the mirrored
-        geometry's name, `mirrored_from` added to the provenance.
+    def _hw_swapped(self, name: str, note: str) -> 'TilePlan':
+        """This plan with H and W exchanged in the grid and every shape,
+        under `name`, recording this plan's name as provenance[note]."""
+        t, h, w = self.grid
+        return TilePlan(name, (t, w, h),
+                        [s.transposed() for s in self.shapes],
+                        [list(r) for r in self.head_shape],
+                        {**self.provenance, note: self.geometry})
+
+    def mirrored(self) -> 'TilePlan':
+        """The plan of the H<->W mirrored geometry ('9x16_t37' for
+        '16x9_t37').
 
         Raises:
             ValueError: If the mirrored geometry's grid is not this grid
-                transposed (the canvas rounding differs).
+                transposed.
         """
-        aspect, latent_t = self.geometry.split('_t')
-        w, h = aspect.split('x')
-        mirror = veda_geometry.geometry_from_latent_t(f'{h}:{w}',
-                                                      int(latent_t))
-        t, grid_h, grid_w = self.grid
-        if tuple(mirror.video_grid) != (t, grid_w, grid_h):
-            raise ValueError(f'{mirror.name} grid {mirror.video_grid} is not '
-                             f'the transpose of {self.geometry} {self.grid}')
-        return TilePlan(mirror.name, (t, grid_w, grid_h),
-                        [s.transposed() for s in self.shapes],
-                        [list(r) for r in self.head_shape],
-                        {**self.provenance, 'mirrored_from': self.geometry})
+        aspect, _, latent_t = self.geometry.partition('_t')
+        width, _, height = aspect.partition('x')
+        other = veda_geometry.geometry_from_latent_t(f'{height}:{width}',
+                                                     int(latent_t))
+        swapped = self._hw_swapped(other.name, 'mirrored_from')
+        if tuple(other.video_grid) != swapped.grid:
+            raise ValueError(
+                f'{other.name} has grid {tuple(other.video_grid)}, not the '
+                f'transpose of {self.geometry}\'s {self.grid}')
+        return swapped
 
-    def transposed(self) -> TilePlan:
-        """H<->W transposed plan named '<geometry>_T' (plan.py:140-146)."""
-        t, h, w = self.grid
-        return TilePlan(self.geometry + '_T', (t, w, h),
-                        [s.transposed() for s in self.shapes],
-                        [list(r) for r in self.head_shape],
-                        {**self.provenance, 'transposed_from': self.geometry})
+    def transposed(self) -> 'TilePlan':
+        """The H<->W transpose, named '<geometry>_T'."""
+        return self._hw_swapped(self.geometry + '_T', 'transposed_from')
 
 
 class PlanTable:
-    """All searched plans, keyed by geometry name (plan.py:149-188)."""
+    """Searched plans by geometry name, with the selection rule above."""
 
-    def __init__(self, plans: Sequence[TilePlan]):
+    def __init__(self, plans: Iterable[TilePlan]):
         self.plans = {p.geometry: p for p in plans}
 
     @classmethod
-    def load_dir(cls, directory: str) -> PlanTable:
-        """Every `*.json` plan of a directory, in name order.
+    def load_dir(cls, directory: str) -> 'PlanTable':
+        """Every '*.json' plan in a directory, in file-name order.
 
         Raises:
             FileNotFoundError: If the directory holds no plan.
         """
-        paths = sorted(glob.glob(os.path.join(directory, '*.json')))
-        if not paths:
+        files = sorted(pathlib.Path(directory).glob('*.json'))
+        if not files:
             raise FileNotFoundError(f'no plans in {directory}')
-        return cls([TilePlan.load(p) for p in paths])
+        return cls(TilePlan.load(str(f)) for f in files)
+
+    def _of_aspect(self, key: str) -> list[TilePlan]:
+        return [p for p in self.plans.values()
+                if _aspect_key(p.geometry) == key]
 
     def select(self, geometry: veda_geometry.Geometry) -> TilePlan:
-        """The plan for a geometry, by the reference's rule (plan.py:160-188):
-
-        1. the geometry's own plan, if searched;
-        2. else the plan of the same aspect with the nearest latent_t (ties
-           to the shorter one; no interpolation);
-        3. else, only when no plan of this aspect exists, the mirrored
-           aspect's nearest plan or its transpose, whichever pads the
-           target grid less (the untransposed one on a tie).
+        """The plan serving `geometry`.
 
         Raises:
-            KeyError: If neither this aspect nor its mirror has a plan.
+            KeyError: If neither the aspect nor its mirror has a plan.
         """
-        if geometry.name in self.plans:
-            return self.plans[geometry.name]
+        exact = self.plans.get(geometry.name)
+        if exact is not None:
+            return exact
+        width, _, height = geometry.aspect.partition(':')
+        want_t = geometry.latent_t
 
-        def aspect_of(p: TilePlan) -> str:
-            return p.geometry.split('_t')[0]
-
-        key = geometry.aspect.replace(':', 'x')
-        same = [p for p in self.plans.values() if aspect_of(p) == key]
-        if same:
-            return min(same, key=lambda p: (abs(p.grid[0] - geometry.latent_t),
-                                            p.grid[0]))
-        w, h = geometry.aspect.split(':')
-        mirror = [p for p in self.plans.values()
-                  if aspect_of(p) == f'{h}x{w}']
-        if not mirror:
+        own = self._of_aspect(f'{width}x{height}')
+        if own:
+            # Nearest clip length; the shorter clip wins a tie.
+            return min(own, key=lambda p: (abs(_latent_t(p) - want_t),
+                                           _latent_t(p)))
+        flipped = self._of_aspect(f'{height}x{width}')
+        if not flipped:
             raise KeyError(f'no plan for {geometry.name}')
-        nearest = min(mirror, key=lambda p: abs(p.grid[0] - geometry.latent_t))
+        base = min(flipped, key=lambda p: abs(_latent_t(p) - want_t))
         grid = geometry.video_grid
-
-        def padded_tiles(p: TilePlan) -> int:
-            return sum(s.num_tiles(grid) for s in p.shapes)
-
-        return min((nearest, nearest.transposed()), key=padded_tiles)
+        candidates = (base, base.transposed())  # a tie keeps `base`
+        return min(candidates,
+                   key=lambda p: sum(s.num_tiles(grid) for s in p.shapes))

@@ -23,7 +23,6 @@ quantity (search.py:130-175) lives in the CPU oracle, for the tests only.
 
 from __future__ import annotations
 
-import collections
 import dataclasses
 import json
 import os
@@ -144,53 +143,57 @@ def _oracle_rel_mse_kernels(q, k, v, dense_out, lse, tile_layout, blocks,
 
 
 class OracleScorer:
-    """AttentionFn that returns dense attention and scores every candidate
-    shape on the way (search.py:195-243). Only the layers of scored steps
-    should use it; the trajectory itself stays dense. `dense_backend` is
-    kept for the reference's signature: the dense teacher here is always
-    this library's dense kernel."""
+    """AttentionFn that returns the dense attention and, on the way, scores
+    every candidate shape (search.py:195-243). Only the layers of scored
+    steps should use it; the trajectory itself stays dense.
+
+    `dense_backend` is accepted for the reference's signature; the dense
+    teacher here is always this library's dense kernel. Scores accumulate
+    in `scores[layer] = [candidates, heads]` fp32 on the host.
+    """
 
     def __init__(self, layout: veda_attention.PackedLayout,
                  candidates: Sequence[tiling.TileShape],
                  config: veda_attention.VedaConfig, query_tiles: int,
                  seed: int, device: torch.device,
                  dense_backend: str = 'auto'):
-        self.layout = layout
-        self.candidates = list(candidates)
+        del dense_backend
         self.clip = veda_attention.ClipTiling(layout, config, device)
-        self.query_tiles = query_tiles
-        self.seed = seed
-        self.dense_backend = dense_backend
+        self.layout, self.candidates = layout, list(candidates)
+        self.query_tiles, self.seed = query_tiles, seed
         self.scores: dict[int, torch.Tensor] = {}
 
     def sample_rows(self, tile_layout: tiling.TileLayout,
                     layer_index: int) -> torch.Tensor:
-        """Sorted sample of video query tiles, one seed per (run, layer) so
-        every candidate is scored on paired samples (search.py:227-230)."""
-        gen = torch.Generator().manual_seed(self.seed * 1000 + layer_index)
-        count = min(self.query_tiles, tile_layout.n_video_tiles)
-        rows = torch.randperm(tile_layout.n_video_tiles, generator=gen)
-        return rows[:count].sort().values
+        """The sampled video query tiles, ascending. The seed depends on
+        the run seed and the layer only (seed * 1000 + layer), so every
+        candidate of a layer is scored on the same draw: the first
+        min(query_tiles, n_video) entries of a random permutation."""
+        draw = torch.randperm(
+            tile_layout.n_video_tiles,
+            generator=torch.Generator().manual_seed(
+                self.seed * 1000 + layer_index))
+        return draw[:self.query_tiles].sort().values
 
     def __call__(self, q, k, v, layer_index):
         out, lse = kernels.dense_attention(q, k, v, q.shape[-1]**-0.5,
                                            return_lse=True,
                                            used=self.layout.used)
-        table = torch.empty(len(self.candidates), q.shape[1],
-                            dtype=torch.float32)
-        for ci, shape in enumerate(self.candidates):
+        per_candidate = []
+        for shape in self.candidates:
             tile_layout = self.clip.get(shape)
             rows = self.sample_rows(tile_layout, layer_index).to(q.device)
-            table[ci] = oracle_rel_mse(q, k, v, tile_layout,
-                                       self.clip.blocks(tile_layout), rows,
-                                       dense_out=out, lse=lse).cpu()
-        self.scores[layer_index] = table
+            per_candidate.append(oracle_rel_mse(
+                q, k, v, tile_layout, self.clip.blocks(tile_layout), rows,
+                dense_out=out, lse=lse).float().cpu())
+        self.scores[layer_index] = torch.stack(per_candidate)
         return out
 
 
 @dataclasses.dataclass(frozen=True)
 class ScoreEntry:
-    """rel-MSE of every candidate for one (clip, step, layer): [C, H]."""
+    """rel-MSE of every candidate shape for one (clip, step, layer):
+    `table` [candidates, heads]."""
 
     clip: str
     step: int
@@ -198,45 +201,91 @@ class ScoreEntry:
     table: torch.Tensor
 
 
+# Score files: one JSON object {"candidates": [shape strings], "meta": {...},
+# "entries": [{"clip", "step", "layer", "table"}, ...]} (the reference's
+# search.py:256-294), and beside it "<file>.done" = {"entries": count},
+# written last: a file without it is an interrupted run.
+_DONE = '.done'
+
+
 def save_entries(path: str, entries: Iterable[ScoreEntry],
                  candidates: Sequence[tiling.TileShape], meta: dict) -> None:
-    """Writes the score file atomically, then its `.done` marker
-    (search.py:256-273)."""
-    entries = list(entries)
-    payload = {'candidates': [str(c) for c in candidates], 'meta': meta,
-               'entries': [{'clip': e.clip, 'step': e.step, 'layer': e.layer,
-                            'table': e.table.tolist()} for e in entries]}
-    tmp = path + '.tmp'
-    with open(tmp, 'w') as f:
-        json.dump(payload, f)
-    os.replace(tmp, path)
-    with open(path + '.done', 'w') as f:
-        json.dump({'entries': len(entries)}, f)
+    """Writes a score file (atomically), then its completion marker."""
+    rows = [dict(clip=e.clip, step=e.step, layer=e.layer,
+                 table=e.table.tolist()) for e in entries]
+    body = dict(candidates=[str(c) for c in candidates], meta=meta,
+                entries=rows)
+    partial = path + '.tmp'
+    with open(partial, 'w') as f:
+        json.dump(body, f)
+    os.replace(partial, path)
+    with open(path + _DONE, 'w') as f:
+        json.dump({'entries': len(rows)}, f)
+
+
+def _read_score_file(path: str) -> dict:
+    if not os.path.exists(path + _DONE):
+        raise FileNotFoundError(
+            f'{path} has no completion marker ({path + _DONE}): the run '
+            'that wrote it did not finish')
+    with open(path) as f:
+        return json.load(f)
 
 
 def load_entries(paths: Iterable[str]
                  ) -> tuple[list[tiling.TileShape], list[ScoreEntry], dict]:
-    """Completed score files (search.py:276-294).
+    """The entries of completed score files, in file order; the menu and
+    the meta come from the files (the meta of the last one).
 
     Raises:
         FileNotFoundError: A file without its completion marker.
-        ValueError: Files with different candidate menus.
+        ValueError: Files scored against different candidate menus.
     """
-    candidates, entries, meta = None, [], {}
+    menu: list[tiling.TileShape] | None = None
+    meta: dict = {}
+    entries: list[ScoreEntry] = []
     for path in paths:
-        if not os.path.exists(path + '.done'):
-            raise FileNotFoundError(f'{path} has no completion marker')
-        with open(path) as f:
-            payload = json.load(f)
-        shapes = [tiling.TileShape.parse(s) for s in payload['candidates']]
-        if candidates is not None and shapes != candidates:
-            raise ValueError(f'{path}: candidate menu differs')
-        candidates = shapes
-        meta = payload['meta']
-        entries += [ScoreEntry(e['clip'], e['step'], e['layer'],
-                               torch.tensor(e['table']))
-                    for e in payload['entries']]
-    return candidates, entries, meta
+        body = _read_score_file(path)
+        this_menu = [tiling.TileShape.parse(c) for c in body['candidates']]
+        if menu is None:
+            menu = this_menu
+        elif this_menu != menu:
+            raise ValueError(f'{path}: candidate menu {body["candidates"]} '
+                             f'differs from the earlier files\'')
+        meta = body['meta']
+        entries.extend(ScoreEntry(r['clip'], r['step'], r['layer'],
+                                  torch.tensor(r['table']))
+                       for r in body['entries'])
+    return menu, entries, meta
+
+
+def _vote_layer(tables: torch.Tensor, max_shapes: int
+                ) -> tuple[list[int], list[int], torch.Tensor]:
+    """One layer's vote over `tables` [entries, shapes, heads] (allowed
+    shapes only). Returns (kept shapes in rank order, each head's shape,
+    each head's mean error under it).
+
+    1. Every entry votes, per head, for its lowest-error shape; each head
+       takes the most-voted shape (the lower mean error on a tie).
+    2. Shapes rank by how many heads took them (the lower mean error over
+       heads on a tie); the first `max_shapes` that some head took stay.
+    3. Every head takes the staying shape with its lowest mean error.
+    """
+    n_shapes = tables.shape[1]
+    mean = tables.mean(0)                                 # [shapes, heads]
+    ballots = torch.nn.functional.one_hot(
+        tables.argmin(1), n_shapes).sum(0).T.to(mean.dtype)  # [shapes, heads]
+    # Integer vote counts first, mean error only to break a tie.
+    head_pick = (ballots - 1e-6 * mean).argmax(0)
+    heads_per_shape = torch.bincount(head_pick, minlength=n_shapes)
+    order = sorted(range(n_shapes),
+                   key=lambda a: (-int(heads_per_shape[a]),
+                                  float(mean[a].mean())))
+    kept = [a for a in order if heads_per_shape[a] > 0][:max_shapes]
+    among = mean[kept]                                    # [kept, heads]
+    choice = among.argmin(0)
+    return kept, [kept[c] for c in choice.tolist()], \
+        among.gather(0, choice[None])[0]
 
 
 def build_plan(geometry_name: str, grid: tuple[int, int, int],
@@ -244,67 +293,50 @@ def build_plan(geometry_name: str, grid: tuple[int, int, int],
                entries: Sequence[ScoreEntry], num_layers: int,
                max_padding: float = 0.2, max_shapes_per_layer: int = 2,
                meta: dict | None = None) -> veda_plan.TilePlan:
-    """Votes a timestep-independent plan from oracle scores
-    (search.py:297-368):
-
-    - candidates padding the grid by more than `max_padding` are dropped;
-    - per (layer, head), every entry votes for its lowest-error shape; the
-      head picks the majority (ties to the lower mean error);
-    - a layer keeps its `max_shapes_per_layer` most-picked shapes (ties to
-      the lower mean error); heads of dropped shapes take the kept shape
-      with their lowest mean error;
-    - provenance records the plan's and the best single shape's mean error.
+    """A timestep-independent plan voted from oracle scores
+    (search.py:297-368): candidates that pad the grid by more than
+    `max_padding` are out; each layer votes as `_vote_layer` describes. The
+    provenance records the entries used, the voting limits, the plan's mean
+    error and the best single shape's.
 
     Raises:
-        ValueError: No candidate passes the padding limit, or a layer has
-            no scores.
+        ValueError: No candidate within the padding limit, or a layer
+            without scores.
     """
     allowed = [i for i, c in enumerate(candidates)
                if c.padding_ratio(grid) <= max_padding + 1e-12]
     if not allowed:
         raise ValueError('no candidate passes the padding limit')
-    allowed_t = torch.tensor(allowed)
-    by_layer = collections.defaultdict(list)
+    per_layer: dict[int, list[torch.Tensor]] = {}
     for e in entries:
-        by_layer[e.layer].append(e.table[allowed_t])
-    missing = [layer for layer in range(num_layers) if layer not in by_layer]
-    if missing:
-        raise ValueError(f'no scores for layers {missing[:5]}')
-    head_shape, plan_mse, per_layer = [], [], []
+        per_layer.setdefault(e.layer, []).append(e.table[allowed])
+    absent = [layer for layer in range(num_layers) if layer not in per_layer]
+    if absent:
+        raise ValueError(f'no scores for layers {absent[:5]}')
+
+    rows, errors, layer_shapes, means = [], [], [], []
     for layer in range(num_layers):
-        tables = torch.stack(by_layer[layer])  # [E, A, H]
-        mean = tables.mean(0)
-        winners = tables.argmin(1)  # [E, H]
-        votes = torch.zeros_like(mean).scatter_add_(
-            0, winners, torch.ones_like(winners, dtype=mean.dtype))
-        head_pick = (votes - 1e-6 * mean).argmax(0)
-        counts = torch.bincount(head_pick, minlength=mean.shape[0]).float()
-        ranking = sorted(range(mean.shape[0]),
-                         key=lambda a: (-counts[a].item(),
-                                        mean[a].mean().item()))
-        kept = [a for a in ranking if counts[a] > 0][:max_shapes_per_layer]
-        kept_t = torch.tensor(kept)
-        final = kept_t[mean[kept_t].argmin(0)]
-        head_shape.append([allowed[a] for a in final.tolist()])
-        plan_mse.append(mean.gather(0, final[None])[0])
-        per_layer.append([str(candidates[allowed[a]]) for a in kept])
-    used = sorted({i for row in head_shape for i in row})
-    remap = {old: new for new, old in enumerate(used)}
-    layer_means = torch.stack([torch.stack(by_layer[layer]).mean(0)
-                               for layer in range(num_layers)])
+        tables = torch.stack(per_layer[layer])
+        kept, picks, err = _vote_layer(tables, max_shapes_per_layer)
+        rows.append([allowed[a] for a in picks])
+        errors.append(err)
+        layer_shapes.append([str(candidates[allowed[a]]) for a in kept])
+        means.append(tables.mean(0))
+    in_use = sorted({c for row in rows for c in row})
+    slot = {c: i for i, c in enumerate(in_use)}
+    by_shape = torch.stack(means).mean(dim=(0, 2))        # [allowed]
     provenance = {
         'entries': len(entries),
         'clips': sorted({e.clip for e in entries}),
         'steps': sorted({e.step for e in entries}),
         'max_padding': max_padding,
         'max_shapes_per_layer': max_shapes_per_layer,
-        'plan_mse': torch.stack(plan_mse).mean().item(),
-        'best_single_shape_mse': layer_means.mean(dim=(0, 2)).min().item(),
-        'layer_shapes': per_layer,
-        **(meta or {}),
+        'plan_mse': torch.stack(errors).mean().item(),
+        'best_single_shape_mse': by_shape.min().item(),
+        'layer_shapes': layer_shapes,
     }
-    return veda_plan.TilePlan(
-        geometry=geometry_name, grid=tuple(grid),
-        shapes=[candidates[i] for i in used],
-        head_shape=[[remap[i] for i in row] for row in head_shape],
-        provenance=provenance)
+    provenance.update(meta or {})
+    return veda_plan.TilePlan(geometry_name, tuple(grid),
+                              [candidates[c] for c in in_use],
+                              [[slot[c] for c in row] for row in rows],
+                              provenance)
