@@ -310,6 +310,9 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-comparators', action='store_true',
                     help='skip the same-box GPU comparators (N=1)')
+    ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=1,
+                    help="the attention forward's softmax: two groups of "
+                         'warps on alternate key blocks (2) or one (1)')
     ap.add_argument('--only', choices=['backward', 'heat', 'compensation',
                                        'search'], default=None,
                     help='time one stage on head group 0 of the config '
@@ -337,6 +340,7 @@ def main():
     if args.impl == 'reference':
         run_reference(args, cfg)
         return
+    kernels.set_fwd_groups(args.fwd_groups)
     if args.warmup < 3:
         raise SystemExit('use at least 3 warm-up steps')
     if args.only:
@@ -483,6 +487,7 @@ def main():
                        'parallelism': (f'clip per GPU x{world}'
                                        if mode == 'clips' else
                                        f'ulysses-heads x{world}'),
+                       'softmax_groups': args.fwd_groups,
                        'l2': 'inputs exceed L2 (q/k/v/tiles >> 126 MB)'},
             'effective_tflops': eff,
             'frac_of_peak': eff / peak,
@@ -878,51 +883,89 @@ def run_stage(args, cfg):
 
 
 def run_train_step(args, cfg):
-    """Config 5 on one GPU: the teacher (dense forward with LSE and the
-    block heat with reduce='sum' for every query tile) and the sparse
-    student forward + backward on the same q, k, v.
+    """Config 5: the teacher (dense forward with LSE and the block heat
+    with reduce='sum' for every query tile) and the sparse student forward +
+    backward on the same q, k, v.
 
     `--teacher fused` (default): per head group, q, k, v in tile order, one
     pass of the fused dense + LSE + heat kernel, and the teacher output
-    scattered back to sequence order. `--teacher separate`: the dense
-    kernel over the packed sequence, the LSE gathered into tile order, and
-    the heat kernel recomputing QK^T."""
+    scattered back to its rows. `--teacher separate`: the dense kernel over
+    the packed sequence, the LSE gathered into tile order, and the heat
+    kernel recomputing QK^T.
+
+    On N GPUs the heads are split (Ulysses): each rank holds a [S/N, H, D]
+    shard of q, k, v and dO; one all-to-all per tensor brings the rank's
+    H/N heads of every row, the teacher and the student run on them, and
+    the student's output returns to the shard through the inverse exchange.
+    The backward exchanges dO into the head layout and dQ, dK, dV back to
+    the shards (autograd through the exchanges). Strong scaling: the value
+    is the time of one step of the whole clip, the max over ranks."""
     from miowtion_b200 import heatmap
     from miowtion_b200 import kernels
-    if int(os.environ.get('WORLD_SIZE', '1')) != 1 or args.gpus != 1:
-        raise SystemExit('cfg5 runs on one GPU')
-    device = torch.device('cuda', 0)
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if world != args.gpus:
+        raise SystemExit(f'--gpus {args.gpus} but WORLD_SIZE={world}')
+    if world > 1 and args.parallel != 'ulysses':
+        raise SystemExit('cfg5 on several GPUs splits the heads '
+                         '(--parallel ulysses)')
+    device = torch.device('cuda', local_rank)
     torch.cuda.set_device(device)
-    student, clip, plan, _ = build_student(cfg, device)
-    q, k, v = synthetic_qkv(cfg, cfg['seq_len'], 0, device)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', device_id=device,
+                                timeout=datetime.timedelta(seconds=120))
+    seq_len, heads = cfg['seq_len'], cfg['heads']
+    if heads % world or seq_len % world:
+        raise SystemExit('heads and sequence must divide by the GPU count')
+    full_plan = veda_plan.TilePlan(
+        'bench', cfg['target'][1],
+        [tiling.TileShape(*s) for s in cfg['shapes']], [cfg['head_shape']])
+    plan = ulysses.local_plan(full_plan, rank, world) if world > 1 else None
+    student, clip, plan, _ = build_student(cfg, device, plan)
+    shard = seq_len // world
+    rows = slice(rank * shard, (rank + 1) * shard)
+    q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
     gen = torch.Generator(device=device).manual_seed(cfg['dout_seed'])
-    dout = torch.randn(q.shape, generator=gen, device=device).to(
-        torch.bfloat16)
+    dout = torch.randn(seq_len, heads, 128, generator=gen,
+                       device=device).to(torch.bfloat16)[rows].contiguous()
+    uly = ulysses.UlyssesSparseStudent(student) if world > 1 else None
+    local = uly.local(0) if uly is not None else student
     scale = 128 ** -0.5
-    groups = plan.head_groups(0, device)
+    groups = plan.head_groups(0, device)  # this rank's heads
     stream = torch.cuda.current_stream()
     fused = args.teacher == 'fused'
-    if fused:
-        stage_ms = {'teacher_gather': 0.0, 'teacher_fused': 0.0,
-                    'student_fwd': 0.0, 'student_bwd': 0.0}
-    else:
-        stage_ms = {'dense_fwd_lse': 0.0, 'heat': 0.0, 'student_fwd': 0.0,
-                    'student_bwd': 0.0}
-    teacher_out = torch.empty(cfg['seq_len'] + 1, cfg['heads'], 128,
+    names = ['exchange_in']
+    names += (['teacher_gather', 'teacher_fused'] if fused else
+              ['dense_fwd_lse', 'heat'])
+    names += ['student_fwd', 'student_bwd']
+    stage_ms = dict.fromkeys(names, 0.0)
+    local_heads = len(plan.head_shape[0])
+    teacher_out = torch.empty(seq_len + 1, local_heads, 128,
                               dtype=torch.bfloat16, device=device)
 
     def step(qs, ks, vs, dos, timed):
-        marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        marks = [torch.cuda.Event(enable_timing=True)
+                 for _ in range(len(names) + 1)]
         marks[0].record(stream)
+        leaves = [t.detach().requires_grad_(True) for t in (qs, ks, vs)]
+        with torch.enable_grad():
+            if uly is not None:
+                qh, kh, vh = (uly.to_heads(t) for t in leaves)
+            else:
+                qh, kh, vh = leaves
+        marks[1].record(stream)
         with torch.no_grad():
+            tq, tk, tv = (t.detach() for t in (qh, kh, vh))
             heat_sum = 0.0
             if fused:
                 tiles = []
                 for g in groups:
                     tl = clip.get(g.shape)
                     tiles.append([tiling.gather_tiles(t, tl, g.heads)
-                                  for t in (qs, ks, vs)])
-                marks[1].record(stream)
+                                  for t in (tq, tk, tv)])
+                marks[2].record(stream)
                 for g, (qt, kt, vt) in zip(groups, tiles):
                     tl = clip.get(g.shape)
                     out_t, _, heat = heatmap.fused_dense_heat(qt, kt, vt, tl,
@@ -931,35 +974,42 @@ def run_train_step(args, cfg):
                     heat_sum = heat_sum + heat.sum()
                 del tiles
             else:
-                _, lse = kernels.dense_attention(qs, ks, vs, scale, True,
+                _, lse = kernels.dense_attention(tq, tk, tv, scale, True,
                                                  used=cfg['used'])
-                marks[1].record(stream)
+                marks[2].record(stream)
                 for g in groups:
                     tl = clip.get(g.shape)
                     lse_t = tiling.gather_lse(lse, tl, g.heads)
-                    qt = tiling.gather_tiles(qs, tl, g.heads)
-                    kt = tiling.gather_tiles(ks, tl, g.heads)
+                    qt = tiling.gather_tiles(tq, tl, g.heads)
+                    kt = tiling.gather_tiles(tk, tl, g.heads)
                     heat = heatmap.teacher_heat(
                         qt, kt, lse_t, tl,
                         torch.arange(tl.n_tiles, device=device), 'sum')
                     heat_sum = heat_sum + heat.sum()
                     del qt, kt, lse_t
-            marks[2].record(stream)
-        leaves = [t.detach().requires_grad_(True) for t in (qs, ks, vs)]
-        with torch.enable_grad():
-            out = student(*leaves, 0)
             marks[3].record(stream)
+        with torch.enable_grad():
+            out = local(qh, kh, vh, 0)
+            if uly is not None:
+                out = uly.to_seq(out)
+            marks[4].record(stream)
             out.backward(dos)
-        marks[4].record(stream)
+        marks[5].record(stream)
         if timed:
             torch.cuda.synchronize()
-            for i, n in enumerate(stage_ms):
+            for i, n in enumerate(names):
                 stage_ms[n] += marks[i].elapsed_time(marks[i + 1])
         return heat_sum + leaves[0].grad.float().abs().sum() * 0
 
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
     for _ in range(args.warmup):
         step(q, k, v, dout, False)
-    torch.cuda.synchronize()
+    barrier()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     with ClockSampler(device) as clocks:
@@ -968,19 +1018,21 @@ def run_train_step(args, cfg):
         for _ in range(args.steps):
             step(q, k, v, dout, False)
         stop.record(stream)
-        torch.cuda.synchronize()
+        barrier()
         clocks.mark('t1')
     ms = start.elapsed_time(stop) / args.steps
     # Stage split (separate, synchronised passes).
     for _ in range(2):
         step(q, k, v, dout, True)
+    barrier()
     stages = {n: t / 2 for n, t in stage_ms.items()}
-    # End to end: H2D of this step's q, k, v, dO from pinned memory, the
-    # step, D2H of its scalar result.
+    # End to end: H2D of this step's q, k, v, dO shards from pinned memory,
+    # the step, D2H of its scalar result.
     host = [t.cpu().pin_memory() for t in (q, k, v, dout)]
     dev_in = [torch.empty_like(t) for t in (q, k, v, dout)]
     res_host = torch.empty((), dtype=torch.float32).pin_memory()
     e2e_steps = max(1, min(args.steps, 5))
+    barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -989,89 +1041,117 @@ def run_train_step(args, cfg):
             d.copy_(h, non_blocking=True)
         res_host.copy_(step(*dev_in, False), non_blocking=True)
     e1.record(stream)
-    torch.cuda.synchronize()
+    barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    # Algorithmic work (counted after timing).
+    # Algorithmic work of this rank's heads (counted after timing).
     blocks = 0
     with torch.no_grad():
+        qh = uly.to_heads(q) if uly is not None else q
+        kh = uly.to_heads(k) if uly is not None else k
         for g in groups:
             tl = clip.get(g.shape)
-            _, fq = tiling.gather_and_pool(q, tl, g.heads)
-            _, fk = tiling.gather_and_pool(k, tl, g.heads)
-            logits = student.predictor.layers[0](fq, fk, g.heads)
+            _, fq = tiling.gather_and_pool(qh, tl, g.heads)
+            _, fk = tiling.gather_and_pool(kh, tl, g.heads)
+            logits = local.predictor.layers[0](fq, fk,
+                                               g.heads + local.head_offset)
             lists = veda_mask.select_block_lists(
                 logits[:, :tl.n_video_tiles], tl, clip.blocks(tl))
             blocks += int(lists.part_cnt.sum() + lists.full_cnt.sum())
-    used, heads = cfg['used'], cfg['heads']
-    n_tiles = sum(clip.get(g.shape).n_tiles * g.heads.numel()
-                  for g in groups)  # query tiles x heads
+        del qh, kh
+    used = cfg['used']
     heat_flops = sum(2.0 * (clip.get(g.shape).n_tiles * 128) ** 2 * 128 *
                      g.heads.numel() for g in groups)
-    dense_flops = 4.0 * used ** 2 * 128 * heads
     # The fused pass runs the dense attention over the tile-ordered rows
     # (padding slots included) and no second QK^T.
     fused_exec_flops = sum(4.0 * (clip.get(g.shape).n_tiles * 128) ** 2 *
                            128 * g.heads.numel() for g in groups)
+    qtile_heads = sum(clip.get(g.shape).n_tiles * g.heads.numel()
+                      for g in groups)
+    maxv = torch.tensor([ms, e2e_ms] + [stages[n] for n in names],
+                        dtype=torch.float64, device=device)
+    sums = torch.tensor([float(blocks), heat_flops, fused_exec_flops,
+                         float(qtile_heads)], dtype=torch.float64,
+                        device=device)
+    if world > 1:
+        dist.all_reduce(maxv, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+    ms, e2e_ms, *stage_vals = maxv.tolist()
+    stages = dict(zip(names, stage_vals))
+    if world == 1:
+        del stages['exchange_in']
+    blocks, heat_flops, fused_exec_flops, qtile_heads = sums.tolist()
+    blocks = int(blocks)
+    dense_flops = 4.0 * used ** 2 * 128 * heads
     sparse_flops = 3.5 * blocks * BLOCK_FLOPS  # fwd + bwd (2.5x fwd)
     total = dense_flops + heat_flops + sparse_flops
-    peaks = load_peaks()
-    peak = peaks['bf16_tflops']
-    bwd_tflops = 2.5 * blocks * BLOCK_FLOPS / stages['student_bwd'] / 1e9
-    if fused:
-        achieved = fused_exec_flops / stages['teacher_fused'] / 1e9
-        stage_tflops = {
-            'teacher_fused_executed': achieved,
-            'teacher_reference_accounting': (dense_flops + heat_flops) /
-                                            stages['teacher_fused'] / 1e9,
-            'student_bwd_attention_equiv': bwd_tflops}
-        kernel = ('bsa_fwd_kernel<heat> (fused dense + LSE + heat, '
-                  'executed FLOPs over tile-ordered rows)')
-    else:
-        achieved = dense_flops / stages['dense_fwd_lse'] / 1e9
-        stage_tflops = {
-            'dense_fwd_lse': achieved,
-            'heat': heat_flops / stages['heat'] / 1e9,
-            'student_bwd_attention_equiv': bwd_tflops}
-        kernel = 'bsa_fwd_kernel (dense mode)'
-    roofline = {'bound': 'tensor', 'kernel': kernel, 'achieved': achieved,
-                'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
-                'traffic': None,
-                'peak_source': f'{peaks["source"]} bf16 burst'}
-    line = {
-        'metric': METRIC, 'value': ms, 'unit': 'ms/step', 'n_gpus': 1,
-        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
-        'higher_is_better': False, 'scaling': 'strong', 'vs_baseline': None,
-        'dtype': 'bf16',
-        'data': 'synthetic (seeded N(0,1) q/k/v and dO, random-init '
-                'predictor N(0,0.02))',
-        'config': {'workload': f'{args.config}: {cfg["desc"]}',
-                   'heads': heads, 'seq_len': cfg['seq_len'],
-                   'head_dim': 128, 'parallelism': 'single GPU',
-                   'l2': 'inputs exceed L2 (q/k/v >> 126 MB)'},
-        'stages_ms': stages,
-        'computed_blocks': blocks,
-        'algorithmic_tflop': total / 1e12,
-        'effective_tflops': total / (ms * 1e-3) / 1e12,
-        'frac_of_peak': total / (ms * 1e-3) / 1e12 / peak,
-        'teacher': args.teacher,
-        'stage_tflops': stage_tflops,
-        'roofline': roofline,
-        'e2e': {'value': e2e_ms, 'unit': 'ms/step', 'steps': e2e_steps,
-                'h2d_bytes_per_step': 4 * q.numel() * 2,
-                'd2h_bytes_per_step': 4},
-        # Ours per step. Teacher, separate: dense fwd, then per group
-        # gather_lse, gather q, k, heat (1 + 4 per group); fused: per group
-        # gather q, k, v, keep-all lists, fused pass, scatter (6). Student
-        # per group: fwd gather+pool q, k, embed, logits, select, transposed
-        # lists, gather v, attention, scatter (9 + 1), backward gather dO,
-        # prep, dq, dkdv, scatter x3 (7).
-        'gpu_launches': args.steps * (
-            (6 * len(groups)) if fused else (1 + 4 * len(groups))) +
-            args.steps * 17 * len(groups),
-        'clocks': clocks.summary(),
-        'query_tile_heads': n_tiles,
-    }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        peaks = load_peaks()
+        peak = peaks['bf16_tflops']
+        # Per-GPU rates: each rank's share of the work over its stage time.
+        bwd_tflops = 2.5 * blocks * BLOCK_FLOPS / world / \
+            stages['student_bwd'] / 1e9
+        if fused:
+            achieved = fused_exec_flops / world / stages['teacher_fused'] / 1e9
+            stage_tflops = {
+                'teacher_fused_executed': achieved,
+                'teacher_reference_accounting': (dense_flops + heat_flops) /
+                                                world /
+                                                stages['teacher_fused'] / 1e9,
+                'student_bwd_attention_equiv': bwd_tflops}
+            kernel = ('bsa_fwd_kernel<heat> (fused dense + LSE + heat, '
+                      'executed FLOPs over tile-ordered rows)')
+        else:
+            achieved = dense_flops / world / stages['dense_fwd_lse'] / 1e9
+            stage_tflops = {
+                'dense_fwd_lse': achieved,
+                'heat': heat_flops / world / stages['heat'] / 1e9,
+                'student_bwd_attention_equiv': bwd_tflops}
+            kernel = 'bsa_fwd_kernel (dense mode)'
+        roofline = {'bound': 'tensor', 'kernel': kernel,
+                    'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s',
+                    'frac': achieved / peak, 'traffic': None,
+                    'peak_source': f'{peaks["source"]} bf16 burst'}
+        # Ours per step and rank. Teacher, separate: dense fwd, then per
+        # group gather_lse, gather q, k, heat (1 + 4 per group); fused: per
+        # group gather q, k, v, keep-all lists, fused pass, scatter (6).
+        # Student per group: fwd gather+pool q, k, embed, logits, select,
+        # transposed lists, gather v, attention, scatter (9 + 1), backward
+        # gather dO, prep, dq, dkdv, scatter x3 (7). Head split: 4 packing
+        # kernels around the forward exchanges and 4 around the backward's.
+        per_step = ((6 * len(groups)) if fused else (1 + 4 * len(groups))) \
+            + 17 * len(groups) + (8 if world > 1 else 0)
+        line = {
+            'metric': METRIC, 'value': ms, 'unit': 'ms/step',
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': False,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16',
+            'data': 'synthetic (seeded N(0,1) q/k/v and dO, random-init '
+                    'predictor N(0,0.02))',
+            'config': {'workload': f'{args.config}: {cfg["desc"]}',
+                       'heads': heads, 'seq_len': seq_len,
+                       'head_dim': 128,
+                       'parallelism': (f'ulysses-heads x{world}'
+                                       if world > 1 else 'single GPU'),
+                       'l2': 'inputs exceed L2 (q/k/v >> 126 MB)'},
+            'stages_ms': stages,
+            'computed_blocks': blocks,
+            'algorithmic_tflop': total / 1e12,
+            'effective_tflops': total / (ms * 1e-3) / 1e12,
+            'frac_of_peak': total / (ms * 1e-3) / 1e12 / peak / world,
+            'teacher': args.teacher,
+            'stage_tflops': stage_tflops,
+            'roofline': roofline,
+            'e2e': {'value': e2e_ms, 'unit': 'ms/step', 'steps': e2e_steps,
+                    'h2d_bytes_per_step': world * 4 * q.numel() * 2,
+                    'd2h_bytes_per_step': world * 4},
+            'gpu_launches': args.steps * world * per_step,
+            'clocks': clocks.summary(),
+            'query_tile_heads': int(qtile_heads),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def launches_per_step(clip, plan, heads_split, pieces=1):

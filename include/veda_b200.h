@@ -73,6 +73,15 @@ int veda_device_status(int32_t* status, int32_t reset);
  * n in [0, 128]. */
 int veda_set_sm_reserve(int32_t n);
 
+/* No counterpart in the reference (a property of this library's forward
+ * kernel). How the attention forward's softmax is organised: 2, two groups
+ * of warps on alternate key blocks of a query tile, each with its own
+ * accumulator, merged in the epilogue; 1 (default), one group of warps on
+ * every block with one accumulator. Both compute the same attention (fp32
+ * summation order differs). The fused dense + heat pass always runs 1.
+ * Process-wide; returns VEDA_ERR_INVALID for other values. */
+int veda_set_fwd_groups(int32_t groups);
+
 /* 1 when the current device is sm_100 (B200) and the library can run. */
 int veda_supported_device(void);
 

@@ -48,6 +48,7 @@ SIGNATURES = {
     'veda_last_error': (c_i32, [ctypes.c_char_p, ctypes.c_size_t]),
     'veda_device_status': (c_i32, [ctypes.POINTER(c_i32), c_i32]),
     'veda_set_sm_reserve': (c_i32, [c_i32]),
+    'veda_set_fwd_groups': (c_i32, [c_i32]),
     'veda_supported_device': (c_i32, []),
     'veda_build_layout': (c_i32, [ctypes.POINTER(Span), c_i32, c_i64, c_i64,
                                   c_i64, c_ptr, c_ptr, c_ptr]),

@@ -51,11 +51,17 @@ namespace veda {
 
 namespace {
 
-constexpr int kSoftmaxWarps = 16;
-constexpr int kProducerWarp = kSoftmaxWarps;
-constexpr int kMmaWarp = kSoftmaxWarps + 1;  // QK issuer, TMEM owner
-constexpr int kPvWarp = kSoftmaxWarps + 2;
-constexpr int kFwdThreads = 32 * (kSoftmaxWarps + 3);
+// Warp roles: the softmax warps (16 in one group, 8 in two groups), then
+// the TMA producer, the QK issuer (TMEM owner) and the PV issuer.
+template <bool kDual>
+struct Roles {
+  static constexpr int kSoftmax = kDual ? 8 : 16;
+  static constexpr int kProducer = kSoftmax;
+  static constexpr int kQk = kSoftmax + 1;
+  static constexpr int kPv = kSoftmax + 2;
+  static constexpr int kThreads = 32 * (kSoftmax + 3);
+};
+constexpr int kSoftmaxWarps = Roles<false>::kSoftmax;
 constexpr int kRing = 2;  // per K and V ring
 constexpr uint32_t kTileBytes = 32768;  // 128 x 128 bf16
 constexpr uint32_t kHalfBytes = 16384;  // 128 x 64 bf16 (one TMA box)
@@ -227,7 +233,7 @@ struct Block {
   int valid;   // valid key rows of the tile (128 when full)
   int blk;     // running block number of the slot (barrier phases)
   int ka;      // running number of non-empty items of the slot
-  bool first, last;
+  bool first, second, last;
 };
 
 // The work items of one slot, item by item and block by block. Every role
@@ -336,6 +342,7 @@ struct Stream {
     b.blk = blk;
     b.ka = ka;
     b.first = j == 0;
+    b.second = j == 1;
     b.last = j == len - 1;
     return b;
   }
@@ -417,6 +424,12 @@ __device__ __forceinline__ void row_sync(int id) {
   asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
 }
 
+// Two-group softmax: the two warps (one per group) of a row range, 64
+// threads (ids 1-4).
+__device__ __forceinline__ void quarter_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
 // Warp-uniform wait: tcgen05.ld/st after it are warp-wide instructions.
 __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity,
                                          volatile int* abort,
@@ -432,17 +445,26 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity,
 // barriers' phase), bit 4 (ka >> 1) & 1 (the parity of the Q buffer's
 // phase), bit 5 ka >= 1 (O held an earlier item).
 constexpr uint32_t kRecEnd = 1, kRecFirst = 2, kRecLast = 4, kRecItem = 8,
-                   kRecQPhase = 16, kRecLater = 32;
+                   kRecQPhase = 16, kRecLater = 32, kRecSecond = 64;
 
 __device__ __forceinline__ uint32_t block_record(const Block& b) {
-  return (b.first ? kRecFirst : 0u) | (b.last ? kRecLast : 0u) |
+  return (b.first ? kRecFirst : 0u) | (b.second ? kRecSecond : 0u) |
+         (b.last ? kRecLast : 0u) |
          ((b.ka & 1) ? kRecItem : 0u) | (((b.ka >> 1) & 1) ? kRecQPhase : 0u) |
          (b.ka >= 1 ? kRecLater : 0u);
 }
 
-template <bool kHeat>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+// kDual: the two-group softmax (see the comment at the softmax role). S
+// buffers: three with one O, two (one per group) with two O accumulators.
+template <bool kHeat, bool kDual>
+__global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ FwdMaps maps, FwdParams p) {
+  static_assert(!(kHeat && kDual), "the fused heat uses the one-group path");
+  constexpr uint32_t kSB = kDual ? 2u : static_cast<uint32_t>(kSBufs);
+  constexpr int kSoftmaxN = Roles<kDual>::kSoftmax;
+  constexpr int kProducerWarp = Roles<kDual>::kProducer;
+  constexpr int kMmaWarp = Roles<kDual>::kQk;
+  constexpr int kPvWarp = Roles<kDual>::kPv;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -467,8 +489,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (tid == 0) {
     for (int b = 0; b < kNumBars; ++b) {
       uint32_t count = 1;
-      if (b >= kPFull0 && b < kPFull1 + kSBufs) count = kSoftmaxWarps / 2;
-      if (b == kOFree || b == kHeatIn || b == kHeatOut) count = kSoftmaxWarps;
+      // P halves: 8 warps (one group), or P of the whole block: the 4
+      // warps of one group (two groups).
+      if (b >= kPFull0 && b < kPFull1 + kSBufs)
+        count = kDual ? 4 : kSoftmaxN / 2;
+      if (b == kOFree || b == kHeatIn || b == kHeatOut) count = kSoftmaxN;
       mbar_init(&bars[b], count);
     }
     *abort = 0;
@@ -647,11 +672,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         break;
       const uint32_t rec = k_rec[slot];
       if (rec & kRecEnd) break;
-      const uint32_t sb = b % kSBufs;
+      const uint32_t sb = b % kSB;
       const uint32_t qb = (rec & kRecItem) ? 1u : 0u;
-      // S[sb] held P of block b - 3: its PV must have finished.
-      if (b >= kSBufs && !wait_all(&bars[kPVDone + sb],
-                                   ((b / kSBufs) - 1) & 1, abort, p.status))
+      // S[sb] held P of block b - kSB: its PV must have finished.
+      if (b >= kSB && !wait_all(&bars[kPVDone + sb],
+                                ((b / kSB) - 1) & 1, abort, p.status))
         break;
       if ((rec & kRecFirst) &&
           !wait_all(&bars[kQFull + qb], (rec & kRecQPhase) ? 1u : 0u, abort,
@@ -682,16 +707,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // V steps advance 16 key rows (2 KB) in the MN-major V tile.
     const uint32_t v_lo = sw128_desc_lo(smem_u32(s_v), kHalfBytes);
     constexpr uint32_t kTileUnits = kTileBytes >> 4;
-    const uint32_t t_o = tmem + kSBufs * 128;
+    const uint32_t t_o0 = tmem + kSB * 128;
     for (uint32_t b = 0;; ++b) {
       const int slot = b % kRing;
       if (!wait_all(&bars[kVFull + slot], (b / kRing) & 1, abort, p.status))
         break;
       const uint32_t rec = v_rec[slot];
       if (rec & kRecEnd) break;
-      const uint32_t sb = b % kSBufs;
-      const uint32_t spar = (b / kSBufs) & 1;
+      const uint32_t sb = b % kSB;
+      const uint32_t spar = (b / kSB) & 1;
       const bool first = rec & kRecFirst;
+      // Two groups: block b accumulates into O[b % 2], which an item first
+      // writes at its block 0 or 1.
+      const uint32_t t_o = kDual ? t_o0 + sb * 128 : t_o0;
+      const bool fresh = kDual ? (rec & (kRecFirst | kRecSecond)) != 0 : first;
       // The item's first PV overwrites O: the epilogue must have read the
       // previous item's.
       if (first && (rec & kRecLater) &&
@@ -701,19 +730,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (!wait_all(&bars[kPFull0 + sb], spar, abort, p.status)) break;
       tc_fence_after();
       const uint32_t bv = v_lo + slot * kTileUnits;
+      // Two groups: P of the whole block is in columns [0, 64) of S[sb],
+      // written at once.
       const uint32_t t_p = tmem + sb * 128;
-      // P of key step kk (16 keys, 8 columns) lies in the first 16 columns
-      // of its key quarter's 32.
+      // P of key step kk (16 keys, 8 columns): one group, the first 16
+      // columns of its key quarter's 32; two groups, columns 8 kk.
+      auto p_col = [](int kk) -> uint32_t {
+        return kDual ? kk * 8 : (kk >> 1) * 32 + (kk & 1) * 8;
+      };
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
-                     idesc_pv, (kk > 0 || !first) ? 1u : 0u);
-      if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) break;
-      tc_fence_after();
+        umma_ts_warp(t_o, t_p + p_col(kk), bv + kk * 128, idesc_pv,
+                     (kk > 0 || !fresh) ? 1u : 0u);
+      if (!kDual) {
+        if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) break;
+        tc_fence_after();
+      }
 #pragma unroll
       for (int kk = 4; kk < 8; ++kk)
-        umma_ts_warp(t_o, t_p + (kk >> 1) * 32 + (kk & 1) * 8, bv + kk * 128,
-                     idesc_pv, 1u);
+        umma_ts_warp(t_o, t_p + p_col(kk), bv + kk * 128, idesc_pv, 1u);
       umma_commit_warp(&bars[kVEmpty + slot]);
       umma_commit_warp(&bars[kPVDone + sb]);
       if (rec & kRecLast) umma_commit_warp(&bars[kODone]);
@@ -722,6 +757,230 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       volatile int never = 0;
       umma_commit_warp(&bars[kDrainPv]);
       mbar_wait(&bars[kDrainPv], 0, &never, nullptr);
+    }
+  } else if constexpr (kDual) {
+    // -------------- softmax + epilogue, two groups (warps 0-7) -------------
+    // Group g = warp / 4 takes the blocks whose running number blk has
+    // parity g: S[g] (TMEM columns 128 g) and its own accumulator O[g]
+    // (columns 256 + 128 g), with its own running maximum and row sums.
+    // While one group loads S and stores P, the other computes
+    // exponentials, so the chain through tensor memory of one block hides
+    // behind the arithmetic of the next. Warp w serves query row
+    // 32 (w % 4) + lane (its TMEM lane) over all 128 keys of its blocks: no
+    // maxima cross warps. The epilogue merges the two accumulators:
+    //   O = (O0 2^(m0 - m) + O1 2^(m1 - m)) / (l0 2^(m0 - m) + l1 2^(m1 - m)).
+    const int grp = warp / 4;
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    // Per item (item parity): each group's maximum and row sum [grp][row].
+    float* xm = s_xchg;
+    float* xl = s_xchg + 2 * 2 * 128;
+    static_assert(2 * (2 * 2 * 128) <= kExchangeFloats, "exchange area");
+    const int quarter_bar = 1 + quarter;  // the two warps of a row: 64
+    const uint32_t t_o0 = tmem + 2 * 128 + lane_base;
+    const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+    Stream st;
+    st.init(p, blockIdx.x, gridDim.x, true);
+    auto part_kv = [&](int jj) -> int {
+      return p.part_idx[st.off + (st.pc - 1 - jj)];
+    };
+    // Valid keys [32 q32, 32 q32 + 32) of a prefix tile with `valid` real
+    // rows, as a bit mask.
+    auto count_word = [](int valid, int q32) -> uint32_t {
+      const int n = valid - q32 * 32;
+      return n >= 32 ? ~0u : (n <= 0 ? 0u : (1u << n) - 1u);
+    };
+    // Valid keys of block jj of the current item: the tile's real rows
+    // (0 for a full tile), or -1 with the packed mode's box masks.
+    auto block_valid = [&](int jj) -> int {
+      if (p.dense) {
+        const int64_t rest = p.used - static_cast<int64_t>(jj) * kTile;
+        return rest < kTile ? static_cast<int>(rest) : kTile;
+      }
+      if (jj >= st.pc) return kTile;
+      const int kv = part_kv(jj);
+      return p.key_mask != nullptr ? -1 - kv : p.valid_count[kv];
+    };
+    auto chunk_word = [&](int valid, int q32) -> uint32_t {
+      return valid < 0 ? p.key_mask[(-1 - valid) * 4 + q32]
+                       : count_word(valid, q32);
+    };
+    // Scores of the 32-key chunk q32, masked.
+    auto load_chunk = [&](uint32_t t_s, int q32, int valid, uint32_t* x) {
+      tmem_ld32(t_s + q32 * 32, x);
+      tmem_wait_ld();
+      if (valid != kTile) {
+        const uint32_t word = chunk_word(valid, q32);
+        float* f = reinterpret_cast<float*>(x);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (!((word >> c) & 1u)) f[c] = -INFINITY;
+      }
+    };
+    int items = 0;
+    bool ok = true;
+    while (ok && st.valid(p)) {
+      const int h = st.h, qt = st.qt, len = st.len, ka = st.ka;
+      const int blk0 = st.blk;
+      const int j0 = (blk0 & 1) == grp ? 0 : 1;  // this group's first block
+      float m_ref = -INFINITY;  // the group's running max, log2 units
+      float l = 0.f;            // the group's row sum
+      int vnext = j0 < len ? block_valid(j0) : kTile;
+      for (int j = j0; j < len; j += 2) {
+        const int valid = vnext;
+        // The next block's valid count loads while this block computes.
+        if (j + 2 < len) vnext = block_valid(j + 2);
+        const uint32_t use = static_cast<uint32_t>(blk0 + j) >> 1;
+        if (!wait_all(&bars[kSFull + grp], use & 1, abort, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_s = tmem + grp * 128 + lane_base;
+        // P of each 32-key chunk is computed against the running reference
+        // as soon as the chunk is loaded (P <= 2^8 while no maximum passes
+        // it by more than 8). A block whose maximum does pass it, and the
+        // group's first block of the item, take the reference from the
+        // block and compute P again from S, which stays in tensor memory
+        // until P is stored.
+        const bool first = j < 2;
+        const float2 negm2 = make_float2(-m_ref, -m_ref);
+        uint32_t pk[4][16];  // P, bf16 pairs, per chunk
+        float2 sums[4];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) {
+          uint32_t x[32];
+          load_chunk(t_s, q32, valid, x);
+          mx = fmaxf(mx, row_max32(reinterpret_cast<float*>(x)));
+          if (!first) {
+            sums[q32] = p32(x, reinterpret_cast<float*>(x), scale2, negm2);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[q32][i] = x[i];
+          }
+        }
+        const float mb = mx * p.scale_log2;
+        const bool grow = !first && mb > m_ref + 8.0f;
+        if (first || __any_sync(0xffffffffu, grow)) {
+          float alpha = 1.0f;
+          const float m_new = first || grow ? mb : m_ref;
+          if (!first) alpha = ex2_approx(m_ref - m_new);
+          m_ref = m_new;
+          const float2 negm = make_float2(-m_ref, -m_ref);
+#pragma unroll
+          for (int q32 = 0; q32 < 4; ++q32) {
+            uint32_t x[32];
+            load_chunk(t_s, q32, valid, x);
+            sums[q32] = p32(x, reinterpret_cast<float*>(x), scale2, negm);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[q32][i] = x[i];
+          }
+          if (!first) {
+            // O[grp] holds the group's previous block once its PV finished.
+            if (!wait_all(&bars[kPVDone + grp], (use - 1) & 1, abort,
+                          p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int q32 = 0; q32 < 4; ++q32)
+              rescale_o32(t_o0 + grp * 128 + q32 * 32, alpha);
+            l *= alpha;
+          }
+        }
+        // P of key 2i, 2i + 1 in column i of S[grp].
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) tmem_st16(t_s + q32 * 16, pk[q32]);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kPFull0 + grp]);
+        l += ((sums[0].x + sums[0].y) + (sums[1].x + sums[1].y)) +
+             ((sums[2].x + sums[2].y) + (sums[3].x + sums[3].y));
+      }
+      if (!ok) break;
+      st.j = len;
+      st.blk = blk0 + len;
+      // ---------------- epilogue of the item ----------------
+      const bool has0 = len >= ((blk0 & 1) == 0 ? 1 : 2);
+      const bool has1 = len >= ((blk0 & 1) == 1 ? 1 : 2);
+      const int ip = items & 1;
+      xm[(ip * 2 + grp) * 128 + row] = m_ref;
+      xl[(ip * 2 + grp) * 128 + row] = l;
+      quarter_sync(quarter_bar);
+      const float m0 = xm[(ip * 2) * 128 + row];
+      const float m1 = xm[(ip * 2 + 1) * 128 + row];
+      const float m = fmaxf(m0, m1);
+      const float f0 = has0 ? ex2_approx(m0 - m) : 0.f;
+      const float f1 = has1 ? ex2_approx(m1 - m) : 0.f;
+      const float l_row = xl[(ip * 2) * 128 + row] * f0 +
+                          xl[(ip * 2 + 1) * 128 + row] * f1;
+      const int64_t slot_row = static_cast<int64_t>(qt) * kTile + row;
+      int64_t out_off = -1;  // element offset of the row's output; -1: none
+      if (p.packed) {
+        const int64_t r = p.box_perm[slot_row];
+        const int64_t hg = p.head_ids[h];
+        // A head outside the tensors reads zeros (TMA bounds) and writes
+        // nothing.
+        if (r >= 0 && hg >= 0 && hg < p.total_heads)
+          out_off = r * p.out_stride_n + hg * p.out_stride_h;
+      } else if (!p.dense || slot_row < p.used) {
+        // Dense mode: rows >= used keep the zeros written before the launch.
+        out_off = slot_row * p.out_stride_n + h * p.out_stride_h;
+      }
+      if (len > 0 && !wait_all(&bars[kODone], ka & 1, abort, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv_l = len > 0 ? 1.0f / l_row : 0.f;
+      const float g0 = f0 * inv_l, g1 = f1 * inv_l;
+      // This warp writes output columns [64 grp, 64 grp + 64) of its row.
+      // An accumulator the item did not write holds an earlier item's
+      // values (or nothing) and is not read.
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int col = grp * 64 + half * 32;
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        uint32_t x[32];
+        if (has0) {
+          tmem_ld32(t_o0 + col, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(x[i]) * g0;
+        }
+        if (has1) {
+          tmem_ld32(t_o0 + 128 + col, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = fmaf(__uint_as_float(x[i]), g1, o[i]);
+        }
+        if (out_off >= 0) {
+          uint4* d4 = reinterpret_cast<uint4*>(p.out + out_off + col);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]),
+                               pack_bf16(o[8 * i + 2], o[8 * i + 3]),
+                               pack_bf16(o[8 * i + 4], o[8 * i + 5]),
+                               pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+        }
+      }
+      if (len > 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kOFree]);  // O may be overwritten
+      }
+      if (grp == 0 && p.lse != nullptr && out_off >= 0)
+        p.lse[slot_row * p.lse_stride_row + h * p.lse_stride_h] =
+            len > 0 ? (m + lg2_approx(l_row)) * 0.69314718055994531f
+                    : -INFINITY;
+      ++items;
+      st.next_item(p, true);
     }
   } else {
     // ---------------- softmax + epilogue (warps 0-15) ----------------
@@ -1035,13 +1294,18 @@ int sm_count() {
   return sms;
 }
 
-template <bool kHeat>
-int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
+// Which softmax the non-fused forward runs: the one-group one (default) or
+// the two-group one (veda_set_fwd_groups).
+int g_fwd_groups = 1;
+
+template <bool kHeat, bool kDual>
+int launch_fwd_variant(const FwdMaps& maps, const FwdParams& p,
+                       cudaStream_t stream) {
   static bool configured = false;
   const int sms = sm_count();
   if (sms == 0) return set_error(VEDA_ERR_CUDA, "no CUDA device");
   if (!configured) {
-    VEDA_CUDA(cudaFuncSetAttribute(bsa_fwd_kernel<kHeat>,
+    VEDA_CUDA(cudaFuncSetAttribute(bsa_fwd_kernel<kHeat, kDual>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemBytes));
     configured = true;
@@ -1057,8 +1321,21 @@ int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
       return set_error(VEDA_ERR_INVALID, "the work order has more CTAs than "
                                          "the device has SMs");
   }
-  bsa_fwd_kernel<kHeat><<<grid, kFwdThreads, kSmemBytes, stream>>>(maps, p);
+  bsa_fwd_kernel<kHeat, kDual>
+      <<<grid, Roles<kDual>::kThreads, kSmemBytes, stream>>>(
+      maps, p);
   return check_launch("bsa_fwd_kernel");
+}
+
+template <bool kHeat>
+int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
+  if constexpr (kHeat) {
+    return launch_fwd_variant<true, false>(maps, p, stream);
+  } else {
+    return g_fwd_groups == 2 ? launch_fwd_variant<false, true>(maps, p, stream)
+                             : launch_fwd_variant<false, false>(maps, p,
+                                                                stream);
+  }
 }
 
 }  // namespace
@@ -1386,4 +1663,11 @@ extern "C" int veda_bsa_fwd_packed(
   p.key_mask = kv_tile_order ? nullptr : key_mask;
   p.status = device_status_ptr();
   return launch_fwd<false>(maps, p, as_stream(stream));
+}
+
+extern "C" int veda_set_fwd_groups(int32_t groups) {
+  VEDA_REQUIRE(groups == 1 || groups == 2,
+               "the forward's softmax runs in 1 or 2 groups");
+  g_fwd_groups = groups;
+  return VEDA_OK;
 }

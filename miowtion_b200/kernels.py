@@ -183,6 +183,15 @@ def set_sm_reserve(n: int) -> None:
     _SM_RESERVE = n
 
 
+DEFAULT_FWD_GROUPS = 1
+
+
+def set_fwd_groups(groups: int) -> None:
+    """veda_set_fwd_groups: the forward's softmax in two groups of warps on
+    alternate key blocks (2, the default) or one group (1)."""
+    _lib.call('veda_set_fwd_groups', groups)
+
+
 def work_order(layout: tiling.TileLayout, n_heads: int,
                blocks: list[veda_mask.ColumnBlock],
                device: torch.device) -> torch.Tensor | None:

@@ -116,6 +116,34 @@ def heads_to_seq(y: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class _ToHeads(torch.autograd.Function):
+    """seq_to_heads as a differentiable op. The exchange is a permutation of
+    rows and heads across the ranks, so its adjoint is the inverse exchange:
+    the incoming gradient [S, H/P, D] goes back through heads_to_seq."""
+
+    @staticmethod
+    def forward(ctx, x, group):  # pylint: disable=arguments-differ
+        ctx.group = group
+        return seq_to_heads(x.contiguous(), group)
+
+    @staticmethod
+    def backward(ctx, grad):  # pylint: disable=arguments-differ
+        return heads_to_seq(grad.contiguous(), ctx.group), None
+
+
+class _ToSeq(torch.autograd.Function):
+    """heads_to_seq as a differentiable op; its adjoint is seq_to_heads."""
+
+    @staticmethod
+    def forward(ctx, y, group):  # pylint: disable=arguments-differ
+        ctx.group = group
+        return heads_to_seq(y.contiguous(), group)
+
+    @staticmethod
+    def backward(ctx, grad):  # pylint: disable=arguments-differ
+        return seq_to_heads(grad.contiguous(), ctx.group), None
+
+
 class UlyssesSparseStudent:
     """`AttentionFn` over sequence-sharded q, k, v [S/P, H, D] per rank.
 
@@ -169,6 +197,9 @@ class UlyssesSparseStudent:
                 self.student.plan.head_shape[layer_index]) != per:
             raise ValueError('the student plan does not hold this rank\'s '
                              f'{per} heads')
+        if torch.is_grad_enabled() and any(t.requires_grad
+                                           for t in (q, k, v)):
+            return self._run_grad(q, k, v, layer_index, rank, per)
         bounds = piece_bounds(per, self.pieces)
         reserve = self.reserve_sms if (world > 1 and len(bounds) > 1
                                        and self.piece_factory is None) else 0
@@ -179,6 +210,46 @@ class UlyssesSparseStudent:
         finally:
             if reserve:
                 kernels.set_sm_reserve(0)
+
+    def to_heads(self, x: torch.Tensor) -> torch.Tensor:
+        """[S/P, H, D] shard -> [S, H/P, D] (differentiable)."""
+        return _ToHeads.apply(x, self.group)
+
+    def to_seq(self, y: torch.Tensor) -> torch.Tensor:
+        """[S, H/P, D] -> [S/P, H, D] shard (differentiable)."""
+        return _ToSeq.apply(y, self.group)
+
+    def local(self, layer_index: int):
+        """The attention function of this rank's heads, in the head
+        layout (global predictor indices)."""
+        if self.student is None:
+            raise ValueError("local() needs the rank's SparseStudent")
+        per = len(self.student.plan.head_shape[layer_index])
+        rank = dist.get_rank(self.group)
+        return self._piece_student(layer_index, 0, per, rank * per)
+
+    def _run_grad(self, q, k, v, layer_index, rank, per):
+        """The differentiable layer (the stage-2 student step across
+        ranks): q, k, v go to the head layout through `_ToHeads`, the rank's
+        heads run the sparse layer with its autograd backward, and the
+        output returns through `_ToSeq`. The backward therefore exchanges
+        dO into the head layout, runs the sparse backward, and exchanges
+        dQ, dK, dV back to the sequence shards. Every rank builds the same
+        graph, so the backward's collectives come in the same order on
+        every rank. One piece: the backward has no overlap to gain."""
+        ev = (self.student.events if self.student is not None
+              else veda_attention._NO_EVENTS)  # pylint: disable=protected-access
+        t = ev.start('exchange')
+        qh, kh, vh = (self.to_heads(x) for x in (q, k, v))
+        ev.stop(t)
+        student = self._piece_student(layer_index, 0, per, rank * per)
+        if self.student is not None:
+            student.events = self.student.events
+        out = student(qh, kh, vh, layer_index)
+        t = ev.start('exchange')
+        out = self.to_seq(out)
+        ev.stop(t)
+        return out
 
     def _run(self, q, k, v, layer_index, world, rank, per, bounds):
         rows, _, dim = q.shape

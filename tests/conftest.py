@@ -4,7 +4,8 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-for path in (ROOT, os.path.join(ROOT, 'tests', 'golden')):
+for path in (ROOT, os.path.join(ROOT, 'tests'),
+             os.path.join(ROOT, 'tests', 'golden')):
     if path not in sys.path:
         sys.path.insert(0, path)
 
@@ -31,3 +32,19 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if 'gpu' in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter):
+    """The normalized parity errors the GPU tests measured, worst (relative
+    to its bound) first."""
+    import parity
+    if not parity.RECORDS:
+        return
+    rows = sorted(parity.RECORDS, key=lambda r: r[1] / r[2], reverse=True)
+    worst = rows[0]
+    terminalreporter.write_line(
+        f'parity: {len(rows)} normalized-error checks '
+        '(max|got-want|/max|want|); worst against its bound: '
+        f'{worst[0]} {worst[1]:.2e} (bound {worst[2]:.0e})')
+    for what, err, bound in rows[:10]:
+        terminalreporter.write_line(f'  {err:.2e} / {bound:.0e}  {what}')

@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import _lib
 from miowtion_b200 import kernels
 from miowtion_b200 import tiling
@@ -85,6 +86,9 @@ def test_backward_matches_oracle(padded, density):
         g = np32(g)
         np.testing.assert_allclose(g[real], w[real], rtol=3e-2, atol=3e-2,
                                    err_msg=f'd{name}')
+        parity.assert_rel(g, w, parity.GRAD,
+                          f'backward d{name}, padded layout, density '
+                          f'{density}', where=real)
         assert not (g[real] == 0).all(), f'd{name} is all zeros'
         if dense is not None:
             sparse_err = np.abs(g[real] - w[real]).max()
@@ -121,3 +125,67 @@ def test_backward_linear_in_dout(padded):
     for x, y in zip(a, b):
         torch.testing.assert_close(y.float(), 2 * x.float(), rtol=2e-2,
                                    atol=2e-2)
+
+
+def test_backward_full_size_cfg3_sampled_tiles():
+    """cfg3 group a at full size (788 tiles, 1024 text rows), one head,
+    lists from the selection kernel at the 90% budget: dQ of sampled query
+    tiles and dK / dV of sampled key tiles against the oracle. A query
+    tile's dQ needs only its own row of the mask; a key tile's dK / dV
+    needs every query tile that keeps it, so the oracle runs on exactly
+    those rows."""
+    from miowtion_b200 import mask as veda_mask
+    spec = inputs.BENCH_LAYOUTS['cfg3_a']
+    spans = [tiling.TiledSpan(st, tuple(g), tiling.TileShape(*sh))
+             for st, g, sh in spec['spans']]
+    lay = tiling.build_tile_layout(spans, spec['used'], spec['seq_len'], DEV)
+    ref = vo.build_tile_layout(
+        [vo.Span(st, tuple(g), tuple(sh)) for st, g, sh in spec['spans']],
+        spec['used'], spec['seq_len'])
+    q, k, v = (t.to(DEV) for t in inputs.qkv(spec['seq_len'], 2, 128, 91,
+                                              torch.bfloat16))
+    hd = torch.tensor([1], device=DEV)
+    qt, kt, vt = (tiling.gather_tiles(t, lay, hd) for t in (q, k, v))
+    blocks = veda_mask.column_blocks(lay, veda_mask.Budget(ratio=0.1))
+    scores = inputs.scores(1, lay.n_tiles, 23)[:, :lay.n_video_tiles]
+    lists = veda_mask.select_block_lists(scores.to(DEV), lay, blocks,
+                                         want_mask=True)
+    mask = lists.mask.bool()
+    dout = inputs.dout(qt.shape, 24).to(DEV)
+    dq, dk, dv = _grads(qt, kt, vt, mask, lay, dout)
+    torch.cuda.synchronize()
+    m = mask.cpu().numpy()
+    n = lay.n_tiles
+    tile_rows = lambda t: (np.asarray(t)[:, None] * 128 +  # noqa: E731
+                           np.arange(128)).reshape(-1)
+    real = ref.slot_valid.astype(bool)
+    # dQ of sampled query tiles: partial, full, last video and global.
+    qs = np.array(sorted({*ref.partial_tiles[:2].tolist(), 0, 411,
+                          lay.n_video_tiles - 1, n - 1}))
+    rows = tile_rows(qs)
+    want_dq, _, _ = vo.block_sparse_attention_bwd(
+        np32(qt)[rows], np32(kt), np32(vt), np32(dout)[rows], m[:, qs],
+        ref.valid_count)
+    ok = real[rows]
+    got_dq = np32(dq)[rows]
+    np.testing.assert_allclose(got_dq[ok], want_dq[ok], rtol=3e-2, atol=3e-2)
+    parity.assert_rel(got_dq, want_dq, parity.GRAD,
+                      'backward dq, cfg3 full size, sampled query tiles',
+                      where=ok)
+    # dK, dV of sampled key tiles (one partial), from every query tile
+    # that keeps them.
+    ks = np.array(sorted({int(ref.partial_tiles[5]), 300, 777}))
+    users = np.nonzero(m[0][:, ks].any(-1))[0]
+    urows = tile_rows(users)
+    _, want_dk, want_dv = vo.block_sparse_attention_bwd(
+        np32(qt)[urows], np32(kt), np32(vt), np32(dout)[urows],
+        m[:, users], ref.valid_count)
+    krows = tile_rows(ks)
+    kok = real[krows]
+    for name, got, want in (('dk', dk, want_dk), ('dv', dv, want_dv)):
+        g, w = np32(got)[krows], want[krows]
+        np.testing.assert_allclose(g[kok], w[kok], rtol=3e-2, atol=3e-2,
+                                   err_msg=name)
+        parity.assert_rel(g, w, parity.GRAD,
+                          f'backward {name}, cfg3 full size, sampled key '
+                          'tiles', where=kok)

@@ -11,6 +11,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import _lib
 from miowtion_b200 import attention as veda_attention
 from miowtion_b200 import compensation
@@ -83,6 +84,8 @@ def test_compensation_matches_oracle(padded):
     want = oracle_out(ref, qt, kt, vt, mask)
     valid = ref.slot_valid.astype(bool)
     np.testing.assert_allclose(np32(got)[valid], want[valid], **TOL)
+    parity.assert_rel(np32(got), want, parity.FWD,
+                      'zero-order compensation', where=valid)
     assert (got.float() - o_kept.float()).abs().max() > 1e-2
     # End to end, and in place, give the same bits.
     e2e = compensation.attention(qt, kt, vt, m, lay)
@@ -114,6 +117,8 @@ def test_query_tile_subset(padded):
     want = oracle_out(ref, qt, kt, vt, mask[:, rows], rows=rows)
     valid = ref.slot_valid.astype(bool)[slots.cpu().numpy()]
     np.testing.assert_allclose(np32(got)[valid], want[valid], **TOL)
+    parity.assert_rel(np32(got), want, parity.FWD,
+                      'zero-order compensation', where=valid)
     with pytest.raises(ValueError, match='same id'):
         compensation.compensate(o_kept, lse, q_sub, kt, vt, m, lay)
 
@@ -136,6 +141,8 @@ def test_many_chunks_and_partial_last_chunk():
     want = oracle_out(ref, qt, kt, vt, mask[:, rows], rows=rows)
     valid = ref.slot_valid.astype(bool)[slots.cpu().numpy()]
     np.testing.assert_allclose(np32(got)[valid], want[valid], **TOL)
+    parity.assert_rel(np32(got), want, parity.FWD,
+                      'zero-order compensation', where=valid)
 
 
 def test_sparse_student_compensation_arm():

@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import _lib
 from miowtion_b200 import heatmap
 from miowtion_b200 import tiling
@@ -63,6 +64,7 @@ def test_heat_matches_oracle(teacher, reduce):
                            round_scores=True)
     atol = 1e-5 if reduce == 'max' else 1e-4
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=3e-2, atol=atol)
+    parity.assert_rel(got, want, 3e-2, f'teacher heat ({reduce})')
     assert (got > 0).any()
 
 
@@ -75,6 +77,7 @@ def test_heat_row_subset_and_order(teacher):
     want = vo.teacher_heat(np32(qt), np32(kt), lse_t, ref, q_tiles, 'max',
                            round_scores=True)
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=3e-2, atol=1e-5)
+    parity.assert_rel(got, want, 3e-2, 'teacher heat (max), query subset')
 
 
 def test_heat_mass_rows_sum_to_valid_rows(teacher):
@@ -130,6 +133,8 @@ def test_fused_dense_heat_matches_oracle(fused_case, reduce):
     valid = ref.slot_valid.astype(bool)
     np.testing.assert_allclose(np32(out)[valid], out_t[valid], rtol=2e-2,
                                atol=2e-2)
+    parity.assert_rel(np32(out), out_t, parity.FWD,
+                      f'fused dense + heat ({reduce}): output', where=valid)
     np.testing.assert_allclose(np32(lse).T[valid], lse_t[valid], atol=2e-3)
     want = vo.teacher_heat(np32(qt), np32(kt), lse_t, ref,
                            np.arange(lay.n_tiles), reduce,
@@ -137,6 +142,7 @@ def test_fused_dense_heat_matches_oracle(fused_case, reduce):
     atol = 1e-5 if reduce == 'max' else 1e-4
     np.testing.assert_allclose(heat.cpu().numpy(), want, rtol=3e-2,
                                atol=atol)
+    parity.assert_rel(heat, want, 3e-2, f'fused dense + heat ({reduce}): heat')
     # The separate heat kernel on the fused pass's own LSE agrees closely.
     sep = heatmap.teacher_heat(qt, kt, lse.T.contiguous(), lay,
                                torch.arange(lay.n_tiles), reduce)

@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import _lib
 from miowtion_b200 import kernels
 from miowtion_b200 import mask as veda_mask
@@ -156,6 +157,7 @@ def test_predictor_logits_match_oracle(padded):
                                pq.numpy(), pk.numpy(), heads.cpu().numpy())
     np.testing.assert_allclose(logits.cpu().numpy(), want, rtol=1e-4,
                                atol=1e-5)
+    parity.assert_rel(logits, want, 1e-4, 'predictor logits')
 
 
 # --- a5-a8: selection and lists --------------------------------------------
@@ -270,6 +272,9 @@ def test_block_sparse_forward_matches_oracle(padded, density):
     real = ref.slot_valid.astype(bool)
     np.testing.assert_allclose(np32(out)[real], want[real], rtol=2e-2,
                                atol=2e-2)
+    parity.assert_rel(np32(out), want, parity.FWD,
+                      f'sparse forward, padded layout, density {density}',
+                      where=real)
     got_lse = lse.cpu().numpy()
     assert np.isneginf(got_lse[:, 5 * 128:6 * 128]).all()
     assert (np32(out)[5 * 128:6 * 128] == 0).all()
@@ -301,6 +306,7 @@ def test_dense_attention_matches_oracle():
     want, want_lse = vo.dense_attention(np32(q), np32(k), np32(v), used,
                                         return_lse=True)
     np.testing.assert_allclose(np32(out), want, rtol=2e-2, atol=2e-2)
+    parity.assert_rel(np32(out), want, parity.FWD, 'dense forward')
     np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=0,
                                atol=2e-3)
     assert (np32(out)[used:] == 0).all() and (lse[used:] == 0).all()
@@ -326,6 +332,8 @@ def test_large_uniform_lists_forward():
     want = vo.block_sparse_attention(np32(qt)[sub], np32(kt), np32(vt),
                                      mask[:, rows], ref.valid_count)
     np.testing.assert_allclose(np32(out)[sub], want, rtol=2e-2, atol=2e-2)
+    parity.assert_rel(np32(out)[sub], want, parity.FWD,
+                      'sparse forward, cfg2 lists, sampled query tiles')
 
 
 def test_lse_is_natural_log():
@@ -334,3 +342,90 @@ def test_lse_is_natural_log():
     s = (q.float()[:, 0] @ k.float()[:, 0].T) / math.sqrt(128)
     torch.testing.assert_close(lse[:, 0], torch.logsumexp(s, -1), rtol=0,
                                atol=2e-3)
+
+
+# --- the forward's two softmax organisations ---------------------------------
+
+@pytest.fixture
+def fwd_groups():
+    """Sets the forward's softmax groups for one test; restores the
+    default."""
+    def set_groups(g):
+        kernels.set_fwd_groups(g)
+    yield set_groups
+    kernels.set_fwd_groups(kernels.DEFAULT_FWD_GROUPS)
+
+
+@pytest.mark.parametrize('density', [0.3, 1.0])
+def test_softmax_groups_agree_and_match_oracle(padded, fwd_groups, density):
+    """Two groups on alternate key blocks (own accumulators, merged at the
+    end) and one group on every block compute the same attention and LSE;
+    both match the oracle."""
+    spec, lay, ref, q, k, v, heads = padded
+    qt, kt, vt = (tiling.gather_tiles(t, lay, heads) for t in (q, k, v))
+    mask = _random_mask(heads.numel(), lay, density, 33)
+    mask[:, 4, 1:] = False  # a query tile with a single key tile
+    mask[:, 6, :] = False   # and one with none
+    outs = {}
+    for g in (1, 2):
+        fwd_groups(g)
+        outs[g] = kernels.block_sparse_attention(qt, kt, vt, mask.to(DEV),
+                                                 lay, return_lse=True)
+    want, want_lse = vo.block_sparse_attention(
+        np32(qt), np32(kt), np32(vt), mask.numpy(), ref.valid_count,
+        return_lse=True)
+    real = ref.slot_valid.astype(bool)
+    for g, (out, lse) in outs.items():
+        parity.assert_rel(np32(out), want, parity.FWD,
+                          f'sparse forward, {g} softmax group(s), density '
+                          f'{density}', where=real)
+        got_lse = lse.cpu().numpy()
+        fin = np.isfinite(want_lse)
+        np.testing.assert_allclose(got_lse[:, real][fin[:, real]],
+                                   want_lse[:, real][fin[:, real]], rtol=0,
+                                   atol=2e-3)
+        assert np.isneginf(got_lse[:, 6 * 128:7 * 128]).all()
+        assert (np32(out)[6 * 128:7 * 128] == 0).all()
+    parity.assert_rel(np32(outs[2][0]), np32(outs[1][0]), 1e-2,
+                      'two softmax groups against one', where=real)
+
+
+def test_softmax_reference_jumps(padded, fwd_groups):
+    """Scores that grow from block to block by more than the lazy-rescale
+    threshold: the two-group softmax recomputes P against the new reference
+    and rescales its accumulator, as the one-group softmax does."""
+    spec, lay, ref, q, k, v, heads = padded
+    qt, kt, vt = (tiling.gather_tiles(t, lay, heads) for t in (q, k, v))
+    # Key tile j scaled by (1 + (n - 1 - j) / 2): the lists are walked from
+    # their ends, so later blocks reach far above the first block's
+    # maximum.
+    n = lay.n_tiles
+    scale = (1.0 + torch.arange(n - 1, -1, -1, dtype=torch.float32)
+             .repeat_interleave(128) / 2.0).to(DEV)
+    kt = (kt.float() * scale[:, None, None]).to(torch.bfloat16)
+    mask = _random_mask(heads.numel(), lay, 0.6, 35)
+    want = vo.block_sparse_attention(np32(qt), np32(kt), np32(vt),
+                                     mask.numpy(), ref.valid_count)
+    real = ref.slot_valid.astype(bool)
+    for g in (1, 2):
+        fwd_groups(g)
+        out = kernels.block_sparse_attention(qt, kt, vt, mask.to(DEV), lay)
+        parity.assert_rel(np32(out), want, parity.FWD,
+                          f'sparse forward with growing scores, {g} '
+                          'softmax group(s)', where=real)
+
+
+def test_dense_two_groups_match_oracle(fwd_groups):
+    q, k, v = qkv(1500, 2, 42)
+    used = 1300
+    want, want_lse = vo.dense_attention(np32(q), np32(k), np32(v), used,
+                                        return_lse=True)
+    for g in (1, 2):
+        fwd_groups(g)
+        out, lse = kernels.dense_attention(q, k, v, 128 ** -0.5, True,
+                                           used=used)
+        parity.assert_rel(np32(out), want, parity.FWD,
+                          f'dense forward, {g} softmax group(s)')
+        np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=0,
+                                   atol=2e-3)
+        assert (np32(out)[used:] == 0).all()

@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import _lib
 from miowtion_b200 import kernels
 from miowtion_b200 import tiling
@@ -163,6 +164,9 @@ def test_packed_forward_matches_tile_path_and_oracle(name, heads, kv_tiles):
     seq = np.zeros((spec['seq_len'] + 1, len(heads), 128), np.float32)
     vo.scatter_tiles(seq, want, ref, np.arange(len(heads)))
     np.testing.assert_allclose(sel, seq[:used], rtol=2e-2, atol=2e-2)
+    parity.assert_rel(sel, seq[:used], parity.FWD,
+                      f'packed forward ({kv_tiles or "boxes"}), {name}, '
+                      f'heads {heads}')
     # The empty query tile's rows are zero.
     if n > 3:
         rows = ref.perm[3 * 128:4 * 128]
@@ -202,6 +206,59 @@ def test_packed_forward_full_size_rows_cfg3():
     real = rows >= 0
     got = np32(out)[rows[real], 1]
     np.testing.assert_allclose(got, want[real][:, 0], rtol=2e-2, atol=2e-2)
+    parity.assert_rel(got, want[real][:, 0], parity.FWD,
+                      'packed forward, cfg3 group a full size, sampled tiles')
+
+
+def test_packed_forward_full_size_rows_cfg4():
+    """cfg4 (Ref2VA) at full size: the reference segment at 95% and the
+    target at 90% sparsity, lists from the selection kernel with both
+    segments' budgets; sampled query tiles of both segments (partial tiles
+    included) of the packed output against the oracle."""
+    from miowtion_b200 import mask as veda_mask
+    spec = inputs.BENCH_LAYOUTS['cfg4']
+    lay = tiling.build_tile_layout(spans_of(spec), spec['used'],
+                                   spec['seq_len'], DEV)
+    ref = oracle_layout(spec)
+    total = 2
+    q, k, v = (t.to(DEV) for t in inputs.qkv(spec['seq_len'], total, 128,
+                                             65, torch.bfloat16))
+    hd = torch.tensor([0], device=DEV)
+    ref_ratio, target_ratio = spec['budgets'][0]
+    blocks = veda_mask.column_blocks(lay, veda_mask.Budget(ratio=target_ratio),
+                                     veda_mask.Budget(ratio=ref_ratio))
+    scores = inputs.scores(1, lay.n_tiles, 17)[:, :lay.n_video_tiles]
+    lists = veda_mask.select_block_lists(scores.to(DEV), lay, blocks,
+                                         want_mask=True)
+    n_ref = 120  # (4,45,80) in (2,8,8) tiles: 2 x 6 x 10
+    # Every row keeps k_lo or k_lo + 1 key tiles of each column block:
+    # 5.32 per row of the reference segment's columns (95%), 68.70 of the
+    # target's (90%).
+    kept = lists.mask[0].cpu()
+    assert set(kept[:, :n_ref].sum(-1).tolist()) == {5, 6}
+    assert set(kept[:, n_ref:].sum(-1).tolist()) == {68, 69}
+    out = torch.zeros_like(q)
+    kernels.block_sparse_attention_packed(
+        q, tiling.gather_images(k, lay, hd), tiling.gather_images(v, lay, hd),
+        lists, lay, hd, out, kv_tiles='images')
+    partial = [t for t in ref.partial_tiles.tolist()]
+    sample = np.array(sorted({0, 57, n_ref - 1, n_ref, 500, lay.n_tiles - 1,
+                              *[t for t in partial if t < n_ref][:2],
+                              *[t for t in partial if t >= n_ref][:2]}))
+    q_rows = (sample[:, None] * 128 + np.arange(128)).reshape(-1)
+    qt, kt, vt = (tiling.gather_tiles(t, lay, hd) for t in (q, k, v))
+    mask = lists.mask.cpu().numpy().astype(bool)
+    want = vo.block_sparse_attention(np32(qt)[q_rows], np32(kt), np32(vt),
+                                     mask[:, sample], ref.valid_count)
+    rows = ref.perm[q_rows]
+    real = rows >= 0
+    got = np32(out)[rows[real], 0]
+    np.testing.assert_allclose(got, want[real][:, 0], rtol=2e-2, atol=2e-2)
+    parity.assert_rel(got, want[real][:, 0], parity.FWD,
+                      'packed forward, cfg4 full size, both segments')
+    in_ref = np.repeat(sample < n_ref, 128)[real]
+    parity.assert_rel(got[in_ref], want[real][in_ref, 0], parity.FWD,
+                      'packed forward, cfg4 reference-segment query tiles')
 
 
 def test_sm_reserve_changes_the_grid_not_the_result():

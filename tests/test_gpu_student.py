@@ -6,6 +6,7 @@ import pytest
 import torch
 
 import inputs
+import parity
 from miowtion_b200 import attention as veda_attention
 from miowtion_b200 import mask as veda_mask
 from miowtion_b200 import plan as veda_plan
@@ -65,6 +66,7 @@ def test_cfg1_layer_matches_oracle():
         spec['ratio'], spec['seed'])
     assert (info[0]['mask'].sum(-1) == 4).all()
     np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2)
+    parity.assert_rel(got, want, parity.FWD, 'SparseStudent layer, cfg1')
     assert student.calls == {'sparse': 1, 'dense': 0}
 
 
@@ -97,6 +99,8 @@ def test_two_shapes_text_rows_and_padding_match_oracle():
                                       grp['mask'])
     np.testing.assert_allclose(got[:used], want[:used], rtol=2e-2,
                                atol=2e-2)
+    parity.assert_rel(got[:used], want[:used], parity.FWD,
+                      'SparseStudent layer, two shapes with text rows')
 
 
 def test_student_backward_matches_oracle():
@@ -139,6 +143,8 @@ def test_student_backward_matches_oracle():
     for name, g, wnt in zip('qkv', got, want):
         np.testing.assert_allclose(g[:used], wnt[:used], rtol=3e-2, atol=3e-2,
                                    err_msg=f'd{name}')
+        parity.assert_rel(g[:used], wnt[:used], parity.GRAD,
+                          f'SparseStudent layer backward d{name}')
         assert (g[used:] == 0).all()
         assert not (g[:used] == 0).all()
 
@@ -188,6 +194,8 @@ def test_oracle_student_matches_oracle(target):
     used = spec['used']
     np.testing.assert_allclose(got.float().cpu().numpy()[:used], want[:used],
                                rtol=2e-2, atol=2e-2)
+    parity.assert_rel(got.float().cpu().numpy()[:used], want[:used],
+                      parity.FWD, 'OracleStudent layer')
     assert student.calls == {'sparse': 1, 'dense': 0}
 
 
@@ -202,6 +210,7 @@ def test_dense_attention_fn_matches_oracle():
                                  spec['used'])
     np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=2e-2,
                                atol=2e-2)
+    parity.assert_rel(got, want, parity.FWD, 'DenseAttention layer')
     with pytest.raises(ValueError):
         veda_attention.dense_attention(q.to(DEV), k.to(DEV), v.to(DEV),
                                        spec['used'], backend='nope')

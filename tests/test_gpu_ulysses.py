@@ -64,6 +64,43 @@ def test_pieced_layer_equals_plain_student(one_rank_group, pieces):
     assert torch.equal(got[:used], want[:used])
 
 
+def test_exchanged_layer_gradients_equal_plain_student(one_rank_group):
+    """The stage-2 student through the exchange (autograd across the NCCL
+    all-to-alls): output and dq, dk, dv equal the plain SparseStudent's bit
+    for bit on one rank. The multi-rank exchange of gradients is tested over
+    gloo on the CPU (tests/test_ulysses.py)."""
+    text, grid, heads = 130, (4, 12, 20), 4
+    used = text + grid[0] * grid[1] * grid[2]
+    seq_len = used + 14
+    layout = veda_attention.PackedLayout(
+        seq_len, used, (veda_attention.VideoSpan(text, grid),))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=0.3))
+    clip = veda_attention.ClipTiling(layout, config, DEV)
+    plan = veda_plan.TilePlan('u', grid, [tiling.TileShape(2, 8, 8),
+                                          tiling.TileShape(1, 8, 16)],
+                              [[0, 1, 1, 0]])
+    pred = veda_predictor.TileScorePredictor(1, heads, 128)
+    pq, pk = inputs.predictor_weights(heads, 128, 46, 0.02)
+    with torch.no_grad():
+        pred.layers[0].proj_q.copy_(pq)
+        pred.layers[0].proj_k.copy_(pk)
+    student = veda_attention.SparseStudent(clip, plan, pred.to(DEV))
+    q, k, v = (t.to(DEV) for t in inputs.qkv(seq_len, heads, 128, 47,
+                                             torch.bfloat16))
+    dout = inputs.dout(q.shape, 48).to(DEV)
+    runs = []
+    for fn in (student, ulysses.UlyssesSparseStudent(student)):
+        leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+        out = fn(*leaves, 0)
+        out.backward(dout)
+        runs.append([out.detach()] + [t.grad for t in leaves])
+    torch.cuda.synchronize()
+    for name, a, b in zip(('out', 'dq', 'dk', 'dv'), *runs):
+        assert torch.equal(a, b), name
+    assert runs[0][1][:used].abs().max() > 0
+
+
 @pytest.mark.parametrize('world,start,stop', [(2, 0, 24), (8, 0, 6),
                                               (4, 3, 9)])
 def test_head_blocks_pack_and_unpack_are_exact(world, start, stop):

@@ -48,6 +48,53 @@ class _PerHeadScale:
         return (q + k + v) * ids[None, :, None] + layer_index
 
 
+class _PerHeadSoftmax:
+    """Differentiable stand-in attention: softmax(q k^T / 4) v per local
+    head, one head at a time (the same arithmetic whichever heads a rank
+    holds), scaled by the global head id + 1."""
+
+    def __init__(self, first: int, local: int):
+        self.first = first
+        self.local = local
+
+    def __call__(self, q, k, v, layer_index):
+        assert q.shape == (SEQ, self.local, DIM)
+        outs = []
+        for j in range(self.local):
+            p = torch.softmax(q[:, j] @ k[:, j].T / 4.0, -1)
+            outs.append((p @ v[:, j]) * (self.first + j + 1))
+        return torch.stack(outs, 1)
+
+
+def _grad_worker(rank: int, world: int, port: int, errors) -> None:
+    """The exchanged layer's gradients on every rank equal the rows of the
+    one-process gradients of the same function over all heads."""
+    try:
+        os.environ['MASTER_ADDR'] = '127.0.0.1'
+        os.environ['MASTER_PORT'] = str(port)
+        dist.init_process_group('gloo', rank=rank, world_size=world)
+        shard = SEQ // world
+        rows = slice(rank * shard, (rank + 1) * shard)
+        q, k, v, dout = (_global(s) for s in (11, 12, 13, 14))
+        leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+        whole = _PerHeadSoftmax(0, HEADS)(*leaves, 0)
+        (whole * dout).sum().backward()
+        shards = [t[rows].clone().requires_grad_(True) for t in (q, k, v)]
+        fn = ulysses.UlyssesSparseStudent(
+            None, piece_factory=lambda layer, a, b, first: _PerHeadSoftmax(
+                first, b - a))
+        out = fn(*shards, 0)
+        assert torch.equal(out, whole.detach()[rows]), 'forward'
+        (out * dout[rows]).sum().backward()
+        for name, mine, full in zip('qkv', shards, leaves):
+            assert torch.equal(mine.grad, full.grad[rows]), f'd{name}'
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # surfaced by the parent
+        errors.put(f'rank {rank}: {e!r}')
+        raise
+
+
 def _worker(rank: int, world: int, port: int, errors) -> None:
     try:
         os.environ['MASTER_ADDR'] = '127.0.0.1'
@@ -82,12 +129,11 @@ def _worker(rank: int, world: int, port: int, errors) -> None:
         raise
 
 
-@pytest.mark.parametrize('world', [2, 4])
-def test_exchange_and_wrapper_gloo(world):
+def _spawn(target, world):
     ctx = mp.get_context('spawn')
     errors = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, errors))
+    procs = [ctx.Process(target=target, args=(r, world, port, errors))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -102,6 +148,18 @@ def test_exchange_and_wrapper_gloo(world):
     assert not alive, 'a rank did not finish'
     assert not msgs, '\n'.join(msgs)
     assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize('world', [2, 4])
+def test_exchange_and_wrapper_gloo(world):
+    _spawn(_worker, world)
+
+
+@pytest.mark.parametrize('world', [2, 4])
+def test_exchange_backward_gloo(world):
+    """The stage-2 student across ranks: gradients flow back through the
+    inverse exchanges (dO to the head layout, dQ / dK / dV to the shards)."""
+    _spawn(_grad_worker, world)
 
 
 def test_local_plan_splits_heads_in_contiguous_blocks():
