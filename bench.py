@@ -273,18 +273,135 @@ def cpu_baseline(cfg, budget_s=12.0, timed_steps=None):
     return per_head * cfg['heads'] * 1e3, len(times), threads, times
 
 
+def reference_layer_head(ref, cfg, head, sample_tiles, layouts, seed):
+    """One head of the layer through the reference's own CPU functions
+    (installed unmodified under baseline/_ref): build_tile_layout (cached per
+    shape, as the reference caches it), gather_tiles of q, k, v,
+    pool_tiles, LayerPredictor.forward, column_blocks, select_video_blocks,
+    dense_block_mask, scatter_tiles_, all at full size; the token-level
+    reference attention (kernels/reference.py:23-56) on `sample_tiles`
+    random query tiles, in chunks of 8 tiles (the function takes any
+    subset of query tiles with their mask rows). Returns (seconds of the
+    full-size stages, seconds of the sampled attention, tiles sampled,
+    tiles in the layout)."""
+    from miowtion.kernels import reference as rref
+    from miowtion.veda import mask as rmask
+    from miowtion.veda import predictor as rpred
+    from miowtion.veda import tiling as rtiling
+    seq_len, used = cfg['seq_len'], cfg['used']
+    shape = tuple(cfg['shapes'][cfg['head_shape'][head]])
+    if shape not in layouts:
+        spans = []
+        if cfg['cond'] is not None:
+            spans.append(rtiling.TiledSpan(cfg['cond'][0],
+                                           tuple(cfg['cond'][1]),
+                                           rtiling.TileShape(2, 8, 8)))
+        spans.append(rtiling.TiledSpan(cfg['target'][0],
+                                       tuple(cfg['target'][1]),
+                                       rtiling.TileShape(*shape)))
+        layouts[shape] = rtiling.build_tile_layout(spans, used, seq_len)
+    lay = layouts[shape]
+    gen = torch.Generator().manual_seed(cfg['seed'] * 31 + head)
+    q, k, v = (torch.randn(seq_len, 1, 128, generator=gen).to(torch.bfloat16)
+               for _ in range(3))
+    gen_w = torch.Generator().manual_seed(1000 + cfg['seed'])
+    pq = torch.randn(cfg['heads'], 384, 128, generator=gen_w) * 0.02
+    pk = torch.randn(cfg['heads'], 384, 128, generator=gen_w) * 0.02
+    pred = rpred.TileScorePredictor(1, 1, 128)
+    with torch.no_grad():
+        pred.layers[0].proj_q.copy_(pq[head:head + 1])
+        pred.layers[0].proj_k.copy_(pk[head:head + 1])
+    one = torch.tensor([0])
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        qt, kt, vt = (rtiling.gather_tiles(x, lay, one) for x in (q, k, v))
+        fq = rpred.pool_tiles(qt, lay)
+        fk = rpred.pool_tiles(kt, lay)
+        logits = pred.layers[0](fq, fk, one)
+        blocks = rmask.column_blocks(
+            lay, rmask.Budget(ratio=cfg['target_ratio']),
+            rmask.Budget(ratio=cfg['ref_ratio']) if cfg['ref_ratio'] else None)
+        sel = rmask.select_video_blocks(logits[:, :lay.n_video_tiles], lay,
+                                        blocks)
+        block_mask = rmask.dense_block_mask(sel, lay)
+        out = torch.zeros(seq_len + 1, 1, 128, dtype=torch.bfloat16)
+        rtiling.scatter_tiles_(out, qt, lay, one)  # a full-size scatter
+        t_stages = time.perf_counter() - t0
+        pick = torch.randperm(lay.n_tiles, generator=torch.Generator()
+                              .manual_seed(seed))[:sample_tiles].sort().values
+        t0 = time.perf_counter()
+        for c0 in range(0, pick.numel(), 8):
+            tiles = pick[c0:c0 + 8]
+            rows = (tiles[:, None] * 128 + torch.arange(128)).view(-1)
+            rref.block_sparse_attention(qt[rows], kt, vt,
+                                        block_mask[:, tiles],
+                                        lay.valid_count)
+        t_attn = time.perf_counter() - t0
+    return t_stages, t_attn, int(pick.numel()), lay.n_tiles
+
+
+def reference_cpu_ms(cfg, timed_steps=None, budget_s=12.0, sample_tiles=32):
+    """ms per layer of the reference's own CPU path (reference_layer_head),
+    one head per step, extrapolated: the sampled attention over all query
+    tiles, every head the cost of the heads timed. Returns (ms, steps,
+    threads, per-step ms, sample description) or None without the
+    reference installed."""
+    try:
+        ref = reference_package()
+    except Exception:  # pylint: disable=broad-except
+        ref = None
+    if ref is None:
+        return None
+    import threadpoolctl
+    cores = os.cpu_count() or 1
+    threadpoolctl.threadpool_limits(cores)
+    torch.set_num_threads(cores)
+    layouts: dict = {}
+    per_step = []
+    t_all = time.perf_counter()
+    head = 0
+    while True:
+        t_st, t_at, n_s, n_t = reference_layer_head(
+            ref, cfg, head, sample_tiles, layouts, seed=len(per_step))
+        per_step.append((t_st + t_at * n_t / n_s) * cfg['heads'] * 1e3)
+        head = (head + 1) % cfg['heads']
+        if timed_steps is not None:
+            if len(per_step) >= timed_steps:
+                break
+        elif time.perf_counter() - t_all > budget_s:
+            break
+    sample = (f'per step one head (of {cfg["heads"]}) through the '
+              "reference's own CPU functions (baseline/_ref, unmodified): "
+              'layout, gather, pool, predictor, selection, block mask and '
+              'scatter at full size; its token-level attention on '
+              f'{sample_tiles} random query tiles, scaled to all query '
+              f'tiles; x{cfg["heads"]} heads')
+    return per_step, cores, sample
+
+
 def run_reference(args, cfg):
+    """The reference arm: the reference's own CPU implementation of the
+    layer on the host cores (reference_cpu_ms), or the oracle port when the
+    reference is not installed. Rank 0 alone runs it."""
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
     warm = max(0, args.warmup)
     steps = max(1, args.steps)
-    _, _, threads, times = cpu_baseline(cfg, timed_steps=warm + steps)
-    timed = times[warm:]
-    ms = sum(timed) / len(timed) * cfg['heads'] * 1e3
-    sample = (f'per step one head (of {cfg["heads"]}) of the full layer '
-              f'through the oracle (numpy restatement of the reference), '
-              f'x{cfg["heads"]} heads')
+    got = reference_cpu_ms(cfg, timed_steps=warm + steps)
+    if got is not None:
+        per_step, threads, sample = got
+        timed = per_step[warm:]
+        ms = sum(timed) / len(timed)
+        kind = 'reference'
+    else:
+        _, _, threads, times = cpu_baseline(cfg, timed_steps=warm + steps)
+        timed = times[warm:]
+        ms = sum(timed) / len(timed) * cfg['heads'] * 1e3
+        kind = 'port'
+        sample = (f'per step one head (of {cfg["heads"]}) of the full layer '
+                  f'through the oracle (numpy restatement of the reference), '
+                  f'x{cfg["heads"]} heads')
     line = {
         'metric': METRIC, 'value': ms, 'unit': 'ms/layer', 'impl': 'reference',
         'n_gpus': args.gpus, 'steps': steps, 'warmup': warm,
@@ -293,7 +410,7 @@ def run_reference(args, cfg):
         'config': {'workload': f'{args.config}: {cfg["desc"]}',
                    'parallelism': 'cpu'},
         'cpu_baseline': {'value': ms, 'unit': 'ms/layer', 'cores': threads,
-                         'kind': 'port', 'sample': sample},
+                         'kind': kind, 'sample': sample},
         'e2e': {'value': ms, 'unit': 'ms/layer', 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }
@@ -522,13 +639,22 @@ def main():
         if comp is not None:
             line['comparators'] = comp
         if world == 1 and not args.no_cpu_baseline:
-            cpu_ms, n_heads, threads, _ = cpu_baseline(cfg)
-            line['cpu_baseline'] = {
-                'value': cpu_ms, 'unit': 'ms/layer', 'cores': threads,
-                'kind': 'port',
-                'sample': f'{n_heads} heads of {heads} through the oracle '
-                          '(numpy restatement), full layer per head, '
-                          'extrapolated linearly over heads'}
+            got = reference_cpu_ms(cfg)
+            if got is not None:
+                per_step, threads, sample = got
+                line['cpu_baseline'] = {
+                    'value': sum(per_step) / len(per_step),
+                    'unit': 'ms/layer', 'cores': threads,
+                    'kind': 'reference',
+                    'sample': f'{len(per_step)} steps: {sample}'}
+            else:
+                cpu_ms, n_heads, threads, _ = cpu_baseline(cfg)
+                line['cpu_baseline'] = {
+                    'value': cpu_ms, 'unit': 'ms/layer', 'cores': threads,
+                    'kind': 'port',
+                    'sample': f'{n_heads} heads of {heads} through the '
+                              'oracle (numpy restatement), full layer per '
+                              'head, extrapolated linearly over heads'}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

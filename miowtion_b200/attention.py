@@ -446,6 +446,9 @@ class SparseStudent:
     (attention.py:692-794)."""
 
     events = _NO_EVENTS  # set a StageEvents to time the stages
+    # Called (once per head group on the inference path) before v is first
+    # read; the head-parallel wrapper waits there for v's exchange.
+    v_ready = None
 
     def __init__(self, clip: ClipTiling, plan: veda_plan.TilePlan,
                  predictor: veda_predictor.TileScorePredictor,
@@ -475,12 +478,14 @@ class SparseStudent:
                  layer_index: int) -> torch.Tensor:
         used = self.clip.layout.used
         if layer_index in self.clip.config.dense_layers:
+            self._wait_v()
             self.calls['dense'] += 1
             return kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5,
                                            False, used=used)[0]
         self.calls['sparse'] += 1
         if torch.is_grad_enabled() and any(t.requires_grad
                                            for t in (q, k, v)):
+            self._wait_v()
             return self._attend_grad(q, k, v, layer_index)
         seq_len = q.shape[0]
         out = torch.empty_like(q)
@@ -498,6 +503,10 @@ class SparseStudent:
                              f'{q.shape[1]}')
         return out
 
+    def _wait_v(self) -> None:
+        if self.v_ready is not None:
+            self.v_ready()
+
     def _attend(self, q, k, v, layer_index: int,
                 tile_layout: tiling.TileLayout, heads: torch.Tensor,
                 out: torch.Tensor) -> None:
@@ -508,6 +517,7 @@ class SparseStudent:
                 and kernels.packed_supported(tile_layout)):
             self._attend_packed(q, k, v, layer_index, tile_layout, heads, out)
             return
+        self._wait_v()
         ev = self.events
         t = ev.start('permute_pool')
         q_tiles, feats_q, sq_q, _ = _gather_pool_moments(q, tile_layout,
@@ -564,7 +574,6 @@ class SparseStudent:
         feats_q = tiling.pool_features(q, tile_layout, heads)
         k_img, feats_k = tiling.gather_images(k, tile_layout, heads,
                                               pool=True)
-        v_img = tiling.gather_images(v, tile_layout, heads)
         ev.stop(t)
         with torch.no_grad():
             t = ev.start('score')
@@ -577,6 +586,12 @@ class SparseStudent:
                 logits[:, :tile_layout.n_video_tiles], tile_layout,
                 self.clip.blocks(tile_layout))
             ev.stop(t)
+        # v is first read here, after the scoring: a caller that is still
+        # receiving v (the head-parallel exchange) lets it arrive meanwhile.
+        self._wait_v()
+        t = ev.start('permute_pool')
+        v_img = tiling.gather_images(v, tile_layout, heads)
+        ev.stop(t)
         t = ev.start('attention')
         kernels.block_sparse_attention_packed(
             q, k_img, v_img, lists, tile_layout, heads, out,

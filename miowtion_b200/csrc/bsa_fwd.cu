@@ -105,8 +105,11 @@ enum Bar {
   kDrainPv = 27,
   kHeatIn = 28,     // fused heat: an item's row maxima / sums stored (16)
   kHeatOut = 29,    // fused heat: the item's heat written (16)
-  kNumBars = 30
+  kRefPub = 30,     // [4] two groups: block b's reference published (4)
+  kNumBars = 34
 };
+// Block records live after the barriers (and the TMEM slot / abort word).
+constexpr int kRecOffset = 40;  // in 8-byte units from the barriers
 
 struct FwdParams {
   int n_heads;
@@ -391,6 +394,19 @@ __device__ __forceinline__ void rescale_o32(uint32_t t_row, float alpha) {
   tmem_wait_st();
 }
 
+// O *= alpha for 16 columns of this thread's row (fewer live registers,
+// for the rare rescale of the two-group softmax).
+__device__ __forceinline__ void rescale_o16(uint32_t t_row, float alpha) {
+  uint32_t o[16];
+  tmem_ld16(t_row, o);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+  tmem_st16(t_row, o);
+  tmem_wait_st();
+}
+
 // P for this warp's 32 keys: x = s*c - m, exp2 on the MUFU (or, for the last
 // kPolyCols columns, on the FMA pipes), bf16 pairs into r[c/2]. Returns the
 // (fp32) sum of the exponentials.
@@ -454,13 +470,12 @@ __device__ __forceinline__ uint32_t block_record(const Block& b) {
          (b.ka >= 1 ? kRecLater : 0u);
 }
 
-// kDual: the two-group softmax (see the comment at the softmax role). S
-// buffers: three with one O, two (one per group) with two O accumulators.
+// kDual: the two-group softmax (see the comment at the softmax role).
 template <bool kHeat, bool kDual>
 __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ FwdMaps maps, FwdParams p) {
   static_assert(!(kHeat && kDual), "the fused heat uses the one-group path");
-  constexpr uint32_t kSB = kDual ? 2u : static_cast<uint32_t>(kSBufs);
+  constexpr uint32_t kSB = static_cast<uint32_t>(kSBufs);
   constexpr int kSoftmaxN = Roles<kDual>::kSoftmax;
   constexpr int kProducerWarp = Roles<kDual>::kProducer;
   constexpr int kMmaWarp = Roles<kDual>::kQk;
@@ -477,9 +492,12 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_xchg + kExchangeFloats);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  static_assert(kNumBars + 1 <= 32, "barriers overlap the block records");
+  static_assert(kNumBars + 1 <= kRecOffset,
+                "barriers overlap the block records");
+  static_assert(kRecOffset * 8 + 2 * kRing * 4 <= 512, "barrier area");
   // Block records beside the K and the V ring slots.
-  volatile uint32_t* k_rec = reinterpret_cast<volatile uint32_t*>(bars + 32);
+  volatile uint32_t* k_rec =
+      reinterpret_cast<volatile uint32_t*>(bars + kRecOffset);
   volatile uint32_t* v_rec = k_rec + kRing;
 
   const int tid = threadIdx.x;
@@ -493,6 +511,7 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       // warps of one group (two groups).
       if (b >= kPFull0 && b < kPFull1 + kSBufs)
         count = kDual ? 4 : kSoftmaxN / 2;
+      if (b >= kRefPub && b < kRefPub + 4) count = 4;
       if (b == kOFree || b == kHeatIn || b == kHeatOut) count = kSoftmaxN;
       mbar_init(&bars[b], count);
     }
@@ -717,10 +736,8 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       const uint32_t sb = b % kSB;
       const uint32_t spar = (b / kSB) & 1;
       const bool first = rec & kRecFirst;
-      // Two groups: block b accumulates into O[b % 2], which an item first
-      // writes at its block 0 or 1.
-      const uint32_t t_o = kDual ? t_o0 + sb * 128 : t_o0;
-      const bool fresh = kDual ? (rec & (kRecFirst | kRecSecond)) != 0 : first;
+      const uint32_t t_o = t_o0;
+      const bool fresh = first;
       // The item's first PV overwrites O: the epilogue must have read the
       // previous item's.
       if (first && (rec & kRecLater) &&
@@ -761,24 +778,31 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
   } else if constexpr (kDual) {
     // -------------- softmax + epilogue, two groups (warps 0-7) -------------
     // Group g = warp / 4 takes the blocks whose running number blk has
-    // parity g: S[g] (TMEM columns 128 g) and its own accumulator O[g]
-    // (columns 256 + 128 g), with its own running maximum and row sums.
-    // While one group loads S and stores P, the other computes
-    // exponentials, so the chain through tensor memory of one block hides
-    // behind the arithmetic of the next. Warp w serves query row
-    // 32 (w % 4) + lane (its TMEM lane) over all 128 keys of its blocks: no
-    // maxima cross warps. The epilogue merges the two accumulators:
-    //   O = (O0 2^(m0 - m) + O1 2^(m1 - m)) / (l0 2^(m0 - m) + l1 2^(m1 - m)).
+    // parity g, so the two groups work on consecutive blocks at once: while
+    // one loads S and stores P, the other computes exponentials. Warp w
+    // serves query row 32 (w % 4) + lane (its TMEM lane) over all 128 keys
+    // of its blocks, so no maxima cross warps inside a group. Both groups
+    // feed the one accumulator O with P against one running reference per
+    // row, handed from block to block through shared memory: block b's
+    // group publishes the reference it used (xref[b % 4], barrier
+    // kRefPub + b % 4), and block b + 1's group starts from it. A block
+    // takes its own maximum as the reference on the item's first block and
+    // when a row's maximum passes the reference by more than 8 (log2
+    // units); O is then rescaled once the PV of block b - 1 has finished
+    // (the PV of block b waits for P(b), which comes after). Each group
+    // keeps its row sum relative to the reference of its latest block; the
+    // epilogue brings both to the final (largest) reference.
     const int grp = warp / 4;
     const int quarter = warp % 4;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    // Per item (item parity): each group's maximum and row sum [grp][row].
-    float* xm = s_xchg;
-    float* xl = s_xchg + 2 * 2 * 128;
-    static_assert(2 * (2 * 2 * 128) <= kExchangeFloats, "exchange area");
-    const int quarter_bar = 1 + quarter;  // the two warps of a row: 64
-    const uint32_t t_o0 = tmem + 2 * 128 + lane_base;
+    float* xref = s_xchg;          // [4][128]
+    float* xm = s_xchg + 4 * 128;  // [item parity][grp][128]
+    float* xl = xm + 2 * 2 * 128;  // [item parity][grp][128]
+    static_assert(4 * 128 + 2 * (2 * 2 * 128) <= kExchangeFloats,
+                  "exchange area");
+    const int quarter_bar = 1 + quarter;  // the two warps of a row range
+    const uint32_t t_o = tmem + kSB * 128 + lane_base;
     const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
     Stream st;
     st.init(p, blockIdx.x, gridDim.x, true);
@@ -791,8 +815,8 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       const int n = valid - q32 * 32;
       return n >= 32 ? ~0u : (n <= 0 ? 0u : (1u << n) - 1u);
     };
-    // Valid keys of block jj of the current item: the tile's real rows
-    // (0 for a full tile), or -1 with the packed mode's box masks.
+    // Valid keys of block jj of the current item: the tile's real rows,
+    // or -1 - kv with the packed mode's box masks.
     auto block_valid = [&](int jj) -> int {
       if (p.dense) {
         const int64_t rest = p.used - static_cast<int64_t>(jj) * kTile;
@@ -802,16 +826,10 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       const int kv = part_kv(jj);
       return p.key_mask != nullptr ? -1 - kv : p.valid_count[kv];
     };
-    auto chunk_word = [&](int valid, int q32) -> uint32_t {
-      return valid < 0 ? p.key_mask[(-1 - valid) * 4 + q32]
-                       : count_word(valid, q32);
-    };
-    // Scores of the 32-key chunk q32, masked.
-    auto load_chunk = [&](uint32_t t_s, int q32, int valid, uint32_t* x) {
-      tmem_ld32(t_s + q32 * 32, x);
-      tmem_wait_ld();
+    auto mask_chunk = [&](uint32_t* x, int q32, int valid) {
       if (valid != kTile) {
-        const uint32_t word = chunk_word(valid, q32);
+        const uint32_t word = valid < 0 ? p.key_mask[(-1 - valid) * 4 + q32]
+                                        : count_word(valid, q32);
         float* f = reinterpret_cast<float*>(x);
 #pragma unroll
         for (int c = 0; c < 32; ++c)
@@ -824,99 +842,10 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       const int h = st.h, qt = st.qt, len = st.len, ka = st.ka;
       const int blk0 = st.blk;
       const int j0 = (blk0 & 1) == grp ? 0 : 1;  // this group's first block
-      float m_ref = -INFINITY;  // the group's running max, log2 units
-      float l = 0.f;            // the group's row sum
-      int vnext = j0 < len ? block_valid(j0) : kTile;
-      for (int j = j0; j < len; j += 2) {
-        const int valid = vnext;
-        // The next block's valid count loads while this block computes.
-        if (j + 2 < len) vnext = block_valid(j + 2);
-        const uint32_t use = static_cast<uint32_t>(blk0 + j) >> 1;
-        if (!wait_all(&bars[kSFull + grp], use & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t t_s = tmem + grp * 128 + lane_base;
-        // P of each 32-key chunk is computed against the running reference
-        // as soon as the chunk is loaded (P <= 2^8 while no maximum passes
-        // it by more than 8). A block whose maximum does pass it, and the
-        // group's first block of the item, take the reference from the
-        // block and compute P again from S, which stays in tensor memory
-        // until P is stored.
-        const bool first = j < 2;
-        const float2 negm2 = make_float2(-m_ref, -m_ref);
-        uint32_t pk[4][16];  // P, bf16 pairs, per chunk
-        float2 sums[4];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int q32 = 0; q32 < 4; ++q32) {
-          uint32_t x[32];
-          load_chunk(t_s, q32, valid, x);
-          mx = fmaxf(mx, row_max32(reinterpret_cast<float*>(x)));
-          if (!first) {
-            sums[q32] = p32(x, reinterpret_cast<float*>(x), scale2, negm2);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[q32][i] = x[i];
-          }
-        }
-        const float mb = mx * p.scale_log2;
-        const bool grow = !first && mb > m_ref + 8.0f;
-        if (first || __any_sync(0xffffffffu, grow)) {
-          float alpha = 1.0f;
-          const float m_new = first || grow ? mb : m_ref;
-          if (!first) alpha = ex2_approx(m_ref - m_new);
-          m_ref = m_new;
-          const float2 negm = make_float2(-m_ref, -m_ref);
-#pragma unroll
-          for (int q32 = 0; q32 < 4; ++q32) {
-            uint32_t x[32];
-            load_chunk(t_s, q32, valid, x);
-            sums[q32] = p32(x, reinterpret_cast<float*>(x), scale2, negm);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[q32][i] = x[i];
-          }
-          if (!first) {
-            // O[grp] holds the group's previous block once its PV finished.
-            if (!wait_all(&bars[kPVDone + grp], (use - 1) & 1, abort,
-                          p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int q32 = 0; q32 < 4; ++q32)
-              rescale_o32(t_o0 + grp * 128 + q32 * 32, alpha);
-            l *= alpha;
-          }
-        }
-        // P of key 2i, 2i + 1 in column i of S[grp].
-#pragma unroll
-        for (int q32 = 0; q32 < 4; ++q32) tmem_st16(t_s + q32 * 16, pk[q32]);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kPFull0 + grp]);
-        l += ((sums[0].x + sums[0].y) + (sums[1].x + sums[1].y)) +
-             ((sums[2].x + sums[2].y) + (sums[3].x + sums[3].y));
-      }
-      if (!ok) break;
-      st.j = len;
-      st.blk = blk0 + len;
-      // ---------------- epilogue of the item ----------------
-      const bool has0 = len >= ((blk0 & 1) == 0 ? 1 : 2);
-      const bool has1 = len >= ((blk0 & 1) == 1 ? 1 : 2);
-      const int ip = items & 1;
-      xm[(ip * 2 + grp) * 128 + row] = m_ref;
-      xl[(ip * 2 + grp) * 128 + row] = l;
-      quarter_sync(quarter_bar);
-      const float m0 = xm[(ip * 2) * 128 + row];
-      const float m1 = xm[(ip * 2 + 1) * 128 + row];
-      const float m = fmaxf(m0, m1);
-      const float f0 = has0 ? ex2_approx(m0 - m) : 0.f;
-      const float f1 = has1 ? ex2_approx(m1 - m) : 0.f;
-      const float l_row = xl[(ip * 2) * 128 + row] * f0 +
-                          xl[(ip * 2 + 1) * 128 + row] * f1;
+      float m_last = -INFINITY;  // reference of this group's latest block
+      float l = 0.f;             // this group's row sum, against m_last
+      // Output row of this thread's query row (packed mode: from the box
+      // layout, loaded here so that the epilogue does not wait for it).
       const int64_t slot_row = static_cast<int64_t>(qt) * kTile + row;
       int64_t out_off = -1;  // element offset of the row's output; -1: none
       if (p.packed) {
@@ -930,44 +859,135 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
         // Dense mode: rows >= used keep the zeros written before the launch.
         out_off = slot_row * p.out_stride_n + h * p.out_stride_h;
       }
+      int vnext = j0 < len ? block_valid(j0) : kTile;
+      for (int j = j0; j < len; j += 2) {
+        const int valid = vnext;
+        // The next block's valid count loads while this block computes.
+        if (j + 2 < len) vnext = block_valid(j + 2);
+        const uint32_t blk = static_cast<uint32_t>(blk0 + j);
+        const uint32_t sb = blk % kSB;
+        if (!wait_all(&bars[kSFull + sb], (blk / kSB) & 1, abort,
+                      p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_s = tmem + sb * 128 + lane_base;
+        // All 128 scores of the row in one round trip to tensor memory.
+        uint32_t x[4][32];
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) tmem_ld32(t_s + q32 * 32, x[q32]);
+        tmem_wait_ld();
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) {
+          mask_chunk(x[q32], q32, valid);
+          mx = fmaxf(mx, row_max32(reinterpret_cast<float*>(x[q32])));
+        }
+        const float mb = mx * p.scale_log2;
+        float m_use = mb;  // the item's first block: its own maximum
+        bool rescale = false;
+        float alpha = 1.0f;
+        if (j > 0) {
+          // The reference after block blk - 1 (the other group's).
+          const uint32_t pb = blk - 1;
+          if (!wait_all(&bars[kRefPub + (pb & 3)], (pb >> 2) & 1, abort,
+                        p.status)) {
+            ok = false;
+            break;
+          }
+          const float m_prev = xref[(pb & 3) * 128 + row];
+          const bool grow = mb > m_prev + 8.0f;
+          rescale = __any_sync(0xffffffffu, grow);
+          m_use = grow ? mb : m_prev;
+          if (rescale) alpha = ex2_approx(m_prev - m_use);
+        }
+        // Publish this block's reference before its exponentials.
+        xref[(blk & 3) * 128 + row] = m_use;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kRefPub + (blk & 3)]);
+        // P = 2^(s c - m_use), packed in place over the first 16 words of
+        // each chunk.
+        const float2 negm2 = make_float2(-m_use, -m_use);
+        float2 sums[4];
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32)
+          sums[q32] = p32(x[q32], reinterpret_cast<float*>(x[q32]), scale2,
+                          negm2);
+        if (rescale) {
+          // O holds the PV of every block before blk once the PV of blk - 1
+          // has finished; the PV of blk waits for this block's P.
+          const uint32_t pb = blk - 1;
+          if (!wait_all(&bars[kPVDone + pb % kSB], (pb / kSB) & 1, abort,
+                        p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int q16 = 0; q16 < 8; ++q16)
+            rescale_o16(t_o + q16 * 16, alpha);
+        }
+        // P of key 2i, 2i + 1 in column i of S[sb].
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) tmem_st16(t_s + q32 * 16, x[q32]);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kPFull0 + sb]);
+        // This group's row sum follows the reference.
+        if (m_use != m_last) l *= ex2_approx(m_last - m_use);
+        m_last = m_use;
+        l += ((sums[0].x + sums[0].y) + (sums[1].x + sums[1].y)) +
+             ((sums[2].x + sums[2].y) + (sums[3].x + sums[3].y));
+      }
+      if (!ok) break;
+      st.j = len;
+      st.blk = blk0 + len;
+      // ---------------- epilogue of the item ----------------
+      const int ip = items & 1;
+      xm[(ip * 2 + grp) * 128 + row] = m_last;
+      xl[(ip * 2 + grp) * 128 + row] = l;
+      quarter_sync(quarter_bar);
+      const float m0 = xm[(ip * 2) * 128 + row];
+      const float m1 = xm[(ip * 2 + 1) * 128 + row];
+      const float l0 = xl[(ip * 2) * 128 + row];
+      const float l1 = xl[(ip * 2 + 1) * 128 + row];
+      // The final reference is the larger one (references only grow).
+      const float m = fmaxf(m0, m1);
+      const float l_row = (l0 > 0.f ? l0 * ex2_approx(m0 - m) : 0.f) +
+                          (l1 > 0.f ? l1 * ex2_approx(m1 - m) : 0.f);
       if (len > 0 && !wait_all(&bars[kODone], ka & 1, abort, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const float inv_l = len > 0 ? 1.0f / l_row : 0.f;
-      const float g0 = f0 * inv_l, g1 = f1 * inv_l;
       // This warp writes output columns [64 grp, 64 grp + 64) of its row.
-      // An accumulator the item did not write holds an earlier item's
-      // values (or nothing) and is not read.
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int col = grp * 64 + half * 32;
-        float o[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        uint32_t x[32];
-        if (has0) {
-          tmem_ld32(t_o0 + col, x);
+        uint32_t o[32];
+        if (len > 0) {
+          tmem_ld32(t_o + col, o);
           tmem_wait_ld();
+        } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(x[i]) * g0;
-        }
-        if (has1) {
-          tmem_ld32(t_o0 + 128 + col, x);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            o[i] = fmaf(__uint_as_float(x[i]), g1, o[i]);
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
         if (out_off >= 0) {
           uint4* d4 = reinterpret_cast<uint4*>(p.out + out_off + col);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]),
-                               pack_bf16(o[8 * i + 2], o[8 * i + 3]),
-                               pack_bf16(o[8 * i + 4], o[8 * i + 5]),
-                               pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+            d4[i] = make_uint4(
+                pack_bf16(__uint_as_float(o[8 * i]) * inv_l,
+                          __uint_as_float(o[8 * i + 1]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 2]) * inv_l,
+                          __uint_as_float(o[8 * i + 3]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 4]) * inv_l,
+                          __uint_as_float(o[8 * i + 5]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 6]) * inv_l,
+                          __uint_as_float(o[8 * i + 7]) * inv_l));
         }
       }
       if (len > 0) {

@@ -267,6 +267,18 @@ class UlyssesSparseStudent:
                 bufs.append((send, recv))
             inputs[j] = (bufs, works)
 
+        def v_waiter(work):
+            # The student reads v only after scoring its heads from q and k:
+            # until then v's exchange runs beside the pooling, predictor and
+            # selection kernels.
+            done = []
+
+            def wait():
+                if not done:
+                    work.wait()
+                    done.append(True)
+            return wait
+
         # Stage timers (bench): the exchanges, packing included, on the
         # launching stream. With several pieces they overlap the attention.
         ev = (self.student.events if self.student is not None
@@ -279,19 +291,31 @@ class UlyssesSparseStudent:
             if j + 1 < len(bounds):
                 post_inputs(j + 1)
             bufs, works = inputs.pop(j)
-            for w in works:
+            student = self._piece_student(layer_index, start, stop,
+                                          rank * per)
+            # A SparseStudent waits for v itself, after scoring from q and
+            # k; any other attention function gets all three first.
+            defer_v = isinstance(student, veda_attention.SparseStudent)
+            for w in (works[:2] if defer_v else works):
                 w.wait()
             if j == 0:
                 ev.stop(t)
             c = stop - start
             qj, kj, vj = (recv.view(world * rows, c, dim)
                           for _, recv in bufs)
-            student = self._piece_student(layer_index, start, stop,
-                                          rank * per)
             if self.student is not None:
                 # Stage timers set on the rank's student cover its pieces.
                 student.events = self.student.events
-            result = student(qj, kj, vj, layer_index)
+            if defer_v:
+                wait_v = v_waiter(works[2])
+                student.v_ready = wait_v
+                try:
+                    result = student(qj, kj, vj, layer_index)
+                finally:
+                    student.v_ready = None
+                wait_v()  # a path that did not read v
+            else:
+                result = student(qj, kj, vj, layer_index)
             back = torch.empty_like(result).view(world, rows, c, dim)
             if j + 1 == len(bounds):
                 t = ev.start('exchange')
