@@ -427,7 +427,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-comparators', action='store_true',
                     help='skip the same-box GPU comparators (N=1)')
-    ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=1,
+    ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=2,
                     help="the attention forward's softmax: two groups of "
                          'warps on alternate key blocks (2) or one (1)')
     ap.add_argument('--only', choices=['backward', 'heat', 'compensation',

@@ -74,10 +74,10 @@ int veda_device_status(int32_t* status, int32_t reset);
 int veda_set_sm_reserve(int32_t n);
 
 /* No counterpart in the reference (a property of this library's forward
- * kernel). How the attention forward's softmax is organised: 2, two groups
- * of warps on alternate key blocks of a query tile, each with its own
- * accumulator, merged in the epilogue; 1 (default), one group of warps on
- * every block with one accumulator. Both compute the same attention (fp32
+ * kernel). How the attention forward's softmax is organised: 2 (default),
+ * two groups of warps on alternate key blocks of a query tile, feeding one
+ * accumulator with a running reference handed from block to block; 1, one
+ * group of warps on every block. Both compute the same attention (fp32
  * summation order differs). The fused dense + heat pass always runs 1.
  * Process-wide; returns VEDA_ERR_INVALID for other values. */
 int veda_set_fwd_groups(int32_t groups);

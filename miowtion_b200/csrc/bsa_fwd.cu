@@ -1314,9 +1314,9 @@ int sm_count() {
   return sms;
 }
 
-// Which softmax the non-fused forward runs: the one-group one (default) or
-// the two-group one (veda_set_fwd_groups).
-int g_fwd_groups = 1;
+// Which softmax the non-fused forward runs: the two-group one (default) or
+// the one-group one (veda_set_fwd_groups).
+int g_fwd_groups = 2;
 
 template <bool kHeat, bool kDual>
 int launch_fwd_variant(const FwdMaps& maps, const FwdParams& p,

@@ -183,7 +183,7 @@ def set_sm_reserve(n: int) -> None:
     _SM_RESERVE = n
 
 
-DEFAULT_FWD_GROUPS = 1
+DEFAULT_FWD_GROUPS = 2
 
 
 def set_fwd_groups(groups: int) -> None:
