@@ -835,14 +835,22 @@ def comparators(cfg, clip, plan, student, q, k, v, reps=3):
                 same['scatter_equal'] = bool(torch.equal(rbuf, buf))
                 theirs['scatter'] = _timed_ms(
                     lambda: rtg.scatter_tiles_(rbuf, qt, rl, heads), reps)
+                del rbuf, rqt, rfq
+            except Exception as exc:  # pylint: disable=broad-except
+                theirs['error'] = f'{type(exc).__name__}: {exc}'[:300]
+            try:
                 rheat = rbh.teacher_heat(qt, kt, lse_t, rl, rows, 'sum')
                 same['teacher_heat_rel_diff'] = _rel_err(heat, rheat)
                 theirs['teacher_heat_sum_all_query_tiles'] = _timed_ms(
                     lambda: rbh.teacher_heat(qt, kt, lse_t, rl, rows,
                                              'sum'), 1)
-                del rbuf, rqt, rfq, rheat
+                del rheat
             except Exception as exc:  # pylint: disable=broad-except
-                theirs['error'] = f'{type(exc).__name__}: {exc}'[:300]
+                # Triton 3.6 (the image's) fails to compile this kernel
+                # for sm_100: an MLIR pass error, not a wrong result.
+                theirs['teacher_heat_sum_all_query_tiles'] = (
+                    'unavailable: the Triton compile failed on this box '
+                    f'({type(exc).__name__}: {str(exc)[:120]})')
             res['reference_triton_ms'] = theirs
             res['agreement'] = same
             try:
@@ -852,21 +860,24 @@ def comparators(cfg, clip, plan, student, q, k, v, reps=3):
                 fo = flex.run(meta)
                 res['flex_attention_ms'] = _timed_ms(lambda: flex.run(meta),
                                                      reps)
-                # flex attends every row of a kept tile (the reference
-                # backend's BlockMask has no partial tiles), so compare the
-                # (query tile, head) pairs that are full and keep only full
-                # key tiles.
+                # The reference backend's BlockMask has no partial tiles:
+                # flex attends every slot of a kept tile, the zero padding
+                # keys included. This library's forward does the same when
+                # told every tile has 128 real rows, so compare against that
+                # on every row.
                 res['flex_note'] = (
                     'torch.compile(flex_attention) with the same kept '
                     'blocks as full blocks (the reference backend, '
-                    'kernels/bench.py:241-262); tile-ordered q, k, v')
-                mask = lists.mask.bool()
-                partial = (mask & ~tl.full_tile[None, None, :]).any(-1)
-                ok = (tl.full_tile[:, None] & ~partial.T).repeat_interleave(
-                    128, 0)[:, :, None]
-                diff = ((fo.float() - ot.float()).abs() * ok).max()
-                res['flex_rel_diff_full_tiles'] = float(
-                    diff / (ot.float().abs() * ok).max().clamp(min=1e-30))
+                    'kernels/bench.py:241-262); tile-ordered q, k, v; '
+                    'agreement against this library\'s forward with every '
+                    'tile taken as full')
+                import dataclasses
+                as_full = dataclasses.replace(
+                    tl, valid_count=torch.full_like(tl.valid_count, 128))
+                of = kernels.block_sparse_attention_lists(qt, kt, vt, lists,
+                                                          as_full)
+                res['flex_rel_diff'] = _rel_err(fo, of)
+                del of
                 del flex, meta, fo
             except Exception as exc:  # pylint: disable=broad-except
                 res['flex_attention_ms'] = (
