@@ -661,10 +661,11 @@ def main():
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) of one bsa_fwd_kernel launch, from one ncu
-# capture of the kernel at config 2 (dram__bytes_read.sum +
-# dram__bytes_write.sum). Other configs have no capture: null.
-FWD_TRAFFIC = {'cfg2': 864.7e6}
+# DRAM bytes (read + write) of one bsa_fwd_kernel launch (one head group),
+# from single-pass ncu captures of the two-group kernel
+# (dram__bytes_read.sum + dram__bytes_write.sum): config 2, and config 3 at
+# full size (3.40 GB + 0.565 GB per launch). Other configs: null.
+FWD_TRAFFIC = {'cfg2': 863.3e6, 'cfg3': 3.965e9}
 
 
 def dense_comparison(cfg, q, k, v, reps=3):
