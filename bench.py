@@ -427,6 +427,9 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-comparators', action='store_true',
                     help='skip the same-box GPU comparators (N=1)')
+    ap.add_argument('--exchange', choices=['nccl', 'copy'], default='copy',
+                    help='ulysses at N > 1: NCCL all-to-alls, or copy-engine '
+                         'copies between IPC-mapped buffers')
     ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=2,
                     help="the attention forward's softmax: two groups of "
                          'warps on alternate key blocks (2) or one (1)')
@@ -493,7 +496,8 @@ def main():
         shard = seq_len // world
         q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
         fn = ulysses.UlyssesSparseStudent(student, pieces=args.pieces,
-                                          reserve_sms=args.reserve_sms)
+                                          reserve_sms=args.reserve_sms,
+                                          transport=args.exchange)
     else:
         # The whole layer on this rank's own clip (clip 0 on one GPU).
         q, k, v = synthetic_qkv(cfg, seq_len, 0, device, clip=rank)
@@ -605,6 +609,8 @@ def main():
                                        if mode == 'clips' else
                                        f'ulysses-heads x{world}'),
                        'softmax_groups': args.fwd_groups,
+                       'exchange': (args.exchange if heads_split
+                                    else None),
                        'l2': 'inputs exceed L2 (q/k/v/tiles >> 126 MB)'},
             'effective_tflops': eff,
             'frac_of_peak': eff / peak,
@@ -656,6 +662,8 @@ def main():
                               'oracle (numpy restatement), full layer per '
                               'head, extrapolated linearly over heads'}
         print(json.dumps(line), flush=True)
+    if heads_split:
+        fn.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

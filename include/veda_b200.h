@@ -82,6 +82,33 @@ int veda_set_sm_reserve(int32_t n);
  * Process-wide; returns VEDA_ERR_INVALID for other values. */
 int veda_set_fwd_groups(int32_t groups);
 
+/* ---- head-parallel exchange on the copy engines ------------------------- */
+/* No counterpart in the reference (it runs one clip per GPU). Plumbing that
+ * lets the head-parallel wrapper move its shards between GPUs with the copy
+ * engines instead of kernels: the persistent attention holds every SM. */
+
+/* Bytes of a CUDA IPC memory handle. */
+#define VEDA_IPC_HANDLE_BYTES 64
+
+/* The IPC handle of the device allocation that holds ptr (which may point
+ * inside it, as tensors of a caching allocator do) and ptr's byte offset in
+ * it. The peer adds the offset to the base veda_ipc_open returns. */
+int veda_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+
+/* Maps another process's allocation (its veda_ipc_handle) into this one,
+ * enabling peer access; *base receives its address here. */
+int veda_ipc_open(const void* handle, void** base);
+
+/* Unmaps an allocation opened with veda_ipc_open. */
+int veda_ipc_close(void* base);
+
+/* Strided device-to-device copy (height rows of width bytes) on the copy
+ * engines, asynchronous on `stream`; either side may be another GPU's
+ * memory mapped with veda_ipc_open. */
+int veda_copy_2d(void* dst, int64_t dst_pitch, const void* src,
+                 int64_t src_pitch, int64_t width, int64_t height,
+                 void* stream);
+
 /* 1 when the current device is sm_100 (B200) and the library can run. */
 int veda_supported_device(void);
 

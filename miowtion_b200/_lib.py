@@ -49,6 +49,11 @@ SIGNATURES = {
     'veda_device_status': (c_i32, [ctypes.POINTER(c_i32), c_i32]),
     'veda_set_sm_reserve': (c_i32, [c_i32]),
     'veda_set_fwd_groups': (c_i32, [c_i32]),
+    'veda_ipc_handle': (c_i32, [c_ptr, c_ptr, c_ptr]),
+    'veda_ipc_open': (c_i32, [c_ptr, c_ptr]),
+    'veda_ipc_close': (c_i32, [c_ptr]),
+    'veda_copy_2d': (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64,
+                             c_ptr]),
     'veda_supported_device': (c_i32, []),
     'veda_build_layout': (c_i32, [ctypes.POINTER(Span), c_i32, c_i64, c_i64,
                                   c_i64, c_ptr, c_ptr, c_ptr]),

@@ -475,20 +475,37 @@ class SparseStudent:
         self.calls = {'sparse': 0, 'dense': 0}
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                 layer_index: int) -> torch.Tensor:
+                 layer_index: int, out: torch.Tensor | None = None
+                 ) -> torch.Tensor:
+        """`out` (not in the reference's AttentionFn): an optional
+        preallocated [S, H, D] output for the inference path, which the
+        layer then writes in place (the head-parallel wrapper passes a
+        buffer its peers read)."""
         used = self.clip.layout.used
+        grad = torch.is_grad_enabled() and any(t.requires_grad
+                                               for t in (q, k, v))
+        if out is not None and (grad or out.shape != q.shape or
+                                out.dtype != q.dtype or
+                                out.device != q.device or
+                                not out.is_contiguous()):
+            raise ValueError('out must be a contiguous tensor like q, and '
+                             'is for the inference path only')
         if layer_index in self.clip.config.dense_layers:
             self._wait_v()
             self.calls['dense'] += 1
-            return kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5,
-                                           False, used=used)[0]
+            result = kernels.dense_attention(q, k, v, q.shape[-1] ** -0.5,
+                                             False, used=used)[0]
+            if out is None:
+                return result
+            out.copy_(result)
+            return out
         self.calls['sparse'] += 1
-        if torch.is_grad_enabled() and any(t.requires_grad
-                                           for t in (q, k, v)):
+        if grad:
             self._wait_v()
             return self._attend_grad(q, k, v, layer_index)
         seq_len = q.shape[0]
-        out = torch.empty_like(q)
+        if out is None:
+            out = torch.empty_like(q)
         if used < seq_len:
             out[used:] = 0
         covered = 0

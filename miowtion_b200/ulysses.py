@@ -24,6 +24,8 @@ receive buffer [P, S/P, c, D] is then [S, c, D] in sequence order.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -144,6 +146,184 @@ class _ToSeq(torch.autograd.Function):
         return seq_to_heads(grad.contiguous(), ctx.group), None
 
 
+class CopyEngineExchange:
+    """The head-parallel exchange of one shard shape on the copy engines.
+
+    Every rank owns receive buffers for q, k and v ([S, H/P, D] each, the
+    rank's heads of every row) and a result buffer of the same shape, and
+    maps its peers' buffers through CUDA IPC. Inputs are pushed: rank r
+    copies rows [r S/P, (r + 1) S/P) of peer p's heads straight from its
+    [S/P, H, D] shard into p's receive buffer, one strided 2-D copy per
+    peer and tensor (no packing pass). Outputs are pulled: rank r copies its
+    rows of every peer's result buffer into the heads of its output shard.
+    The copies run on the copy engines, one stream per peer, and take no SM
+    from the attention.
+
+    Ordering between the ranks uses interprocess CUDA events (one per rank
+    and purpose: inputs pushed, q/k pushed, v pushed, receive buffers free,
+    result written, results pulled), waited on by the GPU streams; a host
+    barrier on a gloo group between each record and the peers' waits makes
+    the waits refer to this step's records. Every rank calls the same
+    barriers in the same order.
+    """
+
+    EVENTS = ('qk', 'v', 'free', 'result', 'pulled')
+
+    def __init__(self, rows: int, heads: int, dim: int, dtype: torch.dtype,
+                 device: torch.device, group=None, host_group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if heads % self.world:
+            raise ValueError('heads must divide by the world size')
+        self.rows, self.heads, self.dim = rows, heads, dim
+        self.per = heads // self.world
+        self.elem = torch.empty((), dtype=dtype).element_size()
+        self.device = device
+        self.host_group = host_group or dist.new_group(backend='gloo')
+        seq = rows * self.world
+        self.recv = torch.empty(3, seq, self.per, dim, dtype=dtype,
+                                device=device)
+        self.result = torch.empty(seq, self.per, dim, dtype=dtype,
+                                  device=device)
+        # One copy stream per peer (own rows included), so the copies to
+        # different GPUs run on different copy engines at once; `stream`
+        # joins them for the events.
+        self.stream = torch.cuda.Stream(device)
+        self.streams = [torch.cuda.Stream(device) for _ in range(self.world)]
+        lib = _lib.load()
+        mine = []
+        for buf in (self.recv, self.result):
+            handle = (ctypes.c_uint8 * 64)()
+            offset = ctypes.c_int64()
+            _lib.check(lib.veda_ipc_handle(ctypes.c_void_p(buf.data_ptr()),
+                                           handle, ctypes.byref(offset)),
+                       'veda_ipc_handle')
+            mine.append((bytes(handle), offset.value))
+        self.events = {name: torch.cuda.Event(interprocess=True)
+                       for name in self.EVENTS}
+        ev_handles = {name: e.ipc_handle() for name, e in self.events.items()}
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, (mine, ev_handles),
+                               group=self.host_group)
+        self._opened = []
+        self.peer_recv, self.peer_result, self.peer_events = [], [], []
+        for p, (bufs, evs) in enumerate(gathered):
+            if p == self.rank:
+                self.peer_recv.append(self.recv.data_ptr())
+                self.peer_result.append(self.result.data_ptr())
+                self.peer_events.append(self.events)
+                continue
+            addrs = []
+            for handle, offset in bufs:
+                base = ctypes.c_void_p()
+                raw = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+                _lib.check(lib.veda_ipc_open(raw, ctypes.byref(base)),
+                           'veda_ipc_open')
+                self._opened.append(base.value)
+                addrs.append(base.value + offset)
+            self.peer_recv.append(addrs[0])
+            self.peer_result.append(addrs[1])
+            self.peer_events.append({
+                name: torch.cuda.Event.from_ipc_handle(device, h)
+                for name, h in evs.items()})
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (after every rank's last use)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.host_group)
+        for base in self._opened:
+            _lib.call('veda_ipc_close', base)
+        self._opened = []
+
+    def _barrier(self) -> None:
+        dist.barrier(group=self.host_group)
+
+    @staticmethod
+    def _copy(stream, dst: int, dst_pitch: int, src: int, src_pitch: int,
+              width: int, height: int) -> None:
+        _lib.call('veda_copy_2d', dst, dst_pitch, src, src_pitch, width,
+                  height, stream.cuda_stream)
+
+    def _join(self) -> None:
+        for st in self.streams:
+            self.stream.wait_stream(st)
+
+    def run(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+            attend, v_wait=None, timers=None) -> torch.Tensor:
+        """One exchanged layer: `attend(q_h, k_h, v_h, out)` runs this
+        rank's heads on [S, H/P, D] views of the receive buffers and writes
+        `out` (the result buffer). With `v_wait`, `attend` receives a
+        callable that makes the current stream wait for v, to call at its
+        first read of v; otherwise all inputs are waited for first. Returns the [S/P, H, D] output
+        shard. `timers` (StageEvents) records 'exchange' on the current
+        stream: until q and k have arrived, and from the result until the
+        output shard is assembled."""
+        timers = timers or veda_attention._NO_EVENTS  # pylint: disable=protected-access
+        for t in (q, k, v):
+            if (t.shape != (self.rows, self.heads, self.dim) or
+                    not t.is_contiguous() or t.device != self.device):
+                raise ValueError('the exchange was set up for contiguous '
+                                 f'[{self.rows}, {self.heads}, {self.dim}] '
+                                 'shards on this device')
+        world, rank, per = self.world, self.rank, self.per
+        row_b = per * self.dim * self.elem        # one row of a head block
+        shard_b = self.heads * self.dim * self.elem  # one row of a shard
+        block_b = self.rows * row_b               # a rank's rows of a block
+        plane_b = world * block_b                 # one receive buffer
+        cur = torch.cuda.current_stream(self.device)
+        ev = self.events
+        tok = timers.start('exchange')
+        # Every rank has enqueued the previous layer (its buffer-free and
+        # pulled records) before anyone waits on them.
+        self._barrier()
+        for p, st in enumerate(self.streams):
+            st.wait_stream(cur)  # q, k, v are ready
+            st.wait_event(self.peer_events[p]['free'])
+        for t, x in enumerate((q, k, v)):
+            for p, st in enumerate(self.streams):
+                self._copy(st, self.peer_recv[p] + t * plane_b +
+                           rank * block_b, row_b, x.data_ptr() + p * row_b,
+                           shard_b, row_b, self.rows)
+            if t == 1:
+                self._join()
+                ev['qk'].record(self.stream)
+        self._join()
+        ev['v'].record(self.stream)
+        self._barrier()
+        for p in range(world):
+            cur.wait_event(self.peer_events[p]['qk'])
+            # The result buffer is free once every peer pulled the last one.
+            cur.wait_event(self.peer_events[p]['pulled'])
+        timers.stop(tok)
+
+        def wait_v():
+            for p in range(world):
+                cur.wait_event(self.peer_events[p]['v'])
+
+        if not v_wait:
+            wait_v()
+        q_h, k_h, v_h = self.recv.unbind(0)
+        attend(q_h, k_h, v_h, self.result, wait_v if v_wait else None)
+        wait_v()  # v arrived before the buffers count as free again
+        ev['result'].record(cur)
+        ev['free'].record(cur)
+        tok = timers.start('exchange')
+        self._barrier()
+        out = torch.empty_like(q)
+        for p, st in enumerate(self.streams):
+            st.wait_stream(cur)  # `out` is allocated on `cur`
+            st.wait_event(self.peer_events[p]['result'])
+            self._copy(st, out.data_ptr() + p * row_b, shard_b,
+                       self.peer_result[p] + rank * block_b, row_b, row_b,
+                       self.rows)
+        self._join()
+        ev['pulled'].record(self.stream)
+        cur.wait_stream(self.stream)
+        timers.stop(tok)
+        return out
+
+
 class UlyssesSparseStudent:
     """`AttentionFn` over sequence-sharded q, k, v [S/P, H, D] per rank.
 
@@ -157,7 +337,15 @@ class UlyssesSparseStudent:
 
     def __init__(self, student: veda_attention.SparseStudent | None,
                  group=None, pieces: int = 1, piece_factory=None,
-                 reserve_sms: int = 16):
+                 reserve_sms: int = 16, transport: str = 'nccl'):
+        """`transport`: 'nccl' (all-to-alls, with packing kernels) or 'copy'
+        (`CopyEngineExchange`: copy-engine copies between IPC-mapped
+        buffers; the inference path of CUDA tensors, one piece)."""
+        if transport not in ('nccl', 'copy'):
+            raise ValueError(f"transport must be 'nccl' or 'copy': "
+                             f'{transport!r}')
+        self.transport = transport
+        self._exchanges: dict = {}
         self.student = student
         self.group = group
         self.pieces = pieces
@@ -200,6 +388,8 @@ class UlyssesSparseStudent:
         if torch.is_grad_enabled() and any(t.requires_grad
                                            for t in (q, k, v)):
             return self._run_grad(q, k, v, layer_index, rank, per)
+        if self.transport == 'copy' and q.is_cuda:
+            return self._run_copy(q, k, v, layer_index, rank, per)
         bounds = piece_bounds(per, self.pieces)
         reserve = self.reserve_sms if (world > 1 and len(bounds) > 1
                                        and self.piece_factory is None) else 0
@@ -210,6 +400,41 @@ class UlyssesSparseStudent:
         finally:
             if reserve:
                 kernels.set_sm_reserve(0)
+
+    def _run_copy(self, q, k, v, layer_index, rank, per):
+        """The inference layer over `CopyEngineExchange` (one piece): the
+        rank's student reads q, k, v from the receive buffers, waits for v
+        only after scoring, and writes the shared result buffer."""
+        key = (tuple(q.shape), q.dtype, q.device)
+        ex = self._exchanges.get(key)
+        if ex is None:
+            ex = CopyEngineExchange(q.shape[0], q.shape[1], q.shape[2],
+                                    q.dtype, q.device, self.group)
+            self._exchanges[key] = ex
+        student = self._piece_student(layer_index, 0, per, rank * per)
+        timers = veda_attention._NO_EVENTS  # pylint: disable=protected-access
+        if self.student is not None:
+            student.events = self.student.events
+            timers = self.student.events
+        sparse = isinstance(student, veda_attention.SparseStudent)
+
+        def attend(q_h, k_h, v_h, out, wait_v):
+            if sparse:
+                student.v_ready = wait_v
+                try:
+                    student(q_h, k_h, v_h, layer_index, out=out)
+                finally:
+                    student.v_ready = None
+            else:
+                out.copy_(student(q_h, k_h, v_h, layer_index))
+
+        return ex.run(q, k, v, attend, v_wait=sparse, timers=timers)
+
+    def close(self) -> None:
+        """Releases the copy-engine exchanges (collective: every rank)."""
+        for ex in self._exchanges.values():
+            ex.close()
+        self._exchanges.clear()
 
     def to_heads(self, x: torch.Tensor) -> torch.Tensor:
         """[S/P, H, D] shard -> [S, H/P, D] (differentiable)."""

@@ -64,6 +64,43 @@ def test_pieced_layer_equals_plain_student(one_rank_group, pieces):
     assert torch.equal(got[:used], want[:used])
 
 
+def test_copy_engine_exchange_equals_plain_student(one_rank_group):
+    """The copy-engine transport (IPC-mapped buffers, 2-D copies, IPC
+    events and host barriers) on one rank: the layer equals the plain
+    SparseStudent bit for bit, on three calls in a row (the receive and
+    result buffers are reused). Across GPUs the same code copies between
+    devices; bench.py --exchange copy measures it."""
+    text, grid, heads = 130, (4, 12, 20), 4
+    used = text + grid[0] * grid[1] * grid[2]
+    seq_len = used + 14
+    layout = veda_attention.PackedLayout(
+        seq_len, used, (veda_attention.VideoSpan(text, grid),))
+    config = veda_attention.VedaConfig(
+        target_budget=veda_mask.Budget(ratio=0.3))
+    clip = veda_attention.ClipTiling(layout, config, DEV)
+    plan = veda_plan.TilePlan('u', grid, [tiling.TileShape(2, 8, 8),
+                                          tiling.TileShape(1, 8, 16)],
+                              [[1, 0, 1, 0]])
+    pred = veda_predictor.TileScorePredictor(1, heads, 128)
+    pq, pk = inputs.predictor_weights(heads, 128, 49, 0.02)
+    with torch.no_grad():
+        pred.layers[0].proj_q.copy_(pq)
+        pred.layers[0].proj_k.copy_(pk)
+    student = veda_attention.SparseStudent(clip, plan, pred.to(DEV))
+    fn = ulysses.UlyssesSparseStudent(student, transport='copy')
+    try:
+        for seed in (50, 51, 52):
+            q, k, v = (t.to(DEV) for t in inputs.qkv(seq_len, heads, 128,
+                                                     seed, torch.bfloat16))
+            with torch.no_grad():
+                want = student(q, k, v, 0)
+                got = fn(q, k, v, 0)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), seed
+    finally:
+        fn.close()
+
+
 def test_exchanged_layer_gradients_equal_plain_student(one_rank_group):
     """The stage-2 student through the exchange (autograd across the NCCL
     all-to-alls): output and dq, dk, dv equal the plain SparseStudent's bit
