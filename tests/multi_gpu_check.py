@@ -30,7 +30,8 @@ def main() -> None:
     torch.cuda.set_device(dev)
     dist.init_process_group('nccl', device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
-    text, grid, heads = 130, (4, 12, 20), 4
+    text, grid = 130, (4, 12, 20)
+    heads = max(4, 2 * world)
     used = text + grid[0] * grid[1] * grid[2]
     seq_len = used + 2
     seq_len += (-seq_len) % world
@@ -41,7 +42,7 @@ def main() -> None:
     clip = veda_attention.ClipTiling(layout, config, dev)
     full_plan = veda_plan.TilePlan(
         'u', grid, [tiling.TileShape(2, 8, 8), tiling.TileShape(1, 8, 16)],
-        [[0, 1, 0, 1]])
+        [[h % 2 for h in range(heads)]])
     pred = veda_predictor.TileScorePredictor(1, heads, 128)
     pq, pk = inputs.predictor_weights(heads, 128, 53, 0.02)
     with torch.no_grad():
