@@ -427,9 +427,12 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-comparators', action='store_true',
                     help='skip the same-box GPU comparators (N=1)')
-    ap.add_argument('--exchange', choices=['nccl', 'copy'], default='copy',
-                    help='ulysses at N > 1: NCCL all-to-alls, or copy-engine '
-                         'copies between IPC-mapped buffers')
+    ap.add_argument('--exchange', choices=['auto', 'nccl', 'copy'],
+                    default='auto',
+                    help='ulysses at N > 1: NCCL all-to-alls, copy-engine '
+                         'copies between IPC-mapped buffers, or (auto) the '
+                         'one measured faster at N: copy at 2 GPUs, NCCL '
+                         'above')
     ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=2,
                     help="the attention forward's softmax: two groups of "
                          'warps on alternate key blocks (2) or one (1)')
@@ -495,9 +498,16 @@ def main():
     if heads_split:
         shard = seq_len // world
         q, k, v = synthetic_qkv(cfg, shard, rank * shard, device)
+        exchange = args.exchange
+        if exchange == 'auto':
+            # cfg3 on B200: 2 GPUs copy 15.4 ms/layer against NCCL 17.1;
+            # 8 GPUs copy 4.76 against NCCL 4.59 (narrower strided rows per
+            # peer, more host barriers).
+            exchange = 'copy' if world == 2 else 'nccl'
+        args.exchange = exchange
         fn = ulysses.UlyssesSparseStudent(student, pieces=args.pieces,
                                           reserve_sms=args.reserve_sms,
-                                          transport=args.exchange)
+                                          transport=exchange)
     else:
         # The whole layer on this rank's own clip (clip 0 on one GPU).
         q, k, v = synthetic_qkv(cfg, seq_len, 0, device, clip=rank)

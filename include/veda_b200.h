@@ -76,10 +76,12 @@ int veda_set_sm_reserve(int32_t n);
 /* No counterpart in the reference (a property of this library's forward
  * kernel). How the attention forward's softmax is organised: 2 (default),
  * two groups of warps on alternate key blocks of a query tile, feeding one
- * accumulator with a running reference handed from block to block; 1, one
- * group of warps on every block. Both compute the same attention (fp32
- * summation order differs). The fused dense + heat pass always runs 1.
- * Process-wide; returns VEDA_ERR_INVALID for other values. */
+ * accumulator with a running reference handed from block to block, and,
+ * where every query tile walks the same key tiles (veda_dense_fwd,
+ * veda_bsa_fwd_heat), query tiles in pairs that share each key and value
+ * tile, one group per tile; 1, one group of warps on every block of one
+ * query tile. Both compute the same attention (fp32 summation order
+ * differs). Process-wide; returns VEDA_ERR_INVALID for other values. */
 int veda_set_fwd_groups(int32_t groups);
 
 /* ---- head-parallel exchange on the copy engines ------------------------- */
@@ -410,8 +412,8 @@ int veda_teacher_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
 
 /* ---- (f) fused dense forward + LSE + teacher heat -------------------------- */
 
-/* Workspace bytes veda_bsa_fwd_heat needs (one [n_tiles][128] fp32 scratch
- * per SM of the current device). */
+/* Workspace bytes veda_bsa_fwd_heat needs (two [n_tiles][128] fp32
+ * scratches per SM of the current device). */
 int64_t veda_bsa_fwd_heat_workspace(int64_t n_tiles);
 
 /* The fused teacher pass the reference plans in
@@ -426,7 +428,11 @@ int64_t veda_bsa_fwd_heat_workspace(int64_t n_tiles);
  * reduce_sum != 0 gives sum_r sum_k exp(q.k * scale - L_r) from the fp32
  * scores the softmax already has. Padding query rows contribute nothing;
  * blocks not walked keep whatever heat holds (the caller zeroes it). The
- * lists are those of veda_bsa_fwd with R = n_tiles. */
+ * lists are those of veda_bsa_fwd with R = n_tiles. With two softmax groups
+ * (veda_set_fwd_groups, the default) the pass runs query tiles in pairs
+ * (2i, 2i + 1) over the key tiles of tile 2i's lists, so every query tile
+ * must have the same lists (all non-empty key tiles, as the teacher passes);
+ * with one group each tile walks its own. */
 int veda_bsa_fwd_heat(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                       const void* k, int64_t k_stride_n, int64_t k_stride_h,
                       const void* v, int64_t v_stride_n, int64_t v_stride_h,

@@ -747,8 +747,8 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       if (!wait_all(&bars[kPFull0 + sb], spar, abort, p.status)) break;
       tc_fence_after();
       const uint32_t bv = v_lo + slot * kTileUnits;
-      // Two groups: P of the whole block is in columns [0, 64) of S[sb],
-      // written at once.
+      // Two groups: P of the block is in columns [0, 64) of S[sb], keys
+      // 0-63 (kPFull0) then 64-127 (kPFull1).
       const uint32_t t_p = tmem + sb * 128;
       // P of key step kk (16 keys, 8 columns): one group, the first 16
       // columns of its key quarter's 32; two groups, columns 8 kk.
@@ -759,10 +759,8 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       for (int kk = 0; kk < 4; ++kk)
         umma_ts_warp(t_o, t_p + p_col(kk), bv + kk * 128, idesc_pv,
                      (kk > 0 || !fresh) ? 1u : 0u);
-      if (!kDual) {
-        if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) break;
-        tc_fence_after();
-      }
+      if (!wait_all(&bars[kPFull1 + sb], spar, abort, p.status)) break;
+      tc_fence_after();
 #pragma unroll
       for (int kk = 4; kk < 8; ++kk)
         umma_ts_warp(t_o, t_p + p_col(kk), bv + kk * 128, idesc_pv, 1u);
@@ -906,14 +904,6 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
         xref[(blk & 3) * 128 + row] = m_use;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kRefPub + (blk & 3)]);
-        // P = 2^(s c - m_use), packed in place over the first 16 words of
-        // each chunk.
-        const float2 negm2 = make_float2(-m_use, -m_use);
-        float2 sums[4];
-#pragma unroll
-        for (int q32 = 0; q32 < 4; ++q32)
-          sums[q32] = p32(x[q32], reinterpret_cast<float*>(x[q32]), scale2,
-                          negm2);
         if (rescale) {
           // O holds the PV of every block before blk once the PV of blk - 1
           // has finished; the PV of blk waits for this block's P.
@@ -928,13 +918,27 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
           for (int q16 = 0; q16 < 8; ++q16)
             rescale_o16(t_o + q16 * 16, alpha);
         }
-        // P of key 2i, 2i + 1 in column i of S[sb].
+        // P = 2^(s c - m_use), packed in place over the first 16 words of
+        // each chunk, stored and released in two halves (keys 0-63, then
+        // 64-127) so the first PVs start before the second half's
+        // exponentials. P of key 2i, 2i + 1 goes to column i of S[sb].
+        const float2 negm2 = make_float2(-m_use, -m_use);
+        float2 sums[4];
 #pragma unroll
-        for (int q32 = 0; q32 < 4; ++q32) tmem_st16(t_s + q32 * 16, x[q32]);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kPFull0 + sb]);
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int q32 = half * 2 + q;
+            sums[q32] = p32(x[q32], reinterpret_cast<float*>(x[q32]), scale2,
+                            negm2);
+            tmem_st16(t_s + q32 * 16, x[q32]);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            mbar_arrive(&bars[(half == 0 ? kPFull0 : kPFull1) + sb]);
+        }
         // This group's row sum follows the reference.
         if (m_use != m_last) l *= ex2_approx(m_last - m_use);
         m_last = m_use;
@@ -1286,6 +1290,534 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dense forward over query-tile pairs (dense mode, and the fused dense + heat
+// pass, whose keep-all lists are the same for every query tile).
+//
+// Every query tile attends to the same key tiles here, so a CTA takes two
+// query tiles of one head (a pair) and streams each key/value tile once for
+// both: per key block, QK of tile A and of tile B read the one K tile, PV of
+// each reads the one V tile. Tensor memory holds an S buffer and an O
+// accumulator per tile (S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511);
+// softmax group g (warps 4g .. 4g + 3) owns tile g, one query row per thread
+// over all 128 keys, with the online softmax and lazy rescaling of the
+// sparse kernel. Per key block the shared memory traffic is half the
+// one-tile kernel's K/V copies plus the operand reads: 128 KB per tile
+// block instead of 160 KB. Warps: 8 softmax, a TMA producer (Q_A and Q_B per
+// item into the two Q buffers, K and V through 2-slot rings, V two blocks
+// behind K), a QK issuer (TMEM owner) and a PV issuer. All roles walk the
+// same items (head, pair) with a stride of the grid and the same blocks, so
+// they agree on barrier phases. All waits are bounded.
+namespace pair {
+
+constexpr int kWarps = 11;
+constexpr int kProducer = 8, kQk = 9, kPv = 10;
+enum PairBar {
+  kQFullP = 0,   // Q_A and Q_B landed (one barrier, 64 KB)
+  kQEmptyP = 1,  // the item's last QKs finished reading Q_A and Q_B
+  kKFullP = 2,   // [2]
+  kKEmptyP = 4,  // [2] both QKs of the block finished
+  kVFullP = 6,   // [2]
+  kVEmptyP = 8,  // [2] both PVs of the block finished
+  kSFullP = 10,  // [2] per tile
+  kPFullP = 12,  // [2] per tile: P written (4 warps)
+  kPVDoneP = 14, // [2] per tile
+  kODoneP = 16,  // the item's last PVs finished
+  kOFreeP = 17,  // the epilogue read O_A and O_B (8 warps)
+  kDrainQkP = 18,
+  kDrainPvP = 19,
+  kPHalfP = 20,  // [2] per tile: P of keys 64-127 written (4 warps)
+  kNumBarsP = 22
+};
+
+// Length and key tile j of item (h, query tile qa): every key tile in dense
+// mode, else the query tile's lists (partial list then full list, each
+// from its end).
+struct PairKeys {
+  int len, pc, fc;
+  int64_t off;
+  __device__ void load(const FwdParams& p, int h, int qa) {
+    if (p.dense) {
+      len = p.n_kv_tiles;
+      pc = fc = 0;
+      off = 0;
+      return;
+    }
+    const int64_t row = static_cast<int64_t>(h) * p.n_q_tiles + qa;
+    pc = p.part_cnt[row];
+    fc = p.full_cnt[row];
+    len = pc + fc;
+    off = row * p.ld_idx;
+  }
+  __device__ int kv(const FwdParams& p, int j) const {
+    if (p.dense) return j;
+    return j < pc ? p.part_idx[off + (pc - 1 - j)]
+                  : p.full_idx[off + (fc - 1 - (j - pc))];
+  }
+  // Valid keys of block j (a prefix of the tile).
+  __device__ int valid(const FwdParams& p, int j) const {
+    if (p.dense) {
+      const int64_t rest = p.used - static_cast<int64_t>(j) * kTile;
+      return rest < kTile ? static_cast<int>(rest) : kTile;
+    }
+    return j < pc ? p.valid_count[kv(p, j)] : kTile;
+  }
+};
+
+}  // namespace pair
+
+template <bool kHeat>
+__global__ void __launch_bounds__(32 * pair::kWarps, 1)
+    pair_fwd_kernel(const __grid_constant__ FwdMaps maps, FwdParams p) {
+  using namespace pair;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_q = smem;                   // [2] x 32 KB: Q_A, Q_B
+  uint8_t* s_k = smem + 2 * kTileBytes;  // [kRing] x 32 KB
+  uint8_t* s_v = s_k + kRing * kTileBytes;
+  int32_t* s_list =
+      reinterpret_cast<int32_t*>(smem + (2 + 2 * kRing) * kTileBytes);
+  float* s_hl = reinterpret_cast<float*>(s_list + kListCap);  // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_hl + kExchangeFloats);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBarsP);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid / 32;
+  const int lane = tid % 32;
+  const int n_pairs = (p.n_q_tiles + 1) / 2;
+  const int n_items = p.n_heads * n_pairs;
+
+  if (tid == 0) {
+    for (int b = 0; b < kNumBarsP; ++b) {
+      uint32_t count = 1;
+      if (b == kPFullP || b == kPFullP + 1 || b == kPHalfP ||
+          b == kPHalfP + 1)
+        count = 4;
+      if (b == kOFreeP) count = 8;
+      mbar_init(&bars[b], count);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kQk) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducer) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensor_map(&maps.q[0]);
+      prefetch_tensor_map(&maps.k[0]);
+      prefetch_tensor_map(&maps.v[0]);
+    }
+    int nk = 0, nv = 0, ka = 0;
+    int kv1 = 0, kv2 = 0, h1 = 0, h2 = 0;  // V lags K by two blocks
+    bool run = true;
+    auto slot_of = [&](int n, int empty_bar) -> int {
+      const int slot = n % kRing;
+      if (n >= kRing && !wait_all(&bars[empty_bar + slot],
+                                  ((n / kRing) - 1) & 1, abort, p.status))
+        return -1;
+      return slot;
+    };
+    auto load_v = [&](int h, int kv) -> bool {
+      const int slot = slot_of(nv, kVEmptyP);
+      if (slot < 0) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[kVFullP + slot], kTileBytes);
+        load_tile(s_v + slot * kTileBytes, maps.v, &bars[kVFullP + slot], p,
+                  h, h, kv, false);
+      }
+      __syncwarp();
+      ++nv;
+      return true;
+    };
+    for (int it = blockIdx.x; run && it < n_items; it += gridDim.x) {
+      const int h = it / n_pairs, qa = 2 * (it % n_pairs);
+      PairKeys keys;
+      keys.load(p, h, qa);
+      if (keys.len == 0) continue;
+      if (!p.dense && keys.len <= kListCap) {
+        __syncwarp();
+        for (int jj = lane; jj < keys.len; jj += 32) s_list[jj] = keys.kv(p, jj);
+        __syncwarp();
+      }
+      if (ka >= 1) {
+        // The previous item's last two V tiles first (its PVs need them),
+        // then its last QKs must finish before Q_A and Q_B are replaced.
+        if (nk - nv >= 2) run = load_v(h2, kv2);
+        if (run && nk - nv >= 1) run = load_v(h1, kv1);
+        if (!run) break;
+        if (!wait_all(&bars[kQEmptyP], (ka - 1) & 1, abort, p.status)) {
+          run = false;
+          break;
+        }
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[kQFullP], 2 * kTileBytes);
+        load_tile(s_q, maps.q, &bars[kQFullP], p, h, h, qa, false);
+        // A missing tile B (odd tile count) reads the map's zero fill.
+        load_tile(s_q + kTileBytes, maps.q, &bars[kQFullP], p, h, h, qa + 1,
+                  false);
+      }
+      __syncwarp();
+      for (int j = 0; j < keys.len; ++j) {
+        const int kv = p.dense ? j
+                               : (keys.len <= kListCap ? s_list[j]
+                                                       : keys.kv(p, j));
+        const int slot = slot_of(nk, kKEmptyP);
+        if (slot < 0) {
+          run = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars[kKFullP + slot], kTileBytes);
+          load_tile(s_k + slot * kTileBytes, maps.k, &bars[kKFullP + slot],
+                    p, h, h, kv, false);
+        }
+        __syncwarp();
+        ++nk;
+        if (nk - nv > 2 && !load_v(h2, kv2)) {
+          run = false;
+          break;
+        }
+        kv2 = kv1;
+        h2 = h1;
+        kv1 = kv;
+        h1 = h;
+      }
+      ++ka;
+    }
+    if (run) {
+      if (nk - nv >= 2) run = load_v(h2, kv2);
+      if (run && nk - nv >= 1) run = load_v(h1, kv1);
+    }
+    if (lane == 0 && *abort) {
+      // Let the copies in flight land before the CTA retires.
+      volatile int never = 0;
+      if (ka >= 1) mbar_wait(&bars[kQFullP], (ka - 1) & 1, &never, nullptr);
+      for (int k = nk - kRing; k < nk; ++k)
+        if (k >= 0)
+          mbar_wait(&bars[kKFullP + k % kRing], (k / kRing) & 1, &never,
+                    nullptr);
+      for (int k = nv - kRing; k < nv; ++k)
+        if (k >= 0)
+          mbar_wait(&bars[kVFullP + k % kRing], (k / kRing) & 1, &never,
+                    nullptr);
+    }
+  } else if (warp == kQk) {
+    // ---------------- QK issuer ----------------
+    constexpr uint32_t idesc_qk = idesc_bf16(128, 128, false, false);
+    const uint32_t q_lo = sw128_desc_lo(smem_u32(s_q), 16);
+    const uint32_t k_lo = sw128_desc_lo(smem_u32(s_k), 16);
+    constexpr uint32_t kTileUnits = kTileBytes >> 4;
+    uint32_t b = 0;
+    int ka = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+      PairKeys keys;
+      keys.load(p, it / n_pairs, 2 * (it % n_pairs));
+      if (keys.len == 0) continue;
+      for (int j = 0; j < keys.len; ++j, ++b) {
+        const int slot = b % kRing;
+        if (!wait_all(&bars[kKFullP + slot], (b / kRing) & 1, abort,
+                      p.status) ||
+            (j == 0 && !wait_all(&bars[kQFullP], ka & 1, abort, p.status))) {
+          ok = false;
+          break;
+        }
+        for (int g = 0; g < 2; ++g) {
+          // S_g held P_g of the previous block until its PV finished.
+          if (b >= 1 && !wait_all(&bars[kPVDoneP + g], (b - 1) & 1, abort,
+                                  p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = q_lo + g * kTileUnits;
+          const uint32_t bk = k_lo + slot * kTileUnits;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2;
+            umma_ss_warp(tmem + g * 128, a + off, bk + off, idesc_qk,
+                         kk > 0 ? 1u : 0u);
+          }
+          umma_commit_warp(&bars[kSFullP + g]);
+        }
+        if (!ok) break;
+        umma_commit_warp(&bars[kKEmptyP + slot]);
+        if (j == keys.len - 1) umma_commit_warp(&bars[kQEmptyP]);
+      }
+      ++ka;
+    }
+    if (*abort) {
+      volatile int never = 0;
+      umma_commit_warp(&bars[kDrainQkP]);
+      mbar_wait(&bars[kDrainQkP], 0, &never, nullptr);
+    }
+  } else if (warp == kPv) {
+    // ---------------- PV issuer ----------------
+    constexpr uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
+    const uint32_t v_lo = sw128_desc_lo(smem_u32(s_v), kHalfBytes);
+    constexpr uint32_t kTileUnits = kTileBytes >> 4;
+    uint32_t b = 0;
+    int ka = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+      PairKeys keys;
+      keys.load(p, it / n_pairs, 2 * (it % n_pairs));
+      if (keys.len == 0) continue;
+      for (int j = 0; j < keys.len; ++j, ++b) {
+        const int slot = b % kRing;
+        if (!wait_all(&bars[kVFullP + slot], (b / kRing) & 1, abort,
+                      p.status) ||
+            (j == 0 && ka >= 1 &&
+             !wait_all(&bars[kOFreeP], (ka - 1) & 1, abort, p.status))) {
+          ok = false;
+          break;
+        }
+        const uint32_t bv = v_lo + slot * kTileUnits;
+        for (int g = 0; g < 2; ++g) {
+          // P of key step kk (16 keys) is in columns 8 kk of S_g; the
+          // keys 0-63 half is written first.
+          if (!wait_all(&bars[kPFullP + g], b & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_ts_warp(tmem + 256 + g * 128, tmem + g * 128 + kk * 8,
+                         bv + kk * 128, idesc_pv,
+                         (kk > 0 || j > 0) ? 1u : 0u);
+          if (!wait_all(&bars[kPHalfP + g], b & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 4; kk < 8; ++kk)
+            umma_ts_warp(tmem + 256 + g * 128, tmem + g * 128 + kk * 8,
+                         bv + kk * 128, idesc_pv, 1u);
+          umma_commit_warp(&bars[kPVDoneP + g]);
+        }
+        if (!ok) break;
+        umma_commit_warp(&bars[kVEmptyP + slot]);
+        if (j == keys.len - 1) umma_commit_warp(&bars[kODoneP]);
+      }
+      ++ka;
+    }
+    if (*abort) {
+      volatile int never = 0;
+      umma_commit_warp(&bars[kDrainPvP]);
+      mbar_wait(&bars[kDrainPvP], 0, &never, nullptr);
+    }
+  } else {
+    // ---------------- softmax + epilogue (warps 0-7) ----------------
+    const int grp = warp / 4;  // tile of the pair
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + grp * 128 + lane_base;
+    const uint32_t t_o = tmem + 256 + grp * 128 + lane_base;
+    const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+    float* hs = nullptr;  // this CTA's heat scratch for this tile
+    if constexpr (kHeat)
+      hs = p.heat_scratch +
+           (static_cast<int64_t>(blockIdx.x) * 2 + grp) * p.n_kv_tiles *
+               kTile;
+    uint32_t b = 0;
+    int ka = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+      const int h = it / n_pairs;
+      const int qa = 2 * (it % n_pairs);
+      const int qt = qa + grp;
+      PairKeys keys;
+      keys.load(p, h, qa);
+      const int len = keys.len;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < len; ++j, ++b) {
+        const int valid = keys.valid(p, j);
+        if (!wait_all(&bars[kSFullP + grp], b & 1, abort, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t x[4][32];
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) tmem_ld32(t_s + q32 * 32, x[q32]);
+        tmem_wait_ld();
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q32 = 0; q32 < 4; ++q32) {
+          if (valid < kTile) {
+            const int n = valid - q32 * 32;
+            const uint32_t word =
+                n >= 32 ? ~0u : (n <= 0 ? 0u : (1u << n) - 1u);
+            float* f = reinterpret_cast<float*>(x[q32]);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (!((word >> c) & 1u)) f[c] = -INFINITY;
+          }
+          mx = fmaxf(mx, row_max32(reinterpret_cast<float*>(x[q32])));
+        }
+        const float mb = mx * p.scale_log2;
+        bool rescale = false;
+        float alpha = 1.0f;
+        if (j == 0) {
+          m_ref = mb;
+        } else {
+          const bool grow = mb > m_ref + 8.0f;
+          rescale = __any_sync(0xffffffffu, grow);
+          if (rescale) {
+            const float m_new = grow ? mb : m_ref;
+            alpha = ex2_approx(m_ref - m_new);
+            m_ref = m_new;
+          }
+        }
+        if (rescale) {
+          // O_g holds the previous blocks once the PV of blk - 1 finished;
+          // it is rescaled before this block's P is released.
+          if (!wait_all(&bars[kPVDoneP + grp], (b - 1) & 1, abort,
+                        p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int q16 = 0; q16 < 8; ++q16)
+            rescale_o16(t_o + q16 * 16, alpha);
+          l *= alpha;
+        }
+        // P in two halves (keys 0-63, then 64-127), each released as soon
+        // as it is stored, so the first PVs start before the second half's
+        // exponentials.
+        const float2 negm2 = make_float2(-m_ref, -m_ref);
+        float2 sums[4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int q32 = half * 2 + q;
+            sums[q32] = p32(x[q32], reinterpret_cast<float*>(x[q32]), scale2,
+                            negm2);
+            tmem_st16(t_s + q32 * 16, x[q32]);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            mbar_arrive(&bars[(half == 0 ? kPFullP : kPHalfP) + grp]);
+        }
+        const float bsum = ((sums[0].x + sums[0].y) + (sums[1].x + sums[1].y)) +
+                           ((sums[2].x + sums[2].y) + (sums[3].x + sums[3].y));
+        if constexpr (kHeat) {
+          // Max mode: the raw score maximum rounded to bf16 (the reference
+          // rounds every score; rounding is monotonic). Sum mode: log2 of
+          // the block's exponential sum against the row's reference.
+          hs[j * kTile + row] =
+              p.heat_sum ? m_ref + lg2_approx(bsum)
+                         : __bfloat162float(__float2bfloat16_rn(mx));
+        }
+        l += bsum;
+      }
+      if (!ok) break;
+      // ---------------- epilogue of the tile ----------------
+      const int64_t slot_row = static_cast<int64_t>(qt) * kTile + row;
+      const bool real_tile = qt < p.n_q_tiles;
+      const bool write = real_tile && (!p.dense || slot_row < p.used);
+      const float inv_l = len > 0 ? 1.0f / l : 0.f;
+      if (len > 0) {
+        if (!wait_all(&bars[kODoneP], ka & 1, abort, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (len > 0) {
+          tmem_ld32(t_o + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (write) {
+          uint4* d4 = reinterpret_cast<uint4*>(
+              p.out + slot_row * p.out_stride_n + h * p.out_stride_h +
+              c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(
+                pack_bf16(__uint_as_float(o[8 * i]) * inv_l,
+                          __uint_as_float(o[8 * i + 1]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 2]) * inv_l,
+                          __uint_as_float(o[8 * i + 3]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 4]) * inv_l,
+                          __uint_as_float(o[8 * i + 5]) * inv_l),
+                pack_bf16(__uint_as_float(o[8 * i + 6]) * inv_l,
+                          __uint_as_float(o[8 * i + 7]) * inv_l));
+        }
+      }
+      if (len > 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kOFreeP]);
+      }
+      const float lse2 = len > 0 ? m_ref + lg2_approx(l) : -INFINITY;
+      if (write && p.lse != nullptr)
+        p.lse[slot_row * p.lse_stride_row + h * p.lse_stride_h] =
+            lse2 * 0.69314718055994531f;
+      if constexpr (kHeat) {
+        if (len > 0 && real_tile) {
+          // Padding query rows carry no heat.
+          s_hl[grp * kTile + row] =
+              row < p.valid_count[qt] ? lse2 : INFINITY;
+          row_sync(1 + grp);  // the tile's 4 warps: rows and scratch stored
+          float* dst = p.heat + h * p.heat_sh + qt * p.heat_sq;
+          for (int jj = quarter; jj < len; jj += 4) {
+            float acc = p.heat_sum ? 0.f : -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = lane + 32 * i;
+              const float v = hs[jj * kTile + r];
+              if (p.heat_sum)
+                acc += ex2_approx(v - s_hl[grp * kTile + r]);
+              else
+                acc = fmaxf(acc, fmaf(v, p.scale_log2, -s_hl[grp * kTile + r]));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+              const float o2 = __shfl_xor_sync(0xffffffffu, acc, off);
+              acc = p.heat_sum ? acc + o2 : fmaxf(acc, o2);
+            }
+            if (lane == 0)
+              dst[keys.kv(p, jj)] = p.heat_sum ? acc : ex2_approx(acc);
+          }
+          row_sync(1 + grp);  // the scratch is free for the next item
+        }
+      }
+      if (len > 0) ++ka;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kQk) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 __global__ void zero_rows_kernel(__nv_bfloat16* out, int64_t stride_s,
                                  int64_t stride_h, float* lse, int64_t ls,
                                  int64_t lh, int64_t row0, int64_t n_rows,
@@ -1347,11 +1879,37 @@ int launch_fwd_variant(const FwdMaps& maps, const FwdParams& p,
   return check_launch("bsa_fwd_kernel");
 }
 
+// The pair kernel: dense mode and the fused dense + heat pass.
+template <bool kHeat>
+int launch_pair(const FwdMaps& maps, const FwdParams& p,
+                cudaStream_t stream) {
+  static bool configured = false;
+  const int sms = sm_count();
+  if (sms == 0) return set_error(VEDA_ERR_CUDA, "no CUDA device");
+  if (!configured) {
+    VEDA_CUDA(cudaFuncSetAttribute(pair_fwd_kernel<kHeat>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemBytes));
+    configured = true;
+  }
+  const int items = p.n_heads * ((p.n_q_tiles + 1) / 2);
+  if (items == 0) return VEDA_OK;
+  const int cap = sms - sm_reserve() > 0 ? sms - sm_reserve() : 1;
+  const int grid = items < cap ? items : cap;
+  pair_fwd_kernel<kHeat><<<grid, 32 * pair::kWarps, kSmemBytes, stream>>>(
+      maps, p);
+  return check_launch("pair_fwd_kernel");
+}
+
 template <bool kHeat>
 int launch_fwd(const FwdMaps& maps, const FwdParams& p, cudaStream_t stream) {
   if constexpr (kHeat) {
-    return launch_fwd_variant<true, false>(maps, p, stream);
+    return g_fwd_groups == 2 ? launch_pair<true>(maps, p, stream)
+                             : launch_fwd_variant<true, false>(maps, p,
+                                                               stream);
   } else {
+    if (g_fwd_groups == 2 && p.dense)
+      return launch_pair<false>(maps, p, stream);
     return g_fwd_groups == 2 ? launch_fwd_variant<false, true>(maps, p, stream)
                              : launch_fwd_variant<false, false>(maps, p,
                                                                 stream);
@@ -1426,7 +1984,8 @@ extern "C" int veda_bsa_fwd(const void* q, int64_t q_stride_n,
 }
 
 extern "C" int64_t veda_bsa_fwd_heat_workspace(int64_t n_kv_tiles) {
-  return static_cast<int64_t>(sm_count()) * n_kv_tiles * kTile *
+  // Two [n_kv_tiles][128] scratches per SM: the pair kernel's two tiles.
+  return 2 * static_cast<int64_t>(sm_count()) * n_kv_tiles * kTile *
          static_cast<int64_t>(sizeof(float));
 }
 

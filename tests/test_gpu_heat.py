@@ -150,3 +150,31 @@ def test_fused_dense_heat_matches_oracle(fused_case, reduce):
         torch.testing.assert_close(heat, sep, rtol=1e-3, atol=1e-6)
     else:
         torch.testing.assert_close(heat, sep, rtol=3e-2, atol=1e-4)
+
+
+@pytest.mark.parametrize('reduce', ['max', 'sum'])
+def test_fused_pass_pairs_equal_single_tiles(fused_case, reduce):
+    """With two softmax groups the fused pass runs query tiles in pairs that
+    share every key and value tile (one group per tile); with one group each
+    tile runs alone. Same output, LSE and heat up to fp32 summation order;
+    the padded layout has an odd number of tiles, so the last pair has one."""
+    from miowtion_b200 import kernels
+    lay, ref, qt, kt, vt, _, _ = fused_case
+    assert lay.n_tiles % 2 == 1
+    runs = {}
+    try:
+        for g in (1, 2):
+            kernels.set_fwd_groups(g)
+            runs[g] = heatmap.fused_dense_heat(qt, kt, vt, lay, reduce)
+    finally:
+        kernels.set_fwd_groups(kernels.DEFAULT_FWD_GROUPS)
+    valid = ref.slot_valid.astype(bool)
+    (o1, l1, h1), (o2, l2, h2) = runs[1], runs[2]
+    parity.assert_rel(np32(o2), np32(o1), 1e-2,
+                      f'fused pass ({reduce}): pairs against single tiles',
+                      where=valid)
+    np.testing.assert_allclose(np32(l2).T[valid], np32(l1).T[valid],
+                               atol=1e-3)
+    parity.assert_rel(h2, h1, 1e-2,
+                      f'fused pass ({reduce}): heat, pairs against single '
+                      'tiles')
