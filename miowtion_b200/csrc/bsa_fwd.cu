@@ -106,10 +106,12 @@ enum Bar {
   kHeatIn = 28,     // fused heat: an item's row maxima / sums stored (16)
   kHeatOut = 29,    // fused heat: the item's heat written (16)
   kRefPub = 30,     // [4] two groups: block b's reference published (4)
-  kNumBars = 34
+  kVFull3 = 34,     // [3] two groups: the 3-slot V ring, tile landed
+  kVEmpty3 = 37,    // [3] two groups: the 3-slot V ring, its PV finished
+  kNumBars = 40
 };
 // Block records live after the barriers (and the TMEM slot / abort word).
-constexpr int kRecOffset = 40;  // in 8-byte units from the barriers
+constexpr int kRecOffset = 44;  // in 8-byte units from the barriers
 
 struct FwdParams {
   int n_heads;
@@ -475,6 +477,17 @@ template <bool kHeat, bool kDual>
 __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     bsa_fwd_kernel(const __grid_constant__ FwdMaps maps, FwdParams p) {
   static_assert(!(kHeat && kDual), "the fused heat uses the one-group path");
+  // Shared memory holds six 32 KB tiles. One group: Q double-buffered
+  // (the next item's Q loads while the current item runs), K and V rings of
+  // two. Two groups: one Q buffer and a V ring of three, since V(b) can
+  // only start loading when PV(b - ring) has finished and a tile takes
+  // longer to land than one PV lasts (measured: with two slots the PV
+  // waited for V in most blocks).
+  constexpr int kQBufs = kDual ? 1 : 2;
+  constexpr int kRingV = kDual ? 3 : 2;
+  constexpr int kVFullB = kDual ? kVFull3 : kVFull;
+  constexpr int kVEmptyB = kDual ? kVEmpty3 : kVEmpty;
+  static_assert(kQBufs + kRing + kRingV == 6, "six tiles of shared memory");
   constexpr uint32_t kSB = static_cast<uint32_t>(kSBufs);
   constexpr int kSoftmaxN = Roles<kDual>::kSoftmax;
   constexpr int kProducerWarp = Roles<kDual>::kProducer;
@@ -483,9 +496,9 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* s_q = smem;                           // [2] x 32 KB (item parity)
-  uint8_t* s_k = smem + 2 * kTileBytes;          // [kRing] x 32 KB
-  uint8_t* s_v = s_k + kRing * kTileBytes;       // [kRing] x 32 KB
+  uint8_t* s_q = smem;                           // [kQBufs] x 32 KB
+  uint8_t* s_k = smem + kQBufs * kTileBytes;     // [kRing] x 32 KB
+  uint8_t* s_v = s_k + kRing * kTileBytes;       // [kRingV] x 32 KB
   int32_t* s_list =
       reinterpret_cast<int32_t*>(smem + (2 + 2 * kRing) * kTileBytes);
   float* s_xchg = reinterpret_cast<float*>(s_list + kListCap);
@@ -494,7 +507,7 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   static_assert(kNumBars + 1 <= kRecOffset,
                 "barriers overlap the block records");
-  static_assert(kRecOffset * 8 + 2 * kRing * 4 <= 512, "barrier area");
+  static_assert(kRecOffset * 8 + (kRing + 3) * 4 <= 512, "barrier area");
   // Block records beside the K and the V ring slots.
   volatile uint32_t* k_rec =
       reinterpret_cast<volatile uint32_t*>(bars + kRecOffset);
@@ -555,10 +568,10 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     uint32_t r1 = 0, r2 = 0;
     bool run = true;
     // Waits for a free slot of a ring (n tiles loaded so far); -1 on abort.
-    auto slot_of = [&](int n, int empty_bar) -> int {
-      const int slot = n % kRing;
-      if (n >= kRing && !wait_all(&bars[empty_bar + slot],
-                                  ((n / kRing) - 1) & 1, abort, p.status))
+    auto slot_of = [&](int n, int empty_bar, int ring) -> int {
+      const int slot = n % ring;
+      if (n >= ring && !wait_all(&bars[empty_bar + slot],
+                                 ((n / ring) - 1) & 1, abort, p.status))
         return -1;
       return slot;
     };
@@ -576,11 +589,11 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
         load_tile(dst, map, &bars[full_bar + slot], p, h, g, kv, p.box_kv);
     };
     auto load_v = [&](int h, int g, int kv, uint32_t rec) -> bool {
-      const int slot = slot_of(nv, kVEmpty);
+      const int slot = slot_of(nv, kVEmptyB, kRingV);
       if (slot < 0) return false;
       if (lane == 0) {
         v_rec[slot] = rec;
-        load(maps.v, p.v_img, s_v, kVFull, slot, h, g, kv);
+        load(maps.v, p.v_img, s_v, kVFullB, slot, h, g, kv);
       }
       __syncwarp();
       ++nv;
@@ -594,10 +607,12 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
             s_list[jj] = st.kv_global(p, jj);
         __syncwarp();
         hg = p.packed ? static_cast<int>(p.head_ids[b.h]) : b.h;
-        // The Q buffer frees after the last QK of the item two back.
-        const int qb = b.ka & 1;
-        if (b.ka >= 2 && !wait_all(&bars[kQEmpty + qb],
-                                   ((b.ka >> 1) & 1) ^ 1, abort, p.status)) {
+        // The Q buffer frees after the last QK of the item two back (one
+        // group) or one back (two groups, one buffer).
+        const int qb = kDual ? 0 : b.ka & 1;
+        const bool qwait = kDual ? b.ka >= 1 : b.ka >= 2;
+        const uint32_t qpar = kDual ? (b.ka - 1) & 1 : ((b.ka >> 1) & 1) ^ 1;
+        if (qwait && !wait_all(&bars[kQEmpty + qb], qpar, abort, p.status)) {
           run = false;
           break;
         }
@@ -614,7 +629,7 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
                              : (st.len <= kListCap ? s_list[st.j]
                                                    : st.kv_global(p, st.j));
       const uint32_t rec = block_record(b);
-      const int slot = slot_of(nk, kKEmpty);
+      const int slot = slot_of(nk, kKEmpty, kRing);
       if (slot < 0) {
         run = false;
         break;
@@ -644,18 +659,18 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       // slot's full barrier without a copy).
       if (nk >= 2) run = load_v(h2, g2, kv2, r2);
       if (run && nk >= 1) run = load_v(h1, g1, kv1, r1);
-      int slot = run ? slot_of(nk, kKEmpty) : -1;
+      int slot = run ? slot_of(nk, kKEmpty, kRing) : -1;
       if (slot >= 0) {
         if (lane == 0) {
           k_rec[slot] = kRecEnd;
           mbar_arrive(&bars[kKFull + slot]);
         }
         __syncwarp();
-        slot = slot_of(nv, kVEmpty);
+        slot = slot_of(nv, kVEmptyB, kRingV);
         if (slot >= 0) {
           if (lane == 0) {
             v_rec[slot] = kRecEnd;
-            mbar_arrive(&bars[kVFull + slot]);
+            mbar_arrive(&bars[kVFullB + slot]);
           }
           __syncwarp();
         }
@@ -664,16 +679,17 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     if (lane == 0 && *abort) {
       // Let the copies already in flight land before the CTA retires.
       volatile int never = 0;
-      for (int ka = q_issued - 2; ka < q_issued; ++ka)
+      for (int ka = q_issued - kQBufs; ka < q_issued; ++ka)
         if (ka >= 0)
-          mbar_wait(&bars[kQFull + (ka & 1)], (ka >> 1) & 1, &never, nullptr);
+          mbar_wait(&bars[kQFull + (kDual ? 0 : ka & 1)],
+                    kDual ? ka & 1 : (ka >> 1) & 1, &never, nullptr);
       for (int k = nk - kRing; k < nk; ++k)
         if (k >= 0)
           mbar_wait(&bars[kKFull + k % kRing], (k / kRing) & 1, &never,
                     nullptr);
-      for (int k = nv - kRing; k < nv; ++k)
+      for (int k = nv - kRingV; k < nv; ++k)
         if (k >= 0)
-          mbar_wait(&bars[kVFull + k % kRing], (k / kRing) & 1, &never,
+          mbar_wait(&bars[kVFullB + k % kRingV], (k / kRingV) & 1, &never,
                     nullptr);
     }
   } else if (warp == kMmaWarp) {
@@ -692,14 +708,17 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
       const uint32_t rec = k_rec[slot];
       if (rec & kRecEnd) break;
       const uint32_t sb = b % kSB;
-      const uint32_t qb = (rec & kRecItem) ? 1u : 0u;
+      // One group: Q buffer ka & 1, phase (ka >> 1) & 1; two groups: the one
+      // buffer, phase ka & 1.
+      const uint32_t qb = kDual ? 0u : ((rec & kRecItem) ? 1u : 0u);
+      const uint32_t qphase = kDual ? ((rec & kRecItem) ? 1u : 0u)
+                                    : ((rec & kRecQPhase) ? 1u : 0u);
       // S[sb] held P of block b - kSB: its PV must have finished.
       if (b >= kSB && !wait_all(&bars[kPVDone + sb],
                                 ((b / kSB) - 1) & 1, abort, p.status))
         break;
       if ((rec & kRecFirst) &&
-          !wait_all(&bars[kQFull + qb], (rec & kRecQPhase) ? 1u : 0u, abort,
-                    p.status))
+          !wait_all(&bars[kQFull + qb], qphase, abort, p.status))
         break;
       tc_fence_after();
       const uint32_t a = q_lo + qb * kTileUnits;
@@ -728,8 +747,9 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
     constexpr uint32_t kTileUnits = kTileBytes >> 4;
     const uint32_t t_o0 = tmem + kSB * 128;
     for (uint32_t b = 0;; ++b) {
-      const int slot = b % kRing;
-      if (!wait_all(&bars[kVFull + slot], (b / kRing) & 1, abort, p.status))
+      const int slot = b % kRingV;
+      if (!wait_all(&bars[kVFullB + slot], (b / kRingV) & 1, abort,
+                    p.status))
         break;
       const uint32_t rec = v_rec[slot];
       if (rec & kRecEnd) break;
@@ -764,7 +784,7 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
 #pragma unroll
       for (int kk = 4; kk < 8; ++kk)
         umma_ts_warp(t_o, t_p + p_col(kk), bv + kk * 128, idesc_pv, 1u);
-      umma_commit_warp(&bars[kVEmpty + slot]);
+      umma_commit_warp(&bars[kVEmptyB + slot]);
       umma_commit_warp(&bars[kPVDone + sb]);
       if (rec & kRecLast) umma_commit_warp(&bars[kODone]);
     }
