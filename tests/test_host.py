@@ -164,3 +164,25 @@ def test_balanced_order_deals_every_item_once_and_evens_the_load():
         qt = n_tiles - 1 - i % n_tiles
         stride[i % ctas] += gw if qt >= n_video else vw
     assert float(load.max()) < float(stride.max())
+
+
+def test_bench_roofline_peak_follows_timed_region():
+    """A timed region of a second or more is compared with the sustained
+    bf16 peak (it runs under the power cap), a shorter one with the burst
+    peak; both fractions are reported either way."""
+    import importlib.util
+    import pathlib
+    path = pathlib.Path(__file__).resolve().parents[1] / 'bench.py'
+    spec = importlib.util.spec_from_file_location('bench_under_test', path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    peaks = {'bf16_tflops': 1600.0, 'bf16_tflops_sustained': 1400.0,
+             'source': 'measured'}
+    short = bench.tensor_roofline(peaks, 800.0, 0.5, 'k', None)
+    assert short['peak'] == 1600.0 and short['frac'] == 0.5
+    assert 'burst' in short['peak_source']
+    long = bench.tensor_roofline(peaks, 700.0, 12.0, 'k', 1e9)
+    assert long['peak'] == 1400.0 and long['frac'] == 0.5
+    assert 'sustained' in long['peak_source'] and long['traffic'] == 1e9
+    assert long['frac_of_burst'] == 700.0 / 1600.0
+    assert long['frac_of_sustained'] == 0.5
