@@ -703,8 +703,8 @@ def main():
 # DRAM bytes (read + write) of one bsa_fwd_kernel launch (one head group),
 # from single-pass ncu captures of the two-group kernel
 # (dram__bytes_read.sum + dram__bytes_write.sum): config 2, and config 3 at
-# full size (3.40 GB + 0.565 GB per launch). Other configs: null.
-FWD_TRAFFIC = {'cfg2': 863.3e6, 'cfg3': 3.965e9}
+# full size (3.18 GB + 0.57 GB per launch). Other configs: null.
+FWD_TRAFFIC = {'cfg2': 864.2e6, 'cfg3': 3.748e9}
 
 
 def dense_comparison(cfg, q, k, v, reps=3):
