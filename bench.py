@@ -460,8 +460,9 @@ def main():
     ap.add_argument('--fwd-groups', type=int, choices=[1, 2], default=2,
                     help="the attention forward's softmax: two groups of "
                          'warps on alternate key blocks (2) or one (1)')
-    ap.add_argument('--only', choices=['backward', 'heat', 'compensation',
-                                       'search'], default=None,
+    ap.add_argument('--only', choices=['backward', 'heat', 'teacher',
+                                       'compensation', 'search'],
+                    default=None,
                     help='time one stage on head group 0 of the config '
                          '(for kernel profiling)')
     ap.add_argument('--reduce', choices=['sum', 'max'], default='sum',
@@ -970,6 +971,19 @@ def run_stage(args, cfg):
             kernels.block_sparse_attention_bwd(qt, kt, vt, out, dout, lse,
                                                lists, t_lists, tl)
         what = 'block-sparse backward (prep + dq + dk/dv)'
+    elif args.only == 'teacher':
+        qt = tiling.gather_tiles(q, tl, group.heads)
+        kt = tiling.gather_tiles(k, tl, group.heads)
+        vt = tiling.gather_tiles(v, tl, group.heads)
+        del q, k, v
+        blocks = tl.n_tiles ** 2 * heads
+        # Dense QK^T and PV of every block; the heat reuses the scores.
+        flops = 4.0 * blocks * 128 ** 3
+
+        def call():
+            heatmap.fused_dense_heat(qt, kt, vt, tl, args.reduce)
+        what = (f'fused dense attention + LSE + heat (reduce={args.reduce}), '
+                'all query tiles')
     elif args.only == 'compensation':
         from miowtion_b200 import compensation
         qt, fq = tiling.gather_and_pool(q, tl, group.heads)
@@ -1054,6 +1068,7 @@ def run_stage(args, cfg):
             'backward': "2.5 x the forward per computed block (the "
                         "reference's)",
             'heat': '2 x 128^3 per block of QK^T',
+            'teacher': '4 x 128^3 per block (QK^T and PV, every block)',
             'compensation': '4 x 128 x n_tiles x 128 per (query tile, head)',
             'search': '2 x 128^3 per heat block of the sampled tiles',
         }[args.only]}), flush=True)
@@ -1275,8 +1290,10 @@ def run_train_step(args, cfg):
                                                 world /
                                                 stages['teacher_fused'] / 1e9,
                 'student_bwd_attention_equiv': bwd_tflops}
-            kernel = ('bsa_fwd_kernel<heat> (fused dense + LSE + heat, '
-                      'executed FLOPs over tile-ordered rows)')
+            kernel = (('pair_fwd_kernel<heat>' if args.fwd_groups == 2 else
+                       'bsa_fwd_kernel<heat>') +
+                      ' (fused dense + LSE + heat, executed FLOPs over '
+                      'tile-ordered rows)')
         else:
             achieved = dense_flops / world / stages['dense_fwd_lse'] / 1e9
             stage_tflops = {
