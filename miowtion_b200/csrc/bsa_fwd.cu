@@ -231,6 +231,48 @@ __device__ __forceinline__ void load_tile(uint8_t* dst,
   }
 }
 
+// Heat of the key tiles jj = first, first + step, ... < len of one query
+// tile, from the scratch value v of each (key tile, row): over the tile's
+// 128 rows, the sum of 2^(v - lse2[row]) (sum mode, v the log2 of the
+// row's exponential sum over the block against the row's reference) or
+// 2^(max of v c - lse2[row]) (max mode, v the raw score maximum). One warp
+// per key tile, lane l reading rows l, l + 32, l + 64, l + 96; four key
+// tiles per round, so that each lane has 16 loads in flight.
+template <typename KvOf>
+__device__ __forceinline__ void reduce_heat(const float* hs,
+                                            const float* lse2, int first,
+                                            int step, int len, bool sum,
+                                            float scale_log2, float* dst,
+                                            KvOf kv_of, int lane) {
+  for (int j0 = first; j0 < len; j0 += 4 * step) {
+    float v[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int jj = j0 + u * step;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        v[u][i] = jj < len ? hs[jj * kTile + lane + 32 * i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int jj = j0 + u * step;
+      float acc = sum ? 0.f : -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float l2 = lse2[lane + 32 * i];
+        acc = sum ? acc + ex2_approx(v[u][i] - l2)
+                  : fmaxf(acc, fmaf(v[u][i], scale_log2, -l2));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float o2 = __shfl_xor_sync(0xffffffffu, acc, off);
+        acc = sum ? acc + o2 : fmaxf(acc, o2);
+      }
+      if (lane == 0 && jj < len) dst[kv_of(jj)] = sum ? acc : ex2_approx(acc);
+    }
+  }
+}
+
 // One key block of a slot's stream.
 struct Block {
   int h, qt;   // work item
@@ -1270,25 +1312,9 @@ __global__ void __launch_bounds__(Roles<kDual>::kThreads, 1)
             break;
           }
           float* dst = p.heat + h * p.heat_sh + qt * p.heat_sq;
-          for (int jj = warp; jj < len; jj += kSoftmaxWarps) {
-            float acc = p.heat_sum ? 0.f : -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = lane + 32 * i;
-              const float v = hs[jj * kTile + r];
-              if (p.heat_sum)
-                acc += ex2_approx(v - s_hl[r]);
-              else
-                acc = fmaxf(acc, fmaf(v, p.scale_log2, -s_hl[r]));
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-              const float o2 = __shfl_xor_sync(0xffffffffu, acc, off);
-              acc = p.heat_sum ? acc + o2 : fmaxf(acc, o2);
-            }
-            if (lane == 0)
-              dst[st.kv_global(p, jj)] = p.heat_sum ? acc : ex2_approx(acc);
-          }
+          reduce_heat(hs, s_hl, warp, kSoftmaxWarps, len, p.heat_sum != 0,
+                      p.scale_log2, dst,
+                      [&](int jj) { return st.kv_global(p, jj); }, lane);
           // The scratch and the LSE rows are free for the next item.
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[kHeatOut]);
@@ -1805,25 +1831,9 @@ __global__ void __launch_bounds__(32 * pair::kWarps, 1)
               row < p.valid_count[qt] ? lse2 : INFINITY;
           row_sync(1 + grp);  // the tile's 4 warps: rows and scratch stored
           float* dst = p.heat + h * p.heat_sh + qt * p.heat_sq;
-          for (int jj = quarter; jj < len; jj += 4) {
-            float acc = p.heat_sum ? 0.f : -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = lane + 32 * i;
-              const float v = hs[jj * kTile + r];
-              if (p.heat_sum)
-                acc += ex2_approx(v - s_hl[grp * kTile + r]);
-              else
-                acc = fmaxf(acc, fmaf(v, p.scale_log2, -s_hl[grp * kTile + r]));
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-              const float o2 = __shfl_xor_sync(0xffffffffu, acc, off);
-              acc = p.heat_sum ? acc + o2 : fmaxf(acc, o2);
-            }
-            if (lane == 0)
-              dst[keys.kv(p, jj)] = p.heat_sum ? acc : ex2_approx(acc);
-          }
+          reduce_heat(hs, s_hl + grp * kTile, quarter, 4, len,
+                      p.heat_sum != 0, p.scale_log2, dst,
+                      [&](int jj) { return keys.kv(p, jj); }, lane);
           row_sync(1 + grp);  // the scratch is free for the next item
         }
       }
