@@ -126,71 +126,93 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
 }
 
 // logits[h, i, j] = q_hat[h, i, :] . k_hat[h, j, :] / sqrt(D)
-// grid (ceil(n_k/64), ceil(n_q/64), H'); 256 threads, 4x4 outputs each.
+// grid (ceil(n_k/128), ceil(n_q/128), H'); 256 threads in a 16 x 16 grid,
+// 8 x 8 outputs each: rows 4 ti + x and 64 + 4 ti + x, columns 4 tj + y and
+// 64 + 4 tj + y (x, y < 4), so each thread reads its 8 query and 8 key
+// values of a k step as four 16-byte shared-memory loads for 32 paired
+// FMAs. Every output sums its 128 products in k order with fused
+// multiply-adds, as a one-output-per-thread loop would.
+constexpr int kLogitTile = 128;
+constexpr int kLogitK = 16;
+
 __global__ void __launch_bounds__(256)
     logits_kernel(const float* q_hat, const float* k_hat, int64_t n_q,
                   int64_t n_k, float sqrt_d, float* logits) {
   const int h = blockIdx.z;
-  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * 64;
-  const int64_t j0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * kLogitTile;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.x) * kLogitTile;
   const float* qh = q_hat + static_cast<int64_t>(h) * n_q * kHeadDim;
   const float* kh = k_hat + static_cast<int64_t>(h) * n_k * kHeadDim;
-  // Two buffers: chunk c + 1 is loaded into registers while chunk c is
-  // multiplied from shared memory.
-  __shared__ __align__(16) float q_s[2][32][64 + 4];
-  __shared__ __align__(16) float k_s[2][32][64 + 4];
+  // Two buffers of a 16-wide k chunk, transposed ([k][row]): chunk c + 1
+  // is loaded into registers while chunk c is multiplied.
+  __shared__ __align__(16) float q_s[2][kLogitK][kLogitTile + 4];
+  __shared__ __align__(16) float k_s[2][kLogitK][kLogitTile + 4];
   const int tid = threadIdx.x;
   const int ti = tid / 16, tj = tid % 16;
-  float2 acc[4][2];  // column pairs, packed fp32x2 FMAs
+  float2 acc[8][4];  // [row][column pair]
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int x = 0; x < 8; ++x)
 #pragma unroll
-    for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
+    for (int y = 0; y < 4; ++y) acc[x][y] = make_float2(0.f, 0.f);
+  // 128 rows x 16 k of each side: 8 values per thread, 16 threads per row
+  // (64 contiguous bytes).
   float rq[8], rk[8];
   auto fetch = [&](int d0) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = tid + 256 * i;
-      const int r = e / 32, d = e % 32;
+      const int r = e / kLogitK, d = e % kLogitK;
       rq[i] = (i0 + r < n_q) ? qh[(i0 + r) * kHeadDim + d0 + d] : 0.f;
       rk[i] = (j0 + r < n_k) ? kh[(j0 + r) * kHeadDim + d0 + d] : 0.f;
     }
   };
   fetch(0);
-  for (int c = 0; c < kHeadDim / 32; ++c) {
+  constexpr int kChunks = kHeadDim / kLogitK;
+  for (int c = 0; c < kChunks; ++c) {
     const int buf = c & 1;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = tid + 256 * i;
-      q_s[buf][e % 32][e / 32] = rq[i];
-      k_s[buf][e % 32][e / 32] = rk[i];
+      q_s[buf][e % kLogitK][e / kLogitK] = rq[i];
+      k_s[buf][e % kLogitK][e / kLogitK] = rk[i];
     }
     __syncthreads();
-    if (c + 1 < kHeadDim / 32) fetch((c + 1) * 32);
-#pragma unroll 8
-    for (int d = 0; d < 32; ++d) {
-      const float4 a4 = *reinterpret_cast<const float4*>(&q_s[buf][d][ti * 4]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&k_s[buf][d][tj * 4]);
-      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
+    if (c + 1 < kChunks) fetch((c + 1) * kLogitK);
+#pragma unroll 4
+    for (int d = 0; d < kLogitK; ++d) {
+      const float4 a_lo = *reinterpret_cast<const float4*>(&q_s[buf][d][ti * 4]);
+      const float4 a_hi =
+          *reinterpret_cast<const float4*>(&q_s[buf][d][64 + ti * 4]);
+      const float4 b_lo = *reinterpret_cast<const float4*>(&k_s[buf][d][tj * 4]);
+      const float4 b_hi =
+          *reinterpret_cast<const float4*>(&k_s[buf][d][64 + tj * 4]);
+      const float a[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w,
+                          a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+      const float2 b[4] = {make_float2(b_lo.x, b_lo.y),
+                           make_float2(b_lo.z, b_lo.w),
+                           make_float2(b_hi.x, b_hi.y),
+                           make_float2(b_hi.z, b_hi.w)};
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
+      for (int x = 0; x < 8; ++x) {
         const float2 ax = make_float2(a[x], a[x]);
-        acc[x][0] = __ffma2_rn(ax, b01, acc[x][0]);
-        acc[x][1] = __ffma2_rn(ax, b23, acc[x][1]);
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = __ffma2_rn(ax, b[y], acc[x][y]);
       }
     }
+    // The next iteration's stash writes the other buffer; this one is
+    // written again only behind the barrier after that.
   }
   float* out = logits + static_cast<int64_t>(h) * n_q * n_k;
 #pragma unroll
-  for (int x = 0; x < 4; ++x) {
-    const int64_t i = i0 + ti * 4 + x;
+  for (int x = 0; x < 8; ++x) {
+    const int64_t i = i0 + (x < 4 ? ti * 4 + x : 64 + ti * 4 + (x - 4));
     if (i >= n_q) continue;
 #pragma unroll
-    for (int y = 0; y < 4; ++y) {
-      const int64_t j = j0 + tj * 4 + y;
+    for (int y = 0; y < 8; ++y) {
+      const int64_t j = j0 + (y < 4 ? tj * 4 + y : 64 + tj * 4 + (y - 4));
       // Divided, not multiplied by the reciprocal, as the reference does.
-      const float v = (y & 1) ? acc[x][y >> 1].y : acc[x][y >> 1].x;
+      const float2 v2 = acc[x][y >> 1];
+      const float v = (y & 1) ? v2.y : v2.x;
       if (j < n_k) out[i * n_k + j] = __fdiv_rn(v, sqrt_d);
     }
   }
@@ -252,8 +274,8 @@ extern "C" int veda_predict_logits(const float* feats_q, const float* feats_k,
   embed_kernel<<<g1, 256, 0, as_stream(stream)>>>(p);
   int rc = check_launch("embed_kernel");
   if (rc != VEDA_OK) return rc;
-  dim3 g2(static_cast<unsigned>((n_k + 63) / 64),
-          static_cast<unsigned>((n_q + 63) / 64),
+  dim3 g2(static_cast<unsigned>((n_k + kLogitTile - 1) / kLogitTile),
+          static_cast<unsigned>((n_q + kLogitTile - 1) / kLogitTile),
           static_cast<unsigned>(n_heads));
   logits_kernel<<<g2, 256, 0, as_stream(stream)>>>(
       q_hat, k_hat, n_q, n_k, sqrtf(static_cast<float>(kHeadDim)), logits);
