@@ -1,8 +1,10 @@
 """Normalized parity errors for the floating-point GPU tests.
 
 The bar for attention outputs, gradients and scores is stated on the
-normalized error max|got - want| / max|want| over the compared elements
-(forward outputs <= 2e-2, gradients <= 3e-2 against the fp32 oracle). Every
+normalized error max|got - want| / max|want| over the compared elements:
+at most 2e-2 against the fp32 oracle for forward outputs and for
+gradients (the tests also keep the reference's own elementwise bars,
+rtol = atol = 2e-2 forward and 3e-2 for gradients). Every
 check is recorded, printed, and summarised at the end of the test session
 (conftest.py) so a run's log carries the measured values, not only a pass.
 """
@@ -14,7 +16,7 @@ import numpy as np
 RECORDS: list[tuple[str, float, float]] = []
 
 FWD = 2e-2   # attention outputs against the fp32 oracle
-GRAD = 3e-2  # dq, dk, dv against the fp32 oracle
+GRAD = 2e-2  # dq, dk, dv against the fp32 oracle
 
 
 def _np(x):
